@@ -1,0 +1,171 @@
+/*
+ * c4s_sampling.h -- C ABI of the B200 (sm_100a) T2S sampling stage.
+ *
+ * This library replaces the host-side sampling stage of the Confucius4-TTS
+ * C++/MLX engine (raoqu/mlx-confucius4-tts). In the reference, every AR decode
+ * step copies one 8194-wide fp32 logits row per stream to the host and runs
+ *
+ *     repetition_penalty -> (greedy: argmax)
+ *                        -> (sample: temperature -> top_k -> top_p -> draw)
+ *
+ * in scalar C++ on a std::vector<float>:
+ *   include/c4tts/t2s.h:82-89          declarations of the five processors
+ *   src/t2s/sampling.cpp:14-76         their definitions
+ *   src/t2s/text2semantic.cpp:142-165  single-stream call order + inline draw
+ *   src/t2s/text2semantic.cpp:303-331  batched call order + inline draw
+ *   src/t2s/text2semantic.cpp:109,294  xorshift64 state seeding
+ *
+ * Here the logits stay in device memory and one call processes a whole batch
+ * of rows. All entry points
+ *   - return 0 (C4S_OK) or a negative c4s_status, and never throw;
+ *   - take caller-owned DEVICE pointers (except where noted) and a
+ *     cudaStream_t passed as void*; work is stream-ordered and asynchronous;
+ *   - never allocate device memory after c4s_create();
+ *   - are thread-compatible: one context per host thread (or stream) at a time.
+ *
+ * Parity contract with the reference (same inputs, same xorshift64 state):
+ *   penalised / tempered / top-k-masked logits are bit-identical; top-p masks
+ *   are identical (ties at the top-p boundary are broken by ascending index,
+ *   where the reference's std::sort leaves the order unspecified); sampled ids
+ *   are identical. Inputs containing NaN or +inf are outside the contract
+ *   (the reference's std::sort is undefined for NaN; +inf makes its softmax NaN).
+ */
+#ifndef C4S_SAMPLING_H_
+#define C4S_SAMPLING_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define C4S_ABI_VERSION 1
+
+/* Status codes. */
+typedef enum c4s_status {
+  C4S_OK = 0,
+  C4S_ERR_INVALID = -1,   /* bad argument (null pointer, size, stride, mode) */
+  C4S_ERR_CUDA = -2,      /* a CUDA runtime call failed; see c4s_last_error() */
+  C4S_ERR_CAPACITY = -3,  /* V above the context's max_vocab / kernel limit */
+  C4S_ERR_DEVICE = -4,    /* a kernel raised a device-side error flag */
+  C4S_ERR_TIMEOUT = -5,   /* a bounded device wait gave up */
+  C4S_ERR_NCCL = -6       /* a collective failed (vocab-sharded path) */
+} c4s_status;
+
+/* Per-row sampling parameters. One struct per row (params_stride = 1) or one
+ * struct broadcast to all rows (params_stride = 0). Defaults of the reference
+ * (include/c4tts/pipeline.h:26-37): T 0.8, top_k 30, top_p 0.8, penalty 10,
+ * greedy 0, min_tokens_to_keep 1.                                           */
+typedef struct c4s_row_params {
+  float temperature;          /* sampling.cpp:14-17; skipped if ==1 or <=0     */
+  int32_t top_k;              /* sampling.cpp:30-40; skipped if <=0 or >=V     */
+  float top_p;                /* sampling.cpp:42-71                            */
+  float repetition_penalty;   /* sampling.cpp:19-28; skipped if ==1            */
+  int32_t greedy;             /* !=0: penalty + argmax (text2semantic.cpp:144) */
+  int32_t min_tokens_to_keep; /* top_p's third argument (t2s.h:88), default 1 */
+} c4s_row_params;
+
+/* Stage bits for c4s_process(): which reference processors to apply, always in
+ * the reference order penalty -> temperature -> top_k -> top_p.             */
+#define C4S_STAGE_PENALTY 1
+#define C4S_STAGE_TEMPERATURE 2
+#define C4S_STAGE_TOP_K 4
+#define C4S_STAGE_TOP_P 8
+
+/* Debug flags for c4s_set_debug(): force the slow exact paths so that tests
+ * can check them on ordinary inputs.                                        */
+#define C4S_DEBUG_FORCE_EXACT 1 /* exact sequential sums; radix-select top-k   */
+#define C4S_DEBUG_FORCE_BINS 2  /* binned top-p and row-pass draw paths        */
+
+/* Device-side error bits reported by c4s_get_status().                     */
+#define C4S_DEVERR_HIST_RANGE 1u /* a row's history offsets were out of range */
+#define C4S_DEVERR_TIMEOUT 2u    /* a bounded wait on a bulk copy gave up      */
+
+/* Counter slots reported by c4s_get_status() (rows that took each path).    */
+#define C4S_CNT_TOPP_EXACT_FALLBACK 0 /* top-p guard band hit: exact re-sum   */
+#define C4S_CNT_DRAW_EXACT_FALLBACK 1 /* draw guard band hit: exact re-sum    */
+#define C4S_CNT_TOPK_RADIX 2          /* top-k needed the full radix select   */
+#define C4S_CNT_TOPP_BINNED 3         /* top-p over more than the list cap     */
+#define C4S_CNT_DRAW_ROWPASS 4        /* draw over more than the list cap      */
+#define C4S_NUM_COUNTERS 8
+
+typedef struct c4s_ctx c4s_ctx;
+
+/* Library ABI version (C4S_ABI_VERSION). */
+int c4s_version(void);
+
+/* Human-readable name of a c4s_status. */
+const char* c4s_status_string(int status);
+
+/* Create a context on `device` able to process rows of up to `max_vocab`
+ * logits. Allocates all device workspace the other calls need. The current
+ * device of the calling thread is left unchanged.
+ * Replaces: nothing in the reference (its processors allocate per call:
+ * sampling.cpp:22,33,45,52).                                                */
+int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device);
+int c4s_destroy(c4s_ctx* ctx);
+
+/* Text of the last error seen by this context ("" if none). */
+const char* c4s_last_error(const c4s_ctx* ctx);
+
+/* Set C4S_DEBUG_* flags (0 for production behaviour). */
+int c4s_set_debug(c4s_ctx* ctx, int32_t flags);
+
+/* Seed B xorshift64 states: state[b] = (seed ? seed : 0x9E3779B97F4A7C15)
+ *                                      + (row_offset + b) * 0x100000001b3.
+ * Replaces text2semantic.cpp:109 (single stream = row 0) and :292-295.     */
+int c4s_seed_states(uint64_t* d_state, int32_t B, uint64_t seed,
+                    int64_t row_offset, void* stream);
+
+/* One fused sampling step over B rows: for each active row b,
+ *   repetition penalty over hist[hist_off[b] .. hist_off[b+1]),
+ *   then greedy ? argmax : temperature, top_k, top_p, xorshift64 draw.
+ * Replaces the per-row body of text2semantic.cpp:303-331 (and :142-165).
+ *   d_logits   fp32 [B, ld], read only; ld >= V (any ld, rows may be unaligned)
+ *   d_hist     int32 token history (generated ids, no prompt), CSR by
+ *   d_hist_off int64 [B+1]; hist_total = number of ids in d_hist. Ids outside
+ *              [0, V) are skipped (sampling.cpp:24). d_hist_off may be NULL:
+ *              no history for any row.
+ *   d_params   c4s_row_params, per row (stride 1) or broadcast (stride 0)
+ *   d_rng      uint64 [B] xorshift64 state, advanced once per sampled row;
+ *              greedy and inactive rows leave it unchanged (:304, :144)
+ *   d_active   uint8 [B] or NULL (all active); inactive rows get id -1 and
+ *              are not touched otherwise
+ *   d_out_ids  int32 [B] sampled token ids
+ *   d_out_logits  NULL, or fp32 [B, out_ld]: the processed logits of each
+ *              active row (what the reference's vector holds before its draw)
+ */
+int c4s_sample(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V,
+               int64_t ld, const int32_t* d_hist, const int64_t* d_hist_off,
+               int64_t hist_total, const c4s_row_params* d_params,
+               int32_t params_stride, uint64_t* d_rng, const uint8_t* d_active,
+               int32_t* d_out_ids, float* d_out_logits, int64_t out_ld,
+               void* stream);
+
+/* Apply the processors selected by `stages` (C4S_STAGE_* bits) in place to B
+ * rows of d_logits, in the reference order, ignoring params.greedy.
+ * Replaces the in-place processors of sampling.cpp:14-71 / t2s.h:83-88:
+ *   repetition_penalty (sampling.cpp:19), temperature (:14), top_k (:30),
+ *   top_p (:42).                                                           */
+int c4s_process(c4s_ctx* ctx, float* d_logits, int32_t B, int32_t V,
+                int64_t ld, const int32_t* d_hist, const int64_t* d_hist_off,
+                int64_t hist_total, const c4s_row_params* d_params,
+                int32_t params_stride, int32_t stages, void* stream);
+
+/* First index of the row maximum for B rows (std::max_element semantics).
+ * Replaces argmax, sampling.cpp:73-76 / t2s.h:89.                          */
+int c4s_argmax(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V,
+               int64_t ld, int32_t* d_out_ids, void* stream);
+
+/* Synchronise `stream`, then report (and optionally clear) the device error
+ * bits (C4S_DEVERR_*) and path counters (C4S_CNT_*; may be NULL).
+ * Returns C4S_ERR_DEVICE / C4S_ERR_TIMEOUT if an error bit is set.          */
+int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors,
+                   uint64_t* counters /* [C4S_NUM_COUNTERS] or NULL */,
+                   int32_t reset, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* C4S_SAMPLING_H_ */
