@@ -1,0 +1,398 @@
+#!/usr/bin/env python3
+"""Benchmark of the T2S sampling stage on B200 (one process per GPU).
+
+Workload (the configuration the headline metric is quoted
+on): per GPU a batch of B=4096 rows of V=8194 fp32 logits ~N(0, 3^2), ragged
+token histories with lengths U[0, 2048], per-row temperature U[0.5, 1.2],
+top_k from {0, 20, 50, 200}, top_p U[0.6, 1.0], repetition penalty
+U[1, 10], sample mode. A step is one fused sampling pass over the batch
+(one c4s_sample call). Inputs are seeded synthetic data; a pool of 3 batches
+(3 x 151 MB, larger than the 126 MB L2) is rotated so that no step reads
+cache-resident logits.
+
+Rows are independent, so N GPUs shard rows with no collective on the data
+path (weak scaling: each rank samples its own 4096-row block of a
+4096*N-row batch, seeded with its global row offset).
+
+  value   sampled tokens/s over all ranks, inputs resident in HBM
+  e2e     the same through SamplingContext.sample_from_host with pinned host
+          buffers: H2D of the step's logits/history/params/states, sampling,
+          D2H of ids and states inside the timed region
+  b1_p50_us   p50 latency of one B=1 decode step (config 0), CUDA-graph replay
+
+`--impl reference` times the reference's CPU implementation of the same step
+(its own sampling.cpp compiled from source plus the restated draw, or the C
+oracle port where that build is absent) on all host threads.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rows", type=int, default=4096, help="rows per GPU")
+    ap.add_argument("--pool", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--b1-steps", type=int, default=500)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="only run this many steps of the main loop (for ncu), print nothing")
+    return ap.parse_args()
+
+
+def load_pkg():
+    import __graft_entry__ as ge
+    return ge._load_pkg()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, phys_index):
+        self.idx = phys_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9 or parts[0] != str(self.idx):
+                    continue
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def phys_index(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = vis.split(",")
+        if local < len(ids) and ids[local].strip().isdigit():
+            return int(ids[local])
+    return local
+
+
+# ---------------------------------------------------------------------------
+def cpu_reference_rows_per_s(c4s, seconds, rows_cap=4096, batch=None):
+    """Time the reference CPU path (compiled reference, else the C port) on
+    config-2 rows with all host threads; returns (rows/s, kind, threads, rows)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    if orc.RefOracle.available():
+        impl, kind = orc.RefOracle(), "reference"
+    else:
+        impl, kind = orc.Oracle(), "port"
+    threads = os.cpu_count() or 1
+    b = batch or c4s.workloads.config2(seed=2, B=rows_cap)
+    done, t0 = 0, time.perf_counter()
+    chunk = min(b.B, max(threads * 8, 256))
+    while True:
+        s = done % b.B
+        e = min(b.B, s + chunk)
+        sub = c4s.workloads.Batch(np.ascontiguousarray(b.logits[s:e]), b.V, b.hist,
+                                  b.hist_off[s:e + 1], b.params[s:e], b.rng[s:e].copy())
+        impl.sample_batch(sub.logits, sub.V, sub.hist, sub.hist_off, sub.params, sub.rng, nthreads=threads)
+        done += e - s
+        el = time.perf_counter() - t0
+        if el >= seconds and done >= chunk:
+            return done / el, kind, threads, done
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    c4s = load_pkg()
+    b = c4s.workloads.config2(seed=2, B=args.rows)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    impl, kind = (orc.RefOracle(), "reference") if orc.RefOracle.available() else (orc.Oracle(), "port")
+    threads = os.cpu_count() or 1
+
+    def step():
+        rng = b.rng.copy()
+        impl.sample_batch(b.logits, b.V, b.hist, b.hist_off, b.params, rng, nthreads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    v = args.rows * args.steps / el
+    line = {
+        "impl": "reference", "metric": "sampled tokens/s (B=4096, V=8194, config 2)", "value": v,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32+f64", "data": "synthetic",
+        "config": {"workload": "config2: B=4096 V=8194 ragged history, per-row T/top_k/top_p/penalty",
+                   "global_batch": args.rows, "rows_per_gpu": args.rows, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"full {args.rows}-row config-2 batch per step, OpenMP over rows "
+                                   f"with {threads} threads"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    c4s = load_pkg()
+    wl = c4s.workloads
+    B = args.rows
+    ctx = c4s.SamplingContext(max_vocab=wl.SEMANTIC_VOCAB, device=local)
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- inputs: pool of batches, this rank's block of the global batch ----
+    pool, host = [], []
+    for k in range(args.pool):
+        b = wl.config2(seed=2 + k, B=B, row_offset=rank * B)
+        pool.append(dict(
+            logits=torch.from_numpy(b.logits).to(dev),
+            hist=torch.from_numpy(b.hist).to(dev),
+            hist_off=torch.from_numpy(b.hist_off).to(dev),
+            params=c4s.params_tensor(b.params, dev),
+            rng=torch.from_numpy(b.rng.view(np.int64).copy()).to(dev),
+            bytes=wl.algorithmic_bytes(b.V, b.hist_off, B)))
+        host.append(b)
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+
+    def step(s):
+        p = pool[s % len(pool)]
+        ctx.sample(p["logits"], p["hist"], p["hist_off"], p["params"], p["rng"], out_ids=ids)
+
+    if args.profile_steps:
+        for s in range(args.profile_steps):
+            step(s)
+        torch.cuda.synchronize()
+        return
+
+    for s in range(max(3, args.warmup)):
+        step(s)
+    torch.cuda.synchronize()
+
+    # ---- clocks under sustained load (~2 s of back-to-back steps) ----
+    clk = ClockSampler(phys_index(local))
+    t_end = time.time() + 2.0
+    s = 0
+    while time.time() < t_end:
+        for _ in range(50):
+            step(s)
+            s += 1
+        torch.cuda.synchronize()
+
+    # ---- timed region: exactly K steps ----
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        step(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = clk.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_per_step = ms / args.steps
+    rows_total = B * world * args.steps
+    value = rows_total / (ms / 1e3)
+    err, counters = ctx.status(reset=True)
+
+    # ---- roofline of the sampling kernel (the only kernel in the timed region) ----
+    alg_bytes = float(np.mean([p["bytes"] for p in pool]))
+    hbm_peak, peak_kind = peaks()
+    achieved_gbs = alg_bytes / (ms_per_step / 1e3) / 1e9
+
+    # ---- e2e through the public host-buffer API ----
+    e2e = None
+    if not args.no_e2e:
+        hp = []
+        for b in host:
+            hp.append(dict(
+                logits=torch.from_numpy(b.logits).pin_memory(),
+                hist=torch.from_numpy(b.hist).pin_memory(),
+                hist_off=torch.from_numpy(b.hist_off).pin_memory(),
+                params=torch.from_numpy(np.ascontiguousarray(b.params).view(np.uint8).copy()).pin_memory(),
+                rng=torch.from_numpy(b.rng.view(np.int64).copy()).pin_memory()))
+        ids_h = torch.empty(B, dtype=torch.int32).pin_memory()
+
+        def hstep(s):
+            p = hp[s % len(hp)]
+            ctx.sample_from_host(p["logits"], p["hist"], p["hist_off"], p["params"], p["rng"], ids_h)
+
+        for s in range(3):
+            hstep(s)
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for s in range(args.steps):
+            hstep(s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        h2d = int(np.mean([sum(t.numel() * t.element_size() for t in p.values()) for p in hp]))
+        d2h = B * 4 + B * 8
+        e2e = {"value": B * world * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": ms_e2e / args.steps}
+
+    # ---- B=1 decode-step latency (config 0), CUDA graph replay and eager ----
+    b1 = None
+    if rank == 0:
+        b0 = wl.config0()
+        d0 = dict(logits=torch.from_numpy(b0.logits).to(dev), hist=torch.from_numpy(b0.hist).to(dev),
+                  hist_off=torch.from_numpy(b0.hist_off).to(dev), params=c4s.params_tensor(b0.params, dev),
+                  rng=torch.from_numpy(b0.rng.view(np.int64).copy()).to(dev))
+        id0 = torch.empty(1, dtype=torch.int32, device=dev)
+
+        def s1():
+            ctx.sample(d0["logits"], d0["hist"], d0["hist_off"], d0["params"], d0["rng"], out_ids=id0)
+
+        def lat(fn, n):
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+            for a, bb in ev:
+                a.record()
+                fn()
+                bb.record()
+            torch.cuda.synchronize()
+            return [a.elapsed_time(bb) * 1e3 for a, bb in ev]
+
+        for _ in range(20):
+            s1()
+        eager = lat(s1, args.b1_steps)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            s1()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            s1()
+        for _ in range(20):
+            g.replay()
+        graph = lat(g.replay, args.b1_steps)
+        b1 = {"graph_p50_us": statistics.median(graph), "eager_p50_us": statistics.median(eager),
+              "steps": args.b1_steps}
+        del g
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, kind, threads, nrows = cpu_reference_rows_per_s(c4s, args.cpu_seconds, batch=host[0])
+        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{nrows} rows of the config-2 batch (first {min(B, nrows)} rows, wrapping), "
+                         f"OpenMP over rows, {threads} host threads, ~{args.cpu_seconds:.0f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": "sampled tokens/s (B=4096, V=8194, config 2)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32+f64", "data": "synthetic",
+            "config": {"workload": "config2: B=4096 V=8194 fp32 logits ~N(0,9), ragged history "
+                                   "U[0,2048], per-row T U[0.5,1.2], top_k {0,20,50,200}, top_p U[0.6,1.0], "
+                                   "penalty U[1,10]",
+                       "global_batch": B * world, "rows_per_gpu": B, "V": wl.SEMANTIC_VOCAB,
+                       "parallelism": f"rows x{world} (no collective)",
+                       "l2": f"pool of {args.pool} batches rotated (inputs > L2)"},
+            "b1_p50_us": None if b1 is None else b1["graph_p50_us"],
+            "b1": b1,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved_gbs / hbm_peak, "traffic": None,
+                         "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "device_errors": err,
+            "path_counters": counters,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,247 @@
+// c4s_device.cuh -- device building blocks for the T2S sampling kernels:
+// order-preserving keys, block reductions/scans, shared-memory bitonic sort,
+// bulk-async (TMA engine) row staging with a bounded mbarrier wait.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace c4s {
+
+constexpr int NT = 256;               // threads per CTA (8 warps)
+constexpr int NWARP = NT / 32;
+constexpr int NBIN = 256;             // distance-from-max bins
+constexpr float BIN_SCALE = 4.0f;     // bins are 1/4 logit wide, bin 255 = overflow
+constexpr int LIST_CAP = 1024;        // candidates sorted in shared memory
+constexpr int SEQ_MAX = 96;           // <= this many survivors: exact sequential sums
+constexpr int MAX_VOCAB = 32768;      // row must fit in shared memory
+constexpr unsigned FULL = 0xffffffffu;
+constexpr unsigned long long KEY_MAX = ~0ull;
+
+// ---------------------------------------------------------------------------
+// Keys. fkey() maps a float to a uint32 whose unsigned order is the float
+// order, with -0 folded onto +0 so that key equality is float equality.
+// ckey() appends the index: ascending ckey order is ascending (value, index),
+// the canonical order of the top-p sort.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned fkey(float f) {
+  unsigned u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(unsigned k) {
+  unsigned u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+__device__ __forceinline__ unsigned long long ckey(float f, int i) {
+  return ((unsigned long long)fkey(f) << 32) | (unsigned)i;
+}
+__device__ __forceinline__ int ckey_idx(unsigned long long k) { return (int)(unsigned)(k & 0xffffffffull); }
+
+// Distance-from-max bin: non-increasing in y, so bins partition the ascending
+// value order into contiguous ranges. -inf (and anything 64+ below the max)
+// lands in the overflow bin NBIN-1.
+__device__ __forceinline__ int vbin(float m, float y) {
+  float t = __fmul_rn(__fsub_rn(m, y), BIN_SCALE);
+  t = fminf(t, (float)(NBIN - 1));
+  return (int)t;
+}
+
+// ---------------------------------------------------------------------------
+// Warp / block reductions and scans (all threads of the CTA must call).
+// `red` is shared scratch of at least NWARP elements of the value type.
+// ---------------------------------------------------------------------------
+template <typename T, typename Op>
+__device__ __forceinline__ T warp_reduce(T v, Op op) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(FULL, v, o));
+  return v;
+}
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_reduce(v, op);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  T r = red[0];
+#pragma unroll
+  for (int w = 1; w < NWARP; ++w) r = op(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
+struct MaxF { __device__ float operator()(float a, float b) const { return fmaxf(a, b); } };
+struct SumU64 { __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a + b; } };
+struct MaxU64 { __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a > b ? a : b; } };
+struct SumI { __device__ int operator()(int a, int b) const { return a + b; } };
+
+// Exclusive scan of one uint64 per thread over the CTA; *total gets the sum.
+__device__ __forceinline__ unsigned long long block_exscan_u64(unsigned long long v, unsigned long long* red,
+                                                               unsigned long long* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    unsigned long long y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) red[warp] = x;
+  __syncthreads();
+  unsigned long long wbase = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < NWARP; ++w) {
+    unsigned long long t = red[w];
+    if (w < warp) wbase += t;
+    tot += t;
+  }
+  __syncthreads();
+  *total = tot;
+  return wbase + x - v;
+}
+
+// Exclusive scan of one int per thread over the CTA.
+__device__ __forceinline__ int block_exscan_i32(int v, int* red, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) red[warp] = x;
+  __syncthreads();
+  int wbase = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < NWARP; ++w) {
+    int t = red[w];
+    if (w < warp) wbase += t;
+    tot += t;
+  }
+  __syncthreads();
+  *total = tot;
+  return wbase + x - v;
+}
+
+// ---------------------------------------------------------------------------
+// Warp 0 search over 256 bins in a given logical order: finds the first
+// logical position c whose inclusive running sum exceeds (strict=true) or
+// reaches (strict=false) `target`. get(j) returns the value of logical bin j.
+// Results are written by lane 0 to *c_out (NBIN if none) and *before_out
+// (sum of logical bins < c). Only warp 0 may call.
+// ---------------------------------------------------------------------------
+template <typename T, typename Get>
+__device__ __forceinline__ void warp_find_bin(Get get, T target, bool strict, int* c_out, T* before_out) {
+  const int lane = threadIdx.x & 31;
+  T loc[8];
+  T s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { loc[j] = get(lane * 8 + j); s += loc[j]; }
+  T incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    T y = __shfl_up_sync(FULL, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const bool hit = strict ? (incl > target) : (incl >= target);
+  const unsigned bal = __ballot_sync(FULL, hit);
+  if (bal == 0) {
+    const T tot = __shfl_sync(FULL, incl, 31);
+    if (lane == 0) { *c_out = NBIN; *before_out = tot; }
+    return;
+  }
+  const int L = __ffs(bal) - 1;
+  if (lane == L) {
+    T run = incl - s;
+    int c = L * 8 + 7;
+    T before = run;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool h = strict ? (run + loc[j] > target) : (run + loc[j] >= target);
+      if (h) { c = L * 8 + j; before = run; break; }
+      run += loc[j];
+    }
+    *c_out = c;
+    *before_out = before;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Bitonic sort (ascending) of n = power of two uint64 keys; `a` may be in
+// shared or global memory (the CTA-wide barrier orders both).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bitonic_sort_u64(unsigned long long* a, int n) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n; i += NT) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long x = a[i], y = a[ixj];
+          const bool up = ((i & k) == 0);
+          if ((x > y) == up) { a[i] = y; a[ixj] = x; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__device__ __forceinline__ int next_pow2(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// Bulk-async copy (TMA engine, non-tensor form) with an mbarrier. No cluster
+// multicast is used anywhere in this library.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned phase) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait (about 2 s of wall time); false if it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned phase) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (unsigned it = 0; it < (1u << 30); ++it) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) return false;
+  }
+  return false;
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace c4s

@@ -1,0 +1,331 @@
+"""Python host side of the B200 T2S sampling stage.
+
+Two layers, matching the C ABI in include/c4s_sampling.h:
+
+* ``SamplingContext`` -- the batched, device-resident entry points
+  (``sample``, ``process``, ``argmax``, ``seed_states``) over torch CUDA
+  tensors, stream-ordered on the current torch stream.
+* Module-level ``temperature``, ``repetition_penalty``, ``top_k``, ``top_p``,
+  ``argmax`` -- the reference's five processors (include/c4tts/t2s.h:82-89,
+  src/t2s/sampling.cpp:14-76 of the reference) with the same names, argument
+  meaning and in-place behaviour: pass a 1-D float32 CUDA tensor, a float32
+  numpy array or a Python list and it is modified in place (argmax returns
+  the index).
+
+There is no CPU fallback: if the CUDA library is missing or no sm_100 device
+is present every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+import numpy as np
+
+from . import workloads
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libc4s.so")
+
+STAGE_PENALTY = 1
+STAGE_TEMPERATURE = 2
+STAGE_TOP_K = 4
+STAGE_TOP_P = 8
+STAGE_ALL = 15
+DEBUG_FORCE_EXACT = 1
+DEBUG_FORCE_BINS = 2
+COUNTER_NAMES = ("topp_exact_fallback", "draw_exact_fallback", "topk_radix",
+                 "topp_binned", "draw_rowpass")
+MAX_VOCAB = 32768
+
+_STATUS = {0: "ok", -1: "invalid argument", -2: "CUDA error", -3: "capacity exceeded",
+           -4: "device-side error", -5: "device wait timed out", -6: "collective failed"}
+
+
+class C4SError(RuntimeError):
+    """A c4s C-ABI call returned a non-zero status."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{_STATUS.get(status, status)}: {message}")
+        self.status = status
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def library() -> C.CDLL:
+    """Load lib/libc4s.so (built by __graft_entry__.build()); raise if absent."""
+    global _lib
+    with _lib_lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(f"c4s CUDA library not built: {LIB_PATH} is missing "
+                                   "(run `python -c 'import __graft_entry__ as g; g.build()'`)")
+            L = C.CDLL(LIB_PATH)
+            vp, i32, i64, u64 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64
+            sig = {
+                "c4s_version": ([], C.c_int),
+                "c4s_status_string": ([C.c_int], C.c_char_p),
+                "c4s_create": ([C.POINTER(vp), i32, i32], C.c_int),
+                "c4s_destroy": ([vp], C.c_int),
+                "c4s_last_error": ([vp], C.c_char_p),
+                "c4s_set_debug": ([vp, i32], C.c_int),
+                "c4s_seed_states": ([vp, i32, u64, i64, vp], C.c_int),
+                "c4s_sample": ([vp, vp, i32, i32, i64, vp, vp, i64, vp, i32, vp, vp, vp, vp, i64, vp],
+                               C.c_int),
+                "c4s_process": ([vp, vp, i32, i32, i64, vp, vp, i64, vp, i32, i32, vp], C.c_int),
+                "c4s_argmax": ([vp, vp, i32, i32, i64, vp, vp], C.c_int),
+                "c4s_get_status": ([vp, vp, vp, i32, vp], C.c_int),
+            }
+            for name, (args, res) in sig.items():
+                f = getattr(L, name)
+                f.argtypes = args
+                f.restype = res
+            _lib = L
+        return _lib
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def params_tensor(params: np.ndarray, device) -> "torch.Tensor":
+    """Upload a ROW_PARAMS_DTYPE array as raw bytes (24 B per row)."""
+    torch = _torch()
+    assert params.dtype == workloads.ROW_PARAMS_DTYPE
+    raw = np.ascontiguousarray(params).view(np.uint8)
+    return torch.from_numpy(raw.copy()).to(device)
+
+
+class SamplingContext:
+    """One c4s context (device workspace) bound to a CUDA device."""
+
+    def __init__(self, max_vocab: int = workloads.SEMANTIC_VOCAB, device=None):
+        torch = _torch()
+        self.lib = library()
+        if device is None:
+            device = torch.cuda.current_device()
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.max_vocab = max_vocab
+        h = C.c_void_p()
+        rc = self.lib.c4s_create(C.byref(h), max_vocab, self.device.index or 0)
+        if rc != 0:
+            raise C4SError(rc, f"c4s_create(max_vocab={max_vocab}, device={self.device})")
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.c4s_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- helpers --------------------------------------------------------------
+    def _check(self, rc: int, what: str):
+        if rc != 0:
+            msg = self.lib.c4s_last_error(self._h).decode()
+            raise C4SError(rc, f"{what}: {msg}")
+
+    def _stream(self, stream):
+        torch = _torch()
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return C.c_void_p(s.cuda_stream)
+
+    def set_debug(self, flags: int):
+        self._check(self.lib.c4s_set_debug(self._h, flags), "c4s_set_debug")
+
+    def status(self, reset: bool = False, stream=None):
+        """Synchronise and return (device error bits, {counter: value})."""
+        err = C.c_uint32(0)
+        cnt = (C.c_uint64 * 8)()
+        rc = self.lib.c4s_get_status(self._h, C.byref(err), cnt, int(reset), self._stream(stream))
+        counters = {n: int(cnt[i]) for i, n in enumerate(COUNTER_NAMES)}
+        if rc not in (0, -4, -5):
+            self._check(rc, "c4s_get_status")
+        return int(err.value), counters
+
+    # -- batched entry points -----------------------------------------------------
+    def seed_states(self, B: int, seed: int, row_offset: int = 0, out=None, stream=None):
+        """int64 CUDA tensor holding the uint64 xorshift states (text2semantic.cpp:292-295)."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty(B, dtype=torch.int64, device=self.device)
+        rc = self.lib.c4s_seed_states(_dptr(out), B, seed & (2**64 - 1), row_offset, self._stream(stream))
+        self._check(rc, "c4s_seed_states")
+        return out
+
+    def sample(self, logits, hist, hist_off, params, rng, active=None, out_ids=None,
+               out_logits=None, V: int | None = None, params_stride: int = 1, stream=None):
+        """One fused sampling step over the rows of ``logits`` [B, ld].
+
+        hist int32 / hist_off int64 [B+1] (CSR, may be None), params uint8
+        [B*24] (or 24 with params_stride=0), rng int64 [B] (advanced in
+        place), active uint8 [B] or None. Returns int32 ids [B].
+        """
+        torch = _torch()
+        B, ld = logits.shape
+        V = ld if V is None else V
+        if out_ids is None:
+            out_ids = torch.empty(B, dtype=torch.int32, device=logits.device)
+        total = 0 if hist is None else hist.numel()
+        rc = self.lib.c4s_sample(
+            self._h, _dptr(logits), B, V, logits.stride(0), _dptr(hist), _dptr(hist_off), total,
+            _dptr(params), params_stride, _dptr(rng), _dptr(active), _dptr(out_ids),
+            _dptr(out_logits), 0 if out_logits is None else out_logits.stride(0), self._stream(stream))
+        self._check(rc, "c4s_sample")
+        return out_ids
+
+    def sample_from_host(self, logits, hist, hist_off, params, rng, out_ids, V: int | None = None,
+                         stream=None):
+        """One sampling step on HOST (ideally pinned) tensors, like the
+        reference's host-vector interface but batched: uploads the step's
+        inputs to device staging buffers, samples, and copies the ids and the
+        advanced xorshift states back into ``out_ids`` / ``rng``. Asynchronous
+        on the current stream; synchronise before reading the host outputs.
+        """
+        torch = _torch()
+        dev = self.device
+        key = (logits.shape, hist.numel(), hist_off.numel(), params.numel(), rng.numel())
+        st = getattr(self, "_staging", None)
+        if st is None or st[0] != key:
+            st = (key, dict(
+                logits=torch.empty(logits.shape, dtype=torch.float32, device=dev),
+                hist=torch.empty(hist.numel(), dtype=torch.int32, device=dev),
+                hist_off=torch.empty(hist_off.numel(), dtype=torch.int64, device=dev),
+                params=torch.empty(params.numel(), dtype=torch.uint8, device=dev),
+                rng=torch.empty(rng.numel(), dtype=torch.int64, device=dev),
+                ids=torch.empty(logits.shape[0], dtype=torch.int32, device=dev)))
+            self._staging = st
+        d = st[1]
+        d["logits"].copy_(logits, non_blocking=True)
+        d["hist"].copy_(hist, non_blocking=True)
+        d["hist_off"].copy_(hist_off, non_blocking=True)
+        d["params"].copy_(params, non_blocking=True)
+        d["rng"].copy_(rng, non_blocking=True)
+        self.sample(d["logits"], d["hist"], d["hist_off"], d["params"], d["rng"], out_ids=d["ids"], V=V,
+                    stream=stream)
+        out_ids.copy_(d["ids"], non_blocking=True)
+        rng.copy_(d["rng"], non_blocking=True)
+        return out_ids
+
+    def process(self, logits, hist, hist_off, params, stages: int, V: int | None = None,
+                params_stride: int = 1, stream=None):
+        """Apply the selected processors in place to the rows of ``logits``."""
+        B, ld = logits.shape
+        V = ld if V is None else V
+        total = 0 if hist is None else hist.numel()
+        rc = self.lib.c4s_process(self._h, _dptr(logits), B, V, logits.stride(0), _dptr(hist),
+                                  _dptr(hist_off), total, _dptr(params), params_stride, stages,
+                                  self._stream(stream))
+        self._check(rc, "c4s_process")
+        return logits
+
+    def argmax(self, logits, V: int | None = None, out=None, stream=None):
+        torch = _torch()
+        B, ld = logits.shape
+        V = ld if V is None else V
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        rc = self.lib.c4s_argmax(self._h, _dptr(logits), B, V, logits.stride(0), _dptr(out),
+                                 self._stream(stream))
+        self._check(rc, "c4s_argmax")
+        return out
+
+
+# ---------------------------------------------------------------------------
+# The reference's five processors, same names and in-place semantics.
+# ---------------------------------------------------------------------------
+_default_ctx: dict = {}
+
+
+def default_context(max_vocab: int = MAX_VOCAB) -> SamplingContext:
+    torch = _torch()
+    dev = torch.cuda.current_device()
+    key = (threading.get_ident(), dev)
+    ctx = _default_ctx.get(key)
+    if ctx is None:
+        ctx = SamplingContext(max_vocab=max_vocab, device=dev)
+        _default_ctx[key] = ctx
+    return ctx
+
+
+def _as_row(logits):
+    """(device tensor [1, V], writeback callable) for a CUDA tensor, numpy array or list."""
+    torch = _torch()
+    if isinstance(logits, torch.Tensor):
+        if not logits.is_cuda or logits.dtype != torch.float32 or logits.dim() != 1:
+            raise TypeError("expected a 1-D float32 CUDA tensor")
+        if not logits.is_contiguous():
+            raise ValueError("logits must be contiguous")
+        return logits.view(1, -1), (lambda dev: None)
+    arr = np.asarray(logits, dtype=np.float32)
+    dev = torch.from_numpy(np.ascontiguousarray(arr).reshape(1, -1).copy()).cuda()
+
+    def writeback(d):
+        host = d.view(-1).cpu().numpy()
+        if isinstance(logits, np.ndarray):
+            logits[...] = host
+        else:
+            logits[:] = host.tolist()
+    return dev, writeback
+
+
+def _run(logits, P: dict, stages: int, prev_tokens=None):
+    torch = _torch()
+    dev, writeback = _as_row(logits)
+    if dev.shape[1] == 0:
+        return
+    ctx = default_context()
+    params = params_tensor(workloads.make_params(1, **P), dev.device)
+    hist = hist_off = None
+    if prev_tokens is not None:
+        h = np.ascontiguousarray(np.asarray(prev_tokens, dtype=np.int64).astype(np.int32))
+        hist = torch.from_numpy(h).to(dev.device)
+        hist_off = torch.tensor([0, h.size], dtype=torch.int64, device=dev.device)
+    ctx.process(dev, hist, hist_off, params, stages, params_stride=0)
+    writeback(dev)
+
+
+_NEUTRAL = dict(temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, greedy=0,
+                min_tokens_to_keep=1)
+
+
+def temperature(logits, temp: float) -> None:
+    """sampling.cpp:14-17: logits /= temp unless temp == 1 or temp <= 0."""
+    _run(logits, dict(_NEUTRAL, temperature=temp), STAGE_TEMPERATURE)
+
+
+def repetition_penalty(logits, prev_tokens, penalty: float) -> None:
+    """sampling.cpp:19-28: penalise each distinct in-range id of prev_tokens once."""
+    _run(logits, dict(_NEUTRAL, repetition_penalty=penalty), STAGE_PENALTY, prev_tokens)
+
+
+def top_k(logits, k: int) -> None:
+    """sampling.cpp:30-40: mask logits below the k-th largest to -inf."""
+    _run(logits, dict(_NEUTRAL, top_k=k), STAGE_TOP_K)
+
+
+def top_p(logits, p: float, min_tokens_to_keep: int = 1) -> None:
+    """sampling.cpp:42-71: nucleus mask with double softmax / cumulative sums."""
+    _run(logits, dict(_NEUTRAL, top_p=p, min_tokens_to_keep=min_tokens_to_keep), STAGE_TOP_P)
+
+
+def argmax(logits) -> int:
+    """sampling.cpp:73-76: index of the first maximum."""
+    torch = _torch()
+    dev, _ = _as_row(logits)
+    if dev.shape[1] == 0:
+        return 0
+    out = default_context().argmax(dev)
+    return int(out.cpu()[0])
