@@ -957,7 +957,9 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   if (prop.major != 10) { delete ctx; return C4S_ERR_CUDA; }  // built for sm_100a only
   ctx->num_sms = prop.multiProcessorCount;
-  const size_t smem_max = c4s::layout_for(max_vocab).total;
+  // The attribute is per kernel (not per context): always allow the largest
+  // row any context may launch, so contexts of different sizes coexist.
+  const size_t smem_max = c4s::layout_for(c4s::MAX_VOCAB).total;
   e = cudaFuncSetAttribute(c4s::rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   int p2 = 1;
