@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="only run this many steps of the main loop (for ncu), print nothing")
+    ap.add_argument("--profile-config", choices=["c2", "c0"], default="c2",
+                    help="with --profile-steps: c2 = config-2 rows (--rows), c0 = one config-0 row")
     return ap.parse_args()
 
 
@@ -216,8 +218,13 @@ def run_ours(args):
 
     # ---- inputs: pool of batches, this rank's block of the global batch ----
     pool, host = [], []
+    if args.profile_steps and args.profile_config == "c0":
+        B = 1
     for k in range(args.pool):
-        b = wl.config2(seed=2 + k, B=B, row_offset=rank * B)
+        if args.profile_steps and args.profile_config == "c0":
+            b = wl.config0(seed=k)
+        else:
+            b = wl.config2(seed=2 + k, B=B, row_offset=rank * B)
         pool.append(dict(
             logits=torch.from_numpy(b.logits).to(dev),
             hist=torch.from_numpy(b.hist).to(dev),

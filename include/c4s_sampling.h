@@ -85,8 +85,9 @@ typedef struct c4s_row_params {
 #define C4S_CNT_TOPP_EXACT_FALLBACK 0 /* top-p guard band hit: exact re-sum   */
 #define C4S_CNT_DRAW_EXACT_FALLBACK 1 /* draw guard band hit: exact re-sum    */
 #define C4S_CNT_TOPK_RADIX 2          /* top-k needed the full radix select   */
-#define C4S_CNT_TOPP_BINNED 3         /* top-p over more than the list cap     */
-#define C4S_CNT_DRAW_ROWPASS 4        /* draw over more than the list cap      */
+#define C4S_CNT_TOPP_BINNED 3         /* top-p over more survivors than one warp sorts */
+#define C4S_CNT_DRAW_ROWPASS 4        /* draw over more survivors than one warp sorts */
+#define C4S_CNT_DEFERRED 5            /* rows the fast kernel left to the general path */
 #define C4S_NUM_COUNTERS 8
 
 typedef struct c4s_ctx c4s_ctx;

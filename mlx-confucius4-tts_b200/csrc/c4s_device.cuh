@@ -74,6 +74,7 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
 struct MaxF { __device__ float operator()(float a, float b) const { return fmaxf(a, b); } };
 struct SumU64 { __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a + b; } };
 struct MaxU64 { __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a > b ? a : b; } };
+struct MinU64 { __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a < b ? a : b; } };
 struct SumI { __device__ int operator()(int a, int b) const { return a + b; } };
 
 // Exclusive scan of one uint64 per thread over the CTA; *total gets the sum.
@@ -242,6 +243,80 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+}  // namespace c4s
+
+namespace c4s {
+
+// ---------------------------------------------------------------------------
+// Warp bitonic sort (ascending) of n <= 32*E uint64 keys held in `buf`
+// (shared memory), by one full warp; blocked layout, lane l owns positions
+// [l*E, l*E+E). Pads with KEY_MAX beyond n.
+// ---------------------------------------------------------------------------
+template <int E>
+__device__ __forceinline__ void warp_sort_e(unsigned long long* buf, int n) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int p = lane * E + e;
+    v[e] = p < n ? buf[p] : KEY_MAX;
+  }
+#pragma unroll
+  for (int k = 2; k <= 32 * E; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j < E) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int e2 = e ^ j;
+          if (e2 > e) {
+            const bool up = ((lane * E + e) & k) == 0;
+            const unsigned long long a = v[e], b = v[e2];
+            if (up ? (a > b) : (a < b)) { v[e] = b; v[e2] = a; }
+          }
+        }
+      } else {
+        const int lj = j / E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int p = lane * E + e;
+          const unsigned long long o = __shfl_xor_sync(FULL, v[e], lj);
+          const bool keep_min = (((p & j) == 0) == ((p & k) == 0));
+          v[e] = keep_min ? (o < v[e] ? o : v[e]) : (o > v[e] ? o : v[e]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int p = lane * E + e;
+    if (p < n) buf[p] = v[e];
+  }
+  __syncwarp();
+}
+
+// n <= 128; whole warp must call.
+__device__ __forceinline__ void warp_sort(unsigned long long* buf, int n) {
+  if (n <= 1) { __syncwarp(); return; }
+  if (n <= 32) warp_sort_e<1>(buf, n);
+  else if (n <= 64) warp_sort_e<2>(buf, n);
+  else warp_sort_e<4>(buf, n);
+}
+
+}  // namespace c4s
+
+namespace c4s {
+
+// Ampere-style asynchronous global->shared copies (per-thread groups).
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 }  // namespace c4s

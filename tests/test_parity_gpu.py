@@ -204,8 +204,9 @@ def test_path_counters_and_no_errors(ctx, wl):
     gpu_sample(ctx, b, torch)
     err, cnt = ctx.status(reset=True)
     assert err == 0
-    # the exact fallbacks are rare events (guard band ~1e-10 of the mass)
-    assert cnt["topp_exact_fallback"] <= 2 and cnt["draw_exact_fallback"] <= 2
+    # rows handed to the general path are rare (only an undecided double-
+    # precision band or inputs outside the fast path's assumptions)
+    assert cnt["deferred"] <= 2
 
 
 # ---------------------------------------------------------------------------
