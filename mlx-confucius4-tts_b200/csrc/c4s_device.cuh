@@ -18,6 +18,12 @@ constexpr int MAX_VOCAB = 32768;      // row must fit in shared memory
 constexpr unsigned FULL = 0xffffffffu;
 constexpr unsigned long long KEY_MAX = ~0ull;
 
+// Barrier of the row-processing group: the NT threads of warps 0..NWARP-1.
+// It is named barrier 1, so warps outside the group (the fast kernel's list
+// warps) never take part; in a CTA of exactly NT threads it acts like
+// __syncthreads(). Orders shared-memory accesses among the participants.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+
 // ---------------------------------------------------------------------------
 // Keys. fkey() maps a float to a uint32 whose unsigned order is the float
 // order, with -0 folded onto +0 so that key equality is float equality.
@@ -63,11 +69,11 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = warp_reduce(v, op);
   if (lane == 0) red[warp] = v;
-  __syncthreads();
+  csync();
   T r = red[0];
 #pragma unroll
   for (int w = 1; w < NWARP; ++w) r = op(r, red[w]);
-  __syncthreads();
+  csync();
   return r;
 }
 
@@ -88,7 +94,7 @@ __device__ __forceinline__ unsigned long long block_exscan_u64(unsigned long lon
     if (lane >= o) x += y;
   }
   if (lane == 31) red[warp] = x;
-  __syncthreads();
+  csync();
   unsigned long long wbase = 0, tot = 0;
 #pragma unroll
   for (int w = 0; w < NWARP; ++w) {
@@ -96,7 +102,7 @@ __device__ __forceinline__ unsigned long long block_exscan_u64(unsigned long lon
     if (w < warp) wbase += t;
     tot += t;
   }
-  __syncthreads();
+  csync();
   *total = tot;
   return wbase + x - v;
 }
@@ -111,7 +117,7 @@ __device__ __forceinline__ int block_exscan_i32(int v, int* red, int* total) {
     if (lane >= o) x += y;
   }
   if (lane == 31) red[warp] = x;
-  __syncthreads();
+  csync();
   int wbase = 0, tot = 0;
 #pragma unroll
   for (int w = 0; w < NWARP; ++w) {
@@ -119,7 +125,7 @@ __device__ __forceinline__ int block_exscan_i32(int v, int* red, int* total) {
     if (w < warp) wbase += t;
     tot += t;
   }
-  __syncthreads();
+  csync();
   *total = tot;
   return wbase + x - v;
 }
@@ -182,7 +188,7 @@ __device__ __forceinline__ void bitonic_sort_u64(unsigned long long* a, int n) {
           if ((x > y) == up) { a[i] = y; a[ixj] = x; }
         }
       }
-      __syncthreads();
+      csync();
     }
   }
 }
@@ -208,6 +214,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, u
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
+// Arrive once (release semantics at CTA scope).
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned phase) {
   unsigned ok;
   asm volatile(
@@ -219,18 +229,33 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
       : "memory");
   return ok != 0;
 }
+// As mbar_try_wait, but a thread whose phase is not complete may be suspended
+// in hardware for up to `ns` nanoseconds (it resumes as soon as the phase
+// completes), so waiting warps take no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(unsigned long long* bar, unsigned phase, unsigned ns) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait (about 2 s of wall time); false if it gave up.
+// Bounded wait (about 2 s of wall time); false if it gave up. Each poll may
+// sleep up to 20 us in hardware until the phase completes.
 __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned phase) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (unsigned it = 0; it < (1u << 30); ++it) {
-    if (mbar_try_wait(bar, phase)) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) return false;
+    if (mbar_try_wait_sleep(bar, phase, 20000u)) return true;
+    if ((it & 15u) == 15u && globaltimer_ns() - t0 > 2000000000ull) return false;
   }
   return false;
 }

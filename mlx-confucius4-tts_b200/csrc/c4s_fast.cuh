@@ -1,49 +1,72 @@
 // c4s_fast.cuh -- the fast path of the fused sampling step (MODE_SAMPLE, rows
-// of up to F_MAXV logits).
+// of up to F_MAXV logits): three kernels per chunk of at most K_CHUNK rows.
 //
-// A persistent CTA processes rows blockIdx.x, +gridDim.x, ... with the row in
-// shared memory (4 CTAs per SM). The next row's logits are prefetched into
-// L2 while the current one is processed, and its metadata (params, history
-// window, xorshift state) arrives in shared memory by cp.async. Per row:
-//   - repetition penalty: scatter over the history, de-duplicated with a
-//     shared bitmap (sampling.cpp:19-28);
-//   - one pass: row max, per-thread maxima, first index of the max;
-//   - greedy rows: first index of the max (sampling.cpp:73-76);
-//   - top-k (sampling.cpp:30-40): each warp takes the ceil(k/8)-th largest of
-//     its 32 thread maxima and the least of these, tau, has at least k
-//     elements above it; the candidates >= tau (a few k at most) are divided
-//     by T and gathered without atomics; the k-th largest is then exact on
-//     that list (x/T is monotone in x);
-//   - top-p (sampling.cpp:42-71) and the draw (text2semantic.cpp:150-165):
-//     with <= F_SORT survivors one warp sorts them, locates the crossings with
-//     fixed-point prefix sums and accepts them outside a proven error band,
-//     else repeats the reference's sequential double sums exactly. Larger
-//     candidate lists use value bins (top-p) and index bins (the draw).
-//   - rows without top-k: a float estimate (untempered-x reciprocal product,
-//     __expf) locates the top-p crossing with per-thread private histograms
-//     (no atomics) and then float bins over one coarse bin; the <= F_SORT
-//     candidates of the crossing bin get exact values. Where the crossing is
-//     inside the estimate's error band, an exact double pass over the row
-//     decides; the draw likewise (index-order prefix, exact pass on demand).
-// Rows outside the fast path's assumptions (all -inf, |logits/T| >= 2^18,
-// min_tokens_to_keep > 1, top_k above 32 per full warp, an undecided double
-// band) go through the general path in the same CTA, on the staged row.
+//   row_kernel (persistent, NT threads, four CTAs per SM): thread t holds the
+//     36 row elements of positions [36t, 36t+36) in registers, loaded with
+//     16-byte streaming loads (no shared-memory row buffer, so many rows are
+//     in flight per SM). It applies the repetition penalty through a
+//     shared-memory bitmap of the row's history (sampling.cpp:19-28) and makes
+//     every pass over the row from registers:
+//       greedy rows: first index of the maximum (sampling.cpp:73-76);
+//       top-k rows: each full warp takes the ceil(k/wfull)-th largest of its
+//         lanes' maxima (of the two largest per lane when k > 64) and tau is
+//         the least of those, so at least k elements are >= tau; the
+//         candidates >= tau (minus a margin covering values that the
+//         temperature division merges) form the row's list: top_k keeps
+//         y >= (k-th largest y) and y = x/T is monotone, so every survivor is
+//         in it (sampling.cpp:30-40);
+//       rows without top-k: an octave histogram of error-bounded estimates
+//         of the probabilities locates the top-p crossing; the octaves down
+//         to it form the list, the deeper ones an estimated tail with a
+//         proven bound. When that list would be too long the row kernel
+//         finishes the row itself (sub-bins of the crossing octave, an exact
+//         sort of one sub-bin, the draw over per-thread survivor masses).
+//     Lists go to global memory (they stay in L2) with a per-row job record.
+//   list_kernel (one warp per row): exact top-k threshold by bisection on the
+//     value keys, exact double-precision probabilities, the top-p crossing
+//     and the draw (sampling.cpp:42-71, text2semantic.cpp:150-165).
+//   defer_kernel: the general path for the rare rows the others hand back
+//     (non-finite maxima, |max/T| >= 2^18, min_tokens_to_keep != 1, lists
+//     over LCAP, undecidable error bands).
+//   mask_kernel (only when processed logits are requested): applies the
+//     list kernel's top-k/top-p decisions to the tempered logits.
+//
+// Exactness: every decision taken from rounded or estimated sums is accepted
+// only outside a proven error band; inside it the reference's sequential
+// double sums are repeated exactly (or the row goes to the general path).
 #pragma once
 
 #include "c4s_general.cuh"
 
 namespace c4s {
 
-constexpr int F_MAXV = 9212;             // widest row the fast kernel takes
-constexpr int NB_Y = 256;                // value bins over candidate lists
-constexpr float YBIN = 8.0f;             // width 1/8
-constexpr int NB_I = 256;                // draw index bins (list path)
-constexpr int F_SORT = 128;              // warp-sort capacity
-constexpr int NB1 = 16;                  // rows without top-k: level-1 bins, width 2
-constexpr float L1SCALE = 0.5f;
-constexpr int NB2 = 256;                 // level-2 bins inside one level-1 bin
-constexpr float L2SCALE = 128.0f;        // width 1/128
-constexpr double EPS_F = 4.0e-5;         // relative error of the float estimates (with margin)
+constexpr int F_MAXV = 9212;              // widest row the fast path takes
+constexpr int OWN = 36;                   // row positions per row-kernel thread
+constexpr int LCAP = 512;                 // candidates per list
+constexpr int K_CHUNK = 8192;             // rows per launch sequence (list storage)
+constexpr int NOCT = 24;                  // octaves of the estimate; bin NOCT = the rest
+constexpr int BIG_SORT = 128;             // crossing sub-bin capacity (one warp sort)
+constexpr int CAND_CAP = 2048;            // crossing-octave candidates
+constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
+static_assert(OWN * NT >= F_MAXV + 3, "the ownership blocks cover every row position");
+static_assert(OWN <= 64, "per-thread candidate masks are 64 bits");
+
+enum { JOB_NONE = 0, JOB_TOPK = 1, JOB_K0 = 2, JOB_DEFER = 3 };
+enum { RES_DONE = 0, RES_DEFER = 1 };
+
+// Per-row job record: written by the row kernel, finished by the list kernel.
+struct __align__(16) RowJob {
+  int kind, n, k, status;
+  float m_y;                 // row maximum after temperature
+  unsigned ykex;             // JOB_K0: key of the largest value below the list (0: none)
+  unsigned thresh_key;       // result: top-k threshold key (0: none)
+  int pad;
+  double thr, u;             // 1 - top_p; uniform of the draw
+  double tail, tail_err;     // JOB_K0: estimated mass below the list and its error bound
+  unsigned long long u53, xs;
+  unsigned long long kstar;  // result: keys below K* are removed by top-p
+  unsigned long long pad2;
+};
 
 // Per-row metadata, fetched asynchronously one row ahead.
 struct __align__(16) MetaSlot {
@@ -54,63 +77,50 @@ struct __align__(16) MetaSlot {
   int pad;
 };
 
-struct FastLayout {
-  size_t row, bitmap, cnt, mass, un, ws, meta, total;
-};
-__host__ __device__ inline FastLayout fast_layout(int V) {
-  FastLayout L;
-  size_t o = 0;
-  L.row = o;    o += align_up((size_t)(V + 8) * 4, 16);      // + float4 over-read of the last block
-  L.bitmap = o; o += align_up((size_t)((V + 31) / 32) * 4, 16);
-  L.cnt = o;    o += 256 * 4;
-  L.mass = o;   o += 256 * 8;
-  L.un = o;     o += (size_t)LIST_CAP * 16;     // lkey[1024] + pv[1024] | float[NB1][NT]
-  L.ws = o;     o += F_SORT * 8;
-  L.meta = o;   o += 2 * sizeof(MetaSlot);
-  L.total = o;
-  return L;
+// Dynamic shared memory of the row kernel: the staged row; for rows without
+// top-k, after it is in registers, their octave columns and then the scratch
+// of their big path (same area).
+constexpr size_t RWORK_BYTES = (size_t)(NOCT + 1) * NT * 4;
+// Every thread reads its whole ownership block (NT * OWN positions), so the
+// buffer covers all of them, whatever V.
+__host__ __device__ inline size_t row_smem(int V) {
+  const size_t rb = (size_t)NT * OWN * 4;
+  (void)V;
+  return rb > RWORK_BYTES ? rb : RWORK_BYTES;
 }
-static_assert(LIST_CAP * 16 >= NB1 * NT * 4, "private histograms fit the union");
-static_assert(NBIN == 256 && NB_Y == 256 && NB_I == 256, "bin arrays are 256 wide");
-
-__device__ __forceinline__ int ybin(float m, float y) {
-  float t = __fmul_rn(__fsub_rn(m, y), YBIN);
-  t = fminf(t, (float)(NB_Y - 1));
-  return (int)t;
-}
-
-__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
+static_assert((size_t)NT * OWN >= (size_t)F_MAXV + 3, "the staged row (with its alignment shift) fits");
+static_assert(RWORK_BYTES >= 5 * 1024 + CAND_CAP * 8, "big-path scratch fits the work area");
 
 __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
   return v;
 }
-
-// Appends key to buf (capacity cap) for the lanes with pred; one shared
-// atomic per warp. All lanes of the warp must call.
-__device__ __forceinline__ void warp_append(bool pred, unsigned long long key, unsigned long long* buf, int cap,
-                                            int* counter) {
-  const unsigned bal = __ballot_sync(FULL, pred);
-  if (bal == 0) return;
-  const int lane = threadIdx.x & 31;
-  const int leader = __ffs(bal) - 1;
-  int base = 0;
-  if (lane == leader) base = atomicAdd(counter, __popc(bal));
-  base = __shfl_sync(FULL, base, leader);
-  if (pred) {
-    const int pos = base + __popc(bal & ((1u << lane) - 1u));
-    if (pos < cap) buf[pos] = key;
-  }
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+  return v;
 }
-
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(FULL, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(FULL, v, o);
+    v = w < v ? w : v;
+  }
+  return v;
+}
 struct SumD { __device__ double operator()(double a, double b) const { return a + b; } };
 struct MinF { __device__ float operator()(float a, float b) const { return fminf(a, b); } };
-struct MaxI { __device__ int operator()(int a, int b) const { return a > b ? a : b; } };
 
-// Exclusive scan of one double per thread over the CTA; *total gets the sum.
+// Exclusive scan of one double per thread of the CTA; *total gets the sum.
 __device__ __forceinline__ double block_exscan_f64(double v, double* red, double* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double x = v;
@@ -120,7 +130,7 @@ __device__ __forceinline__ double block_exscan_f64(double v, double* red, double
     if (lane >= o) x += y;
   }
   if (lane == 31) red[warp] = x;
-  __syncthreads();
+  csync();
   double wbase = 0.0, tot = 0.0;
 #pragma unroll
   for (int w = 0; w < NWARP; ++w) {
@@ -128,16 +138,16 @@ __device__ __forceinline__ double block_exscan_f64(double v, double* red, double
     if (w < warp) wbase += t;
     tot += t;
   }
-  __syncthreads();
+  csync();
   *total = tot;
   return wbase + x - v;
 }
 
-// Warp 0 search over NB bins (PER = NB/32 per lane), same contract as
-// warp_find_bin: first logical bin whose inclusive running sum exceeds
-// (strict) or reaches `target`.
+// Warp search over NB bins (PER = NB/32 per lane): first logical bin whose
+// inclusive running sum exceeds `target`; *before_out = sum of the bins
+// before it; *c_out = NB if none. Whole warp calls; one lane writes.
 template <int PER, typename T, typename Get>
-__device__ __forceinline__ void warp_find_bin_n(Get get, T target, bool strict, int* c_out, T* before_out) {
+__device__ __forceinline__ void warp_find_bin_n(Get get, T target, int* c_out, T* before_out) {
   const int lane = threadIdx.x & 31;
   T loc[PER];
   T s = 0;
@@ -149,8 +159,7 @@ __device__ __forceinline__ void warp_find_bin_n(Get get, T target, bool strict, 
     T y = __shfl_up_sync(FULL, incl, o);
     if (lane >= o) incl += y;
   }
-  const bool hit = strict ? (incl > target) : (incl >= target);
-  const unsigned bal = __ballot_sync(FULL, hit);
+  const unsigned bal = __ballot_sync(FULL, incl > target);
   if (bal == 0) {
     const T tot = __shfl_sync(FULL, incl, 31);
     if (lane == 0) { *c_out = 32 * PER; *before_out = tot; }
@@ -163,8 +172,7 @@ __device__ __forceinline__ void warp_find_bin_n(Get get, T target, bool strict, 
     T before = run;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      const bool h = strict ? (run + loc[j] > target) : (run + loc[j] >= target);
-      if (h) { c = L * PER + j; before = run; break; }
+      if (run + loc[j] > target) { c = L * PER + j; before = run; break; }
       run += loc[j];
     }
     *c_out = c;
@@ -172,999 +180,939 @@ __device__ __forceinline__ void warp_find_bin_n(Get get, T target, bool strict, 
   }
 }
 
-// Exact top-p of the reference over ws[0..n) sorted ascending by ckey, by one
-// warp: sequential double sum, per-term division, sequential cumulative sum.
-// Returns the first position whose cumulative probability exceeds thr (n if
-// none).
-__device__ __forceinline__ int warp_topp_exact(const unsigned long long* ws, int n, float m, double thr,
-                                               double* pv) {
-  const int lane = threadIdx.x & 31;
-  for (int e = lane; e < n; e += 32) pv[e] = prob(fkey_inv((unsigned)(ws[e] >> 32)), m);
-  __syncwarp();
-  double sum = 0.0;
-  if (lane == 0)
-    for (int e = 0; e < n; ++e) sum = __dadd_rn(sum, pv[e]);
-  sum = __shfl_sync(FULL, sum, 0);
-  for (int e = lane; e < n; e += 32) pv[e] = __ddiv_rn(pv[e], sum);
-  __syncwarp();
-  int js = n;
-  if (lane == 0) {
-    double cum = 0.0;
-    for (int e = 0; e < n; ++e) {
-      cum = __dadd_rn(cum, pv[e]);
-      if (!(cum <= thr)) { js = e; break; }
-    }
-  }
-  return __shfl_sync(FULL, js, 0);
+// Octave/sub-bin rank of an estimate p in (0, 1]: ((0x3F800000 - bits(p)) >>
+// 15) = 256 b + s, where octave b holds p in (2^-(b+1), 2^-b] and the 256
+// sub-bins s split it linearly in p; a larger rank is a smaller p. Clamped to
+// the last (open) octave NOCT.
+__device__ __forceinline__ int est_rank(float p) {
+  const int r = (int)(0x3F800000u - __float_as_uint(p)) >> 15;
+  return min(max(r, 0), NOCT * 256 + 255);
+}
+// |d| = |y - m_y| of an element whose estimate lies in octave b is below
+// (b+1) ln 2 (up to the estimate's own tiny error); the open octave holds
+// everything down to the clamp at -200.
+__device__ __forceinline__ double oct_d(int b) { return b < NOCT ? 0.6932 * (b + 1) : 200.0; }
+
+// Everything one sampled row's passes need.
+struct RowCtx {
+  int row, V, i0;            // i0: element index of this thread's first position
+  float m_x, m_y, T, rT;     // rT = RN(1/T) (1 without temperature)
+  bool do_t;
+  double thr, u;
+  unsigned long long xs, u53;
+};
+// fl(x / T), the reference's tempered value (sampling.cpp:16).
+__device__ __forceinline__ float yex(const RowCtx& rc, float x) { return rc.do_t ? div_rn(x, rc.T, rc.rT) : x; }
+// Estimate of y - m_y: one rounding of x * RN(1/T) - m_y, clamped at -200.
+__device__ __forceinline__ float dest(const RowCtx& rc, float x) { return fmaxf(fmaf(x, rc.rT, -rc.m_y), -200.0f); }
+
+// Unit roundoff of float.
+constexpr double U24 = 5.9604644775390625e-08;
+
+// Error bound of an estimated mass `mass` = sum of p~ over a set, where
+// dmass >= sum of |d| p~ over the same set. Per element, with u = 2^-24 and
+// |d| = |y - m_y|: the estimate d~ of y - m_y (one FMA from x, RN(1/T) and
+// m_y) is within u(2|m_y| + 4|d|) of the reference's fl(fl(x/T) - m_y);
+// __expf adds at most (2 + 1.2|d|) ulps (CUDA documents 2 + floor(|1.173 d|)),
+// i.e. (4 + 2.4|d|)u relative; so |p~ - p| <= u(4 + 2|m_y| + 6.4|d|) p~. Float
+// sums of at most nsum terms add nsum*u of their magnitude. Results that
+// __expf flushes to zero (or the clamp at -200) hide at most 2^-125 each.
+// 5% margin on the whole.
+__device__ __forceinline__ double est_err(double mass, double dmass, float m_y, int nsum, int nelem) {
+  return U24 * 1.05 * ((4.0 + 2.0 * fabs((double)m_y) + (double)nsum) * mass + 6.4 * dmass) +
+         (double)nelem * 2.3509887016445750e-38;
 }
 
-// Exact draw of the reference over ws[0..n) sorted by index, keys
-// (index << 32 | fkey(y)), by one warp. Returns the token.
-__device__ __forceinline__ int warp_draw_exact(const unsigned long long* ws, int n, float md, double u, int V,
-                                               double* pv) {
+// Hands a row to the general path (defer_kernel).
+__device__ __forceinline__ void defer_row(const Args& a, int row) {
+  const unsigned t = atomicAdd(&a.defer_cnt[0], 1u);
+  a.defer_rows[t] = row;
+  atomicAdd(&a.counters[C4S_CNT_DEFERRED], 1ull);
+}
+
+// ===========================================================================
+// List kernel: one warp per row
+// ===========================================================================
+
+// Warp bitonic sort (ascending) of np (power of two, <= LCAP) keys.
+__device__ void warp_bitonic(unsigned long long* b, int np) {
   const int lane = threadIdx.x & 31;
-  for (int e = lane; e < n; e += 32) pv[e] = prob(fkey_inv((unsigned)ws[e]), md);
-  __syncwarp();
-  int tok = V - 1;
-  if (lane == 0) {
-    double sum = 0.0;
-    for (int e = 0; e < n; ++e) sum = __dadd_rn(sum, pv[e]);
-    const double r = __dmul_rn(u, sum);
-    if (r == 0.0) {
-      tok = 0;
-    } else {
-      double acc = 0.0;
-      for (int e = 0; e < n; ++e) {
-        acc = __dadd_rn(acc, pv[e]);
-        if (r <= acc) { tok = (int)(ws[e] >> 32); break; }
+  for (int k = 2; k <= np; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < np; i += 32) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long x = b[i], y = b[ixj];
+          const bool up = (i & k) == 0;
+          if ((x > y) == up) { b[i] = y; b[ixj] = x; }
+        }
       }
-    }
-  }
-  return __shfl_sync(FULL, tok, 0);
-}
-
-// Warp-level inclusive prefix of fixed-point masses over ws[0..n) (blocked,
-// 4 entries per lane, n <= 128); finds the first entry whose prefix
-// (plus `before`) satisfies pred(prefix). Returns the entry (n if none) and
-// the prefixes just before it and at it.
-template <typename QOf, typename Pred>
-__device__ __forceinline__ int warp_prefix_find(const unsigned long long* ws, int n, unsigned long long before,
-                                                QOf qof, Pred pred, unsigned long long* prev_out,
-                                                unsigned long long* cur_out) {
-  const int lane = threadIdx.x & 31;
-  unsigned long long q[4];
-  unsigned long long s = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    q[j] = e < n ? qof(ws[e]) : 0ull;
-    s += q[j];
-  }
-  unsigned long long incl = s;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long y = __shfl_up_sync(FULL, incl, o);
-    if (lane >= o) incl += y;
-  }
-  unsigned long long run = before + incl - s;
-  int found = n;
-  unsigned long long pv_ = 0, cv = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    if (found == n && e < n && pred(run + q[j])) { found = e; pv_ = run; cv = run + q[j]; }
-    run += q[j];
-  }
-  const unsigned bal = __ballot_sync(FULL, found < n);
-  if (bal == 0) {
-    *prev_out = __shfl_sync(FULL, run, 31);
-    *cur_out = *prev_out;
-    return n;
-  }
-  const int L = __ffs(bal) - 1;
-  *prev_out = __shfl_sync(FULL, pv_, L);
-  *cur_out = __shfl_sync(FULL, cv, L);
-  return __shfl_sync(FULL, found, L);
-}
-
-
-// ---------------------------------------------------------------------------
-// Small survivor set (ns <= F_SORT), one warp: ws[0..ns) holds the survivors
-// of top-k as ckeys. Decides top-p and draws; each crossing is taken from
-// fixed-point prefix sums when it lies outside the proven error band, else
-// the reference's sequential sums are repeated exactly. exp() runs once per
-// survivor. Returns the token; K* via *kstar. pv needs 2*F_SORT doubles.
-// Whole warp must call.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ int warp_small_row(unsigned long long* ws, int ns, bool presorted, float m, double thr,
-                                              int mk, unsigned long long u53, double u, int V, double qs,
-                                              double* pv, unsigned long long* kstar) {
-  const int lane = threadIdx.x & 31;
-  if (!presorted) warp_sort(ws, ns);
-  else __syncwarp();
-  unsigned long long q[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    const double p = e < ns ? prob(fkey_inv((unsigned)(ws[e] >> 32)), m) : 0.0;
-    if (e < ns) pv[e] = p;
-    q[j] = qfix(p, qs);
-  }
-  __syncwarp();
-  // blocked warp prefix: first entry whose inclusive prefix satisfies pred
-  auto find = [&](const unsigned long long (&qq)[4], int n, auto pred, unsigned long long* prev,
-                  unsigned long long* cur, unsigned long long* total) {
-    const unsigned long long s = qq[0] + qq[1] + qq[2] + qq[3];
-    unsigned long long incl = s;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long y = __shfl_up_sync(FULL, incl, o);
-      if (lane >= o) incl += y;
-    }
-    *total = __shfl_sync(FULL, incl, 31);
-    unsigned long long run = incl - s, pv_ = 0, cv = 0;
-    int found = n;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = lane * 4 + j;
-      if (found == n && e < n && pred(run + qq[j])) { found = e; pv_ = run; cv = run + qq[j]; }
-      run += qq[j];
-    }
-    const unsigned bal = __ballot_sync(FULL, found < n);
-    if (bal == 0) { *prev = *total; *cur = *total; return n; }
-    const int L = __ffs(bal) - 1;
-    *prev = __shfl_sync(FULL, pv_, L);
-    *cur = __shfl_sync(FULL, cv, L);
-    return __shfl_sync(FULL, found, L);
-  };
-  int js;
-  if (thr < 0.0) {
-    js = 0;                                             // p > 1: nothing removed
-  } else if (thr == 0.0) {
-    int first = ns;                                     // p == 1: only zero probabilities go
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = lane * 4 + j;
-      if (e < ns && pv[e] > 0.0) first = e < first ? e : first;
-    }
-    js = (int)__reduce_min_sync(FULL, (unsigned)first);
-  } else {
-    unsigned long long prev, cur, SQ;
-    const int e0 = find(q, ns, [&](unsigned long long A) { return false; }, &prev, &cur, &SQ);
-    (void)e0;
-    const double SQd = (double)SQ, Tq = __dmul_rn(thr, SQd), bq = band_q(ns, SQd);
-    const int e = find(q, ns, [Tq](unsigned long long A) { return (double)A > Tq; }, &prev, &cur, &SQ);
-    bool ok;
-    if (mk >= 1 && e >= ns - 1) {
-      // the last element is kept anyway: only the mass below it must be certain
-      const unsigned long long below = (e == ns - 1) ? prev : SQ - qfix(pv[ns - 1], qs);
-      ok = (double)below <= Tq - bq;
-      js = ns - 1;
-    } else {
-      ok = (double)prev <= Tq - bq && (e == ns || (double)cur > Tq + bq);
-      js = e;
-    }
-    if (!ok) js = warp_topp_exact(ws, ns, m, thr, pv + F_SORT);
-  }
-  const unsigned long long Kp = js < ns ? ws[js] : KEY_MAX;
-  const unsigned long long Kk = mk <= 0 ? KEY_MAX : ws[ns - 1];
-  const unsigned long long K = Kp < Kk ? Kp : Kk;
-  *kstar = K;
-  if (u53 == 0ull) return 0;
-  int jf = 0;
-  for (int e = lane; e < ns; e += 32) jf += (ws[e] < K) ? 1 : 0;
-  jf = __reduce_add_sync(FULL, jf);
-  const int nk = ns - jf;
-  if (nk == 0) return 0;
-  // survivors of top-p by index; the low word keeps their position in pv
-  unsigned long long t[F_SORT / 32];
-#pragma unroll
-  for (int qq = 0; qq < F_SORT / 32; ++qq) {
-    const int e = jf + lane + 32 * qq;
-    t[qq] = e < ns ? (((unsigned long long)ckey_idx(ws[e]) << 32) | (unsigned)e) : KEY_MAX;
-  }
-  __syncwarp();
-#pragma unroll
-  for (int qq = 0; qq < F_SORT / 32; ++qq) {
-    const int e = lane + 32 * qq;
-    if (e < nk) ws[e] = t[qq];
-  }
-  __syncwarp();
-  warp_sort(ws, nk);
-  unsigned long long qd[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    qd[j] = e < nk ? qfix(pv[(unsigned)ws[e]], qs) : 0ull;
-  }
-  unsigned long long prev, cur, S2;
-  (void)find(qd, nk, [&](unsigned long long A) { return false; }, &prev, &cur, &S2);
-  const double S2d = (double)S2, rq = __dmul_rn(u, S2d), bq2 = band_q(nk, S2d);
-  const int e = find(qd, nk, [rq](unsigned long long A) { return (double)A >= rq; }, &prev, &cur, &S2);
-  if (S2 > 0 && e < nk && (double)prev < rq - bq2 && (double)cur > rq + bq2) return (int)(ws[e] >> 32);
-  // exact: the reference's sequential sums over the same probabilities, index order
-  int tok = V - 1;
-  if (lane == 0) {
-    double sum = 0.0;
-    for (int e2 = 0; e2 < nk; ++e2) sum = __dadd_rn(sum, pv[(unsigned)ws[e2]]);
-    const double r = __dmul_rn(u, sum);
-    if (r == 0.0) {
-      tok = 0;
-    } else {
-      double acc = 0.0;
-      for (int e2 = 0; e2 < nk; ++e2) {
-        acc = __dadd_rn(acc, pv[(unsigned)ws[e2]]);
-        if (r <= acc) { tok = (int)(ws[e2] >> 32); break; }
-      }
-    }
-  }
-  return __shfl_sync(FULL, tok, 0);
-}
-
-// ---------------------------------------------------------------------------
-// Top-p and the draw over the survivors of top-k, lkey[0..ns) (unordered
-// ckeys of the tempered values). Commits the id and the state and leaves K*
-// in S.kp. Returns false to defer the row (nothing written then).
-// ---------------------------------------------------------------------------
-__device__ bool list_topp_draw(const Args& a, int row, int ns, float m_y, double thr, int mk,
-                               unsigned long long u53, double u, unsigned long long xs, bool force_bins,
-                               unsigned long long* lkey, double* pv, unsigned long long* ws,
-                               unsigned long long* mass, Shared& S) {
-  const int V = a.V;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  auto each = [&](auto&& f) {
-    for (int e = tid; e < ns; e += NT) {
-      const unsigned long long key = lkey[e];
-      f(fkey_inv((unsigned)(key >> 32)), ckey_idx(key));
-    }
-  };
-  if (ns <= F_SORT && !force_bins) {
-    // one warp finishes the row
-    if (warp == 0) {
-      for (int e = lane; e < ns; e += 32) ws[e] = lkey[e];
       __syncwarp();
-      unsigned long long K;
-      const int t = warp_small_row(ws, ns, false, m_y, thr, mk, u53, u, V, a.qscale, pv, &K);
-      if (lane == 0) {
-        S.kp = K;
-        a.out_ids[row] = t;
-        a.rng[row] = xs;
-      }
     }
-    __syncthreads();
-    return true;
   }
-  // ---- top-p: fixed-point mass per value bin ----
-  for (int j = tid; j < NB_Y; j += NT) mass[j] = 0ull;
-  __syncthreads();
-  unsigned long long kmax = 0, kminp = KEY_MAX;
-  each([&](float y, int i) {
-    const double pr = prob(y, m_y);
-    atomicAdd(&mass[ybin(m_y, y)], qfix(pr, a.qscale));
-    const unsigned long long key = ckey(y, i);
-    kmax = key > kmax ? key : kmax;
-    if (pr > 0.0) kminp = key < kminp ? key : kminp;
-  });
-  kmax = block_reduce(kmax, MaxU64(), S.red64);
-  kminp = block_reduce(kminp, MinU64(), S.red64);
-  const unsigned long long SQ = block_reduce(mass[tid], SumU64(), S.red64);
-  const unsigned long long Kk = mk <= 0 ? KEY_MAX : kmax;
-  const double SQd = (double)SQ, Tq = __dmul_rn(thr, SQd), bq = band_q(ns, SQd);
-  unsigned long long Kp = 0ull;
-  bool need_cross = true;
+}
+
+// One list job. keys[0..n): ckey(y, i) of the candidates in index order
+// (list position = index order); pv: their probabilities by position (zero
+// for candidates that top-k removes); sb: sort buffer of the exact fallback.
+__device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const unsigned long long* keys, double* pv,
+                                      unsigned long long* sb) {
+  const int lane = threadIdx.x & 31;
+  const int n = J.n, V = a.V, k = J.k;
+  const float m_y = J.m_y;
+  const bool k0 = J.kind == JOB_K0;
+  const bool forced = (a.debug & C4S_DEBUG_FORCE_BINS) != 0;
+  auto vkey = [&](int e) { return (unsigned)(keys[e] >> 32); };
+  auto hand_back = [&]() {
+    if (lane == 0) {
+      J.status = RES_DEFER;
+      defer_row(a, row);
+    }
+  };
+  unsigned vmin = 0xffffffffu, vmax = 0u;
+  for (int e = lane; e < n; e += 32) {
+    const unsigned v = vkey(e);
+    vmin = min(vmin, v);
+    vmax = max(vmax, v);
+  }
+  vmin = __reduce_min_sync(FULL, vmin);
+  vmax = __reduce_max_sync(FULL, vmax);
+  // no-top-k list: everything below it must be strictly smaller in value
+  if (k0 && J.ykex >= vmin) { hand_back(); return; }
+
+  // ---- top-k threshold: the k-th largest value key (sampling.cpp:30-40) ----
+  unsigned tk = vmin;
+  if (k > 0 && k < n && vmin != vmax) {
+    const int b0 = 31 - __clz(vmin ^ vmax);
+    unsigned v = b0 >= 31 ? 0u : (vmax & ~((2u << b0) - 1u));
+    for (int b = b0; b >= 0; --b) {
+      const unsigned c = v | (1u << b);
+      int cnt = 0;
+      for (int e = lane; e < n; e += 32) cnt += vkey(e) >= c ? 1 : 0;
+      if (__reduce_add_sync(FULL, cnt) >= k) v = c;
+    }
+    tk = v;
+  }
+
+  // ---- exact probabilities of the survivors (sampling.cpp:52-55) ----
+  double ps = 0.0;
+  int ns = 0;
+  unsigned smin = 0xffffffffu;
+  unsigned long long kmax = 0ull;
+  for (int e = lane; e < n; e += 32) {
+    const unsigned v = vkey(e);
+    double p = 0.0;
+    if (v >= tk) {
+      p = prob(fkey_inv(v), m_y);
+      ++ns;
+      smin = min(smin, v);
+      const unsigned long long kk = keys[e];
+      kmax = kk > kmax ? kk : kmax;
+    }
+    pv[e] = p;
+    ps += p;
+  }
+  ps = warp_sum_d(ps);
+  ns = __reduce_add_sync(FULL, ns);
+  smin = __reduce_min_sync(FULL, smin);
+  kmax = warp_max_u64(kmax);
+  __syncwarp();
+
+  // ---- top-p (sampling.cpp:42-71) ----
+  const double thr = J.thr;
+  const double tail = J.tail;
+  const double St = tail + ps;
+  unsigned long long kst = 0ull;
+  bool exact_tp = false;
   if (thr < 0.0) {
-    need_cross = false;                                   // p > 1: nothing removed
+    kst = 0ull;                                       // p > 1: nothing removed
   } else if (thr == 0.0) {
-    Kp = kminp;                                           // p == 1: only zero probabilities go
-    need_cross = false;
-  } else if (Tq >= SQd - a.qscale) {
-    if ((mk >= 1 && SQd - a.qscale <= Tq - bq) || (mk <= 0 && SQd <= Tq - bq)) {
-      Kp = KEY_MAX;                                       // crossing at the largest element at most
-      need_cross = false;
-    } else if (Tq >= SQd) {
-      return false;
+    unsigned long long mk0 = KEY_MAX;                 // p == 1: only zero probabilities go
+    for (int e = lane; e < n; e += 32)
+      if (vkey(e) >= tk && pv[e] > 0.0) mk0 = keys[e] < mk0 ? keys[e] : mk0;
+    kst = warp_min_u64(mk0);
+  } else {
+    const double Th = thr * St;
+    // G(c) = tail + sum of p over value keys < c (removed candidates have p = 0);
+    // the largest c with G(c) <= Th is the value of the crossing element
+    const int b0 = (smin == vmax) ? -1 : 31 - __clz(smin ^ vmax);
+    unsigned v = b0 < 0 ? smin : (b0 >= 31 ? 0u : (vmax & ~((2u << b0) - 1u)));
+    for (int b = b0; b >= 0; --b) {
+      const unsigned c = v | (1u << b);
+      double g = 0.0;
+      for (int e = lane; e < n; e += 32) g += vkey(e) < c ? pv[e] : 0.0;
+      if (tail + warp_sum_d(g) <= Th) v = c;
+    }
+    double G = 0.0, Mg = 0.0;
+    int cg = 0;
+    for (int e = lane; e < n; e += 32) {
+      const unsigned ve = vkey(e);
+      if (ve < v) G += pv[e];
+      else if (ve == v && ve >= tk) { Mg += pv[e]; ++cg; }
+    }
+    G = tail + warp_sum_d(G);
+    Mg = warp_sum_d(Mg);
+    cg = __reduce_add_sync(FULL, cg);
+    if (cg > 0 && G <= Th && G + Mg > Th) {
+      // crossing inside the value group v; equal values have equal p and
+      // keep index order
+      const double pg = Mg / cg;
+      int t = 1;
+      if (cg > 1) {
+        const double q = floor((Th - G) / pg) + 1.0;
+        t = (int)fmin(fmax(q, 1.0), (double)cg);
+      }
+      int es = 0, acc = 0;
+      for (int e0 = 0; e0 < n; e0 += 32) {
+        const int e = e0 + lane;
+        unsigned bal = __ballot_sync(FULL, e < n && vkey(e) == v);
+        const int c = __popc(bal);
+        if (t <= acc + c) {
+          for (int r = acc + 1; r < t; ++r) bal &= bal - 1u;
+          es = e0 + __ffs(bal) - 1;
+          break;
+        }
+        acc += c;
+      }
+      const double before = G + (double)(t - 1) * pg, cur = G + (double)t * pg;
+      const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
+      kst = keys[es];
+      exact_tp = !(before <= Th - bd && cur > Th + bd);
+    } else {
+      kst = KEY_MAX;                                  // no crossing: only the kept maximum
+      exact_tp = true;
+    }
+    exact_tp = exact_tp || forced;
+  }
+  if (exact_tp) {
+    if (k0) { hand_back(); return; }                  // the tail is only estimated here
+    // the reference's sequential sums over the survivors in ascending order
+    int base = 0;
+    for (int e0 = 0; e0 < n; e0 += 32) {
+      const int e = e0 + lane;
+      const bool sv = e < n && vkey(e) >= tk;
+      const unsigned bal = __ballot_sync(FULL, sv);
+      if (sv) sb[base + __popc(bal & ((1u << lane) - 1u))] = keys[e];
+      base += __popc(bal);
+    }
+    int np = 1;
+    while (np < ns) np <<= 1;
+    for (int s = ns + lane; s < np; s += 32) sb[s] = KEY_MAX;
+    __syncwarp();
+    warp_bitonic(sb, np);
+    for (int s = lane; s < ns; s += 32) pv[s] = prob(fkey_inv((unsigned)(sb[s] >> 32)), m_y);
+    __syncwarp();
+    int js = ns;
+    if (lane == 0) {
+      double sum = 0.0;
+      for (int s = 0; s < ns; ++s) sum = __dadd_rn(sum, pv[s]);
+      double cum = 0.0;
+      for (int s = 0; s < ns; ++s) {
+        cum = __dadd_rn(cum, __ddiv_rn(pv[s], sum));
+        if (!(cum <= thr)) { js = s; break; }
+      }
+      atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
+    }
+    js = __shfl_sync(FULL, js, 0);
+    kst = js < ns ? sb[js] : KEY_MAX;
+    __syncwarp();
+    // probabilities by position again, for the draw
+    for (int e = lane; e < n; e += 32) pv[e] = vkey(e) >= tk ? prob(fkey_inv(vkey(e)), m_y) : 0.0;
+    __syncwarp();
+  }
+  kst = kst < kmax ? kst : kmax;                      // min_tokens_to_keep = 1
+
+  // ---- the draw (text2semantic.cpp:150-165); index order = position order ----
+  auto kept = [&](int e) { return e < n && vkey(e) >= tk && keys[e] >= kst; };
+  int tok = 0;
+  if (J.u53 != 0ull) {
+    const double u = J.u;
+    double s2 = 0.0;
+    int nk = 0;
+    for (int e = lane; e < n; e += 32)
+      if (kept(e)) { s2 += pv[e]; ++nk; }
+    s2 = warp_sum_d(s2);
+    nk = __reduce_add_sync(FULL, nk);
+    const double r = u * s2;
+    double carry = 0.0, prev = 0.0, cur = 0.0;
+    int found = -1;
+    for (int e0 = 0; e0 < n; e0 += 32) {
+      const int e = e0 + lane;
+      const bool kp = kept(e);
+      const double x = kp ? pv[e] : 0.0;
+      double incl = x;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += y;
+      }
+      incl += carry;
+      const unsigned bal = __ballot_sync(FULL, kp && incl >= r);
+      if (bal) {
+        const int L = __ffs(bal) - 1;
+        found = e0 + L;
+        prev = __shfl_sync(FULL, incl - x, L);
+        cur = __shfl_sync(FULL, incl, L);
+        break;
+      }
+      carry = __shfl_sync(FULL, incl, 31);
+    }
+    const double bd2 = 2.0 * ((4.0 * nk + 16.0) * U53 * s2);
+    if (!forced && found >= 0 && prev < r - bd2 && cur > r + bd2) {
+      tok = ckey_idx(keys[found]);
+    } else {
+      // the reference's sequential sums in index order
+      int t = V - 1;
+      if (lane == 0) {
+        double sum = 0.0;
+        for (int e = 0; e < n; ++e)
+          if (kept(e)) sum = __dadd_rn(sum, pv[e]);
+        const double rr = __dmul_rn(u, sum);
+        double acc = 0.0;
+        for (int e = 0; e < n; ++e) {
+          if (kept(e)) {
+            acc = __dadd_rn(acc, pv[e]);
+            if (rr <= acc) { t = ckey_idx(keys[e]); break; }
+          }
+        }
+        atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
+      }
+      tok = __shfl_sync(FULL, t, 0);
     }
   }
-  if (need_cross) {
-    const unsigned long long target = (unsigned long long)floor(Tq);
-    if (warp == 0)
-      warp_find_bin_n<NB_Y / 32, unsigned long long>([&](int j) { return mass[NB_Y - 1 - j]; }, target, true,
-                                                     &S.c, &S.mbefore);
-    if (tid == 0) S.slot = 0;
-    __syncthreads();
-    const int cb = NB_Y - 1 - S.c;
-    each([&](float y, int i) {
-      if (ybin(m_y, y) == cb) {
-        const int sl = atomicAdd(&S.slot, 1);
-        if (sl < F_SORT) ws[sl] = ckey(y, i);
+  if (lane == 0) {
+    a.out_ids[row] = tok;
+    a.rng[row] = J.xs;
+    J.kstar = kst;
+    J.thresh_key = k > 0 ? tk : 0u;
+    J.status = RES_DONE;
+  }
+}
+
+__global__ void __launch_bounds__(32 * LIST_WARPS) list_kernel(Args a) {
+  const int row = blockIdx.x * LIST_WARPS + (threadIdx.x >> 5);
+  if (row >= a.B) return;
+  RowJob& J = a.jobs[row];
+  const int kind = J.kind;
+  if (kind != JOB_TOPK && kind != JOB_K0) return;
+  const size_t o = (size_t)row * LCAP;
+  list_job(a, row, J, a.lkeys + o, a.lpv + o, a.lsb + o);
+}
+
+// ===========================================================================
+// Row kernel
+// ===========================================================================
+
+// This thread's block of the staged row into registers: buffer positions
+// [36t, 36t+36) (element index = position - shift); positions outside the row
+// read as -inf (never a candidate, mass 0).
+__device__ __forceinline__ void load_block(const float* rowbuf, int shift, int V, float (&x)[OWN]) {
+  const int p0 = threadIdx.x * OWN;
+#pragma unroll
+  for (int q = 0; q < OWN / 4; ++q) {
+    const int i = p0 + 4 * q - shift;
+    const float4 v = *reinterpret_cast<const float4*>(rowbuf + p0 + 4 * q);
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) x[4 * q + r] = (unsigned)(i + r) < (unsigned)V ? vv[r] : -INFINITY;
+  }
+}
+
+// x[j] for a run-time j (a select chain: registers cannot be indexed).
+__device__ __forceinline__ float pick(const float (&x)[OWN], int j) {
+  float v = x[0];
+#pragma unroll
+  for (int jj = 1; jj < OWN; ++jj) v = (j == jj) ? x[jj] : v;
+  return v;
+}
+
+// Writes a row of processed logits from the registers: y, or -inf where the
+// top-k threshold key or K* removes it.
+__device__ __forceinline__ void write_row(const Args& a, const RowCtx& rc, const float (&x)[OWN], bool temper,
+                                          unsigned thresh_key, unsigned long long kst) {
+  float* o = a.out_logits + (long long)rc.row * a.out_ld;
+#pragma unroll
+  for (int j = 0; j < OWN; ++j) {
+    const int i = rc.i0 + j;
+    if ((unsigned)i < (unsigned)rc.V) {
+      const float y = temper ? yex(rc, x[j]) : x[j];
+      const bool masked = fkey(y) < thresh_key || (y > -INFINITY && ckey(y, i) < kst);
+      o[i] = masked ? -INFINITY : y;
+    }
+  }
+}
+
+// Candidate of the big path: a row element of the crossing octave.
+struct Cand {
+  float x;
+  int pos;                   // owner thread * OWN + j
+};
+
+// The kw-th largest (1 <= kw <= 64) of the warp's 64 keys (a and b of each
+// lane): bitonic sort of two keys per lane (blocked layout).
+__device__ __forceinline__ unsigned warp_kth_largest64(unsigned a, unsigned b, int kw) {
+  const int lane = threadIdx.x & 31;
+  unsigned v0 = a, v1 = b;
+#pragma unroll
+  for (int k2 = 2; k2 <= 64; k2 <<= 1) {
+#pragma unroll
+    for (int jj = k2 >> 1; jj > 0; jj >>= 1) {
+      if (jj == 1) {
+        const bool up = ((2 * lane) & k2) == 0;
+        const unsigned lo = min(v0, v1), hi = max(v0, v1);
+        v0 = up ? lo : hi;
+        v1 = up ? hi : lo;
+      } else {
+        const int lj = jj >> 1;
+        const unsigned o0 = __shfl_xor_sync(FULL, v0, lj), o1 = __shfl_xor_sync(FULL, v1, lj);
+        const int q0 = 2 * lane, q1 = 2 * lane + 1;
+        const bool m0 = ((q0 & jj) == 0) == ((q0 & k2) == 0);
+        const bool m1 = ((q1 & jj) == 0) == ((q1 & k2) == 0);
+        v0 = m0 ? min(v0, o0) : max(v0, o0);
+        v1 = m1 ? min(v1, o1) : max(v1, o1);
       }
-    });
-    __syncthreads();
-    const int nc = S.slot;
-    if (nc > F_SORT) return false;
+    }
+  }
+  const int pos = 64 - kw;                         // ascending order
+  const unsigned w0 = __shfl_sync(FULL, v0, pos >> 1), w1 = __shfl_sync(FULL, v1, pos >> 1);
+  return (pos & 1) ? w1 : w0;
+}
+// The kw-th largest (1 <= kw <= 32) of the warp's 32 keys.
+__device__ __forceinline__ unsigned warp_kth_largest32(unsigned key, int kw) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+    for (int jj = k2 >> 1; jj > 0; jj >>= 1) {
+      const unsigned o = __shfl_xor_sync(FULL, key, jj);
+      const bool keep_min = (((lane & jj) == 0) == ((lane & k2) == 0));
+      key = keep_min ? (o < key ? o : key) : (o > key ? o : key);
+    }
+  }
+  return __shfl_sync(FULL, key, 32 - kw);
+}
+
+// Header fields common to both list job kinds (thread 0).
+__device__ __forceinline__ void fill_job(RowJob& J, const RowCtx& rc, int kind, int n, int k) {
+  J.kind = kind;
+  J.n = n;
+  J.k = k;
+  J.status = RES_DONE;
+  J.m_y = rc.m_y;
+  J.thresh_key = 0u;
+  J.thr = rc.thr;
+  J.u = rc.u;
+  J.u53 = rc.u53;
+  J.xs = rc.xs;
+  J.kstar = 0ull;
+}
+
+// Writes the keys of this thread's candidates (bit j of mask: position j)
+// into the row's list from wpos on, in index order.
+__device__ __forceinline__ void write_keys(unsigned long long* keys, const RowCtx& rc, const float (&x)[OWN],
+                                           unsigned long long mask, int wpos) {
+  while (mask) {
+    const int j = __ffsll((long long)mask) - 1;
+    mask &= mask - 1ull;
+    keys[wpos++] = ckey(yex(rc, pick(x, j)), rc.i0 + j);
+  }
+}
+
+enum { ROW_DONE = 0, ROW_GENERAL = 1 };
+
+// Rows without top-k (top-p over the whole row, sampling.cpp:42-71, and the
+// draw). One pass builds an octave histogram of the estimates (private
+// per-thread columns, no atomics) and locates the octave of the top-p
+// crossing. If the octaves down to it hold at most LCAP elements they become
+// a list job whose tail (the deeper octaves) is an estimate with a proven
+// bound that the list kernel checks exactly. Otherwise the row kernel
+// finishes the row: sub-bins and candidates of the crossing octave, an exact
+// sort of the crossing sub-bin, then the draw over per-thread survivor masses.
+__device__ __noinline__ int k0_row(const Args& a, const RowCtx& rc, const float (&x)[OWN], unsigned char* work,
+                                   Shared& S, bool forced) {
+  const int V = rc.V, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = rc.row;
+  const float m_y = rc.m_y;
+  const double thr = rc.thr;
+
+  // ---- octave histogram of the estimates ----
+  float* Hc = reinterpret_cast<float*>(work);
+#pragma unroll
+  for (int b = 0; b <= NOCT; ++b) Hc[b * NT + tid] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < OWN; ++j) {
+    const float p = __expf(dest(rc, x[j]));
+    Hc[(est_rank(p) >> 8) * NT + tid] += p;
+  }
+  csync();
+  for (int b = warp; b <= NOCT; b += NWARP) {
+    double v = 0.0;
+#pragma unroll
+    for (int q = 0; q < NT / 32; ++q) v += (double)Hc[b * NT + lane + 32 * q];
+    v = warp_sum_d(v);
+    if (lane == 0) S.oct[b] = v;
+  }
+  csync();
+  double Se = 0.0, Ee = 0.0;
+  for (int b = 0; b <= NOCT; ++b) {
+    Se += S.oct[b];
+    Ee += S.oct[b] * oct_d(b);
+  }
+  const double Th = thr * Se;
+  const double es = est_err(Se, Ee, m_y, 36, V);
+  const double rnd = 2.0 * ((4.0 * V + 16.0) * U53 * Se);
+  int bc = -1;                     // crossing octave; -1: top_p > 1, everything is kept
+  double cum = 0.0, Eb = 0.0;      // estimated mass (and |d| mass) of the octaves below it
+  if (thr > 0.0) {
+    for (int b = NOCT; b >= 0; --b) {
+      if (cum + S.oct[b] > Th) { bc = b; break; }
+      cum += S.oct[b];
+      Eb += S.oct[b] * oct_d(b);
+    }
+    if (bc < 0 || bc == NOCT) return ROW_GENERAL;
+  }
+
+  // ---- list job: octaves 0..bl, the deeper ones an estimated tail ----
+  if (thr > 0.0 && !forced) {
+    int bl = bc;
+    for (;;) {
+      double tl = 0.0, et = 0.0;
+      for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
+      if (tl + 2.0 * est_err(tl, et, m_y, 36, V) + thr * es + rnd < Th) break;
+      if (++bl >= NOCT) break;
+    }
+    double nb = 0.0;                              // count bound: p~ > 2^-(b+1) in octave b
+    for (int b = 0; b <= bl && b < NOCT; ++b) nb += S.oct[b] * exp2((double)(b + 1));
+    if (bl < NOCT && nb <= 2.0 * LCAP) {
+      unsigned long long mask = 0ull;
+      float xmx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < OWN; ++j) {
+        if ((est_rank(__expf(dest(rc, x[j]))) >> 8) <= bl) mask |= 1ull << j;
+        else xmx = fmaxf(xmx, x[j]);
+      }
+      int ng;
+      const int wpos = block_exscan_i32(__popcll(mask), S.redi, &ng);
+      if (ng <= LCAP) {
+        write_keys(a.lkeys + (size_t)row * LCAP, rc, x, mask, wpos);
+        const float xm = block_reduce(xmx, MaxF(), S.redf);
+        if (tid == 0) {
+          RowJob& J = a.jobs[row];
+          double tl = 0.0, et = 0.0;
+          for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
+          fill_job(J, rc, JOB_K0, ng, 0);
+          J.tail = tl;
+          J.tail_err = est_err(tl, et, m_y, 36, V);
+          J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
+        }
+        if (a.out_logits) write_row(a, rc, x, true, 0u, 0ull);
+        return ROW_DONE;
+      }
+    }
+  }
+
+  // ---- the row kernel finishes the row ----
+  // survivor mass of this thread's elements in the octaves above the crossing one
+  float hi = 0.0f;
+  {
+    const int btop = bc < 0 ? NOCT + 1 : bc;
+    for (int b = 0; b < btop; ++b) hi += Hc[b * NT + tid];
+  }
+  csync();                                        // the columns are read before the area is reused
+  unsigned long long kst = 0ull;
+  int fc = -1;                                    // crossing rank: octave * 256 + sub-bin
+  double Ed = Ee;                                 // |d| mass bound of the survivors
+  if (bc >= 0) {
+    float* SBm = reinterpret_cast<float*>(work);
+    unsigned* SBc = reinterpret_cast<unsigned*>(work + 1024);
+    unsigned long long* ws = reinterpret_cast<unsigned long long*>(work + 2048);
+    double* wpv = reinterpret_cast<double*>(work + 2048 + BIG_SORT * 8);
+    float* acc2 = reinterpret_cast<float*>(work + 2048 + BIG_SORT * 16);
+    Cand* cand = reinterpret_cast<Cand*>(work + 5 * 1024);
+    SBm[tid] = 0.0f;
+    SBc[tid] = 0u;
+    acc2[tid] = 0.0f;
+    if (tid == 0) { S.slot = 0; S.slot2 = 0; }
+    csync();
+    // sub-bins of the crossing octave and its elements
+    float xdeep = -INFINITY, xhigh = INFINITY;
+#pragma unroll
+    for (int j = 0; j < OWN; ++j) {
+      const float p = __expf(dest(rc, x[j]));
+      const int rk = est_rank(p);
+      const int ob = rk >> 8;
+      if (ob == bc) {
+        atomicAdd(&SBm[rk & 255], p);
+        atomicAdd(&SBc[rk & 255], 1u);
+        const int sl = atomicAdd(&S.slot, 1);
+        if (sl < CAND_CAP) cand[sl] = Cand{x[j], tid * OWN + j};
+      } else if (ob > bc) {
+        xdeep = fmaxf(xdeep, x[j]);
+      } else {
+        xhigh = fminf(xhigh, x[j]);
+      }
+    }
+    csync();
+    if (warp == 0)
+      warp_find_bin_n<8, float>([&](int jb) { return SBm[255 - jb]; }, (float)(Th - cum), &S.c, &S.fbefore);
+    csync();
+    const int ncand = S.slot;
+    if (S.c >= 256 || ncand > CAND_CAP) return ROW_GENERAL;
+    const int c2 = 255 - S.c;
+    const int nc = (int)SBc[c2];
+    if (nc > BIG_SORT || nc == 0) return ROW_GENERAL;
+    fc = bc * 256 + c2;
+    const double before = cum + (double)S.fbefore;
+    // the crossing sub-bin with exact keys; the nearest values outside it
+    float xb = xdeep, xa = xhigh;
+    const int ishift = rc.i0 - tid * OWN;         // element index = position + ishift
+    for (int e = tid; e < ncand; e += NT) {
+      const Cand cd = cand[e];
+      const int sub = est_rank(__expf(dest(rc, cd.x))) & 255;
+      if (sub == c2) {
+        const int sl = atomicAdd(&S.slot2, 1);
+        if (sl < BIG_SORT) ws[sl] = ckey(yex(rc, cd.x), cd.pos + ishift);
+      } else if (sub > c2) {
+        xb = fmaxf(xb, cd.x);
+      } else {
+        xa = fminf(xa, cd.x);
+      }
+    }
+    xb = block_reduce(xb, MaxF(), S.redf);
+    xa = block_reduce(xa, MinF(), S.redf);
     if (warp == 0) {
       warp_sort(ws, nc);
-      unsigned long long prev, cur;
-      const double qs = a.qscale;
-      const float my = m_y;
-      const int e = warp_prefix_find(
-          ws, nc, S.mbefore,
-          [qs, my](unsigned long long key) { return qfix(prob(fkey_inv((unsigned)(key >> 32)), my), qs); },
-          [Tq](unsigned long long A) { return (double)A > Tq; }, &prev, &cur);
-      const bool ok = e < nc && (double)prev <= Tq - bq && (double)cur > Tq + bq;
-      if (lane == 0) { S.defer = ok ? 0 : 1; S.kp = ok ? ws[e] : 0ull; }
+      const unsigned klo = (unsigned)(ws[0] >> 32), khi = (unsigned)(ws[nc - 1] >> 32);
+      // values outside the sub-bin must order strictly outside it
+      const bool ok = (xb == -INFINITY || fkey(yex(rc, xb)) < klo) && (xa == INFINITY || fkey(yex(rc, xa)) > khi);
+      for (int e = lane; e < nc; e += 32) wpv[e] = prob(fkey_inv((unsigned)(ws[e] >> 32)), m_y);
+      __syncwarp();
+      if (lane == 0) {
+        // error bounds: the estimated mass below the crossing and the estimated total
+        const double eb = est_err(before, Eb + (double)S.fbefore * oct_d(bc), m_y, 36 + ncand, V);
+        const double bd = eb + thr * est_err(Se, Ee, m_y, 36 + ncand, V) + rnd;
+        int e = -1;
+        double prev = 0.0, curv = 0.0, run = before;
+        for (int t = 0; t < nc; ++t) {
+          if (run + wpv[t] > Th) { e = t; prev = run; curv = run + wpv[t]; break; }
+          run += wpv[t];
+        }
+        S.defer = ok ? 0 : 1;
+        S.done = (ok && e >= 0 && prev <= Th - bd && curv > Th + bd && !forced) ? 1 : 0;
+        S.kp = e >= 0 ? ws[e] : KEY_MAX;
+      }
     }
-    __syncthreads();
-    if (S.defer) return false;
-    Kp = S.kp;
-  }
-  const unsigned long long ks = Kp < Kk ? Kp : Kk;
-  if (tid == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_BINNED], 1ull);
-
-  // ---- draw over the survivors of top-p, in index order ----
-  int tok = 0;
-  if (u53 != 0ull) {
-    int cl = 0;
-    each([&](float y, int i) { cl += ckey(y, i) >= ks ? 1 : 0; });
-    const int nk = block_reduce(cl, SumI(), S.redi);
-    if (nk <= F_SORT && !force_bins) {
-      if (tid == 0) S.slot = 0;
-      __syncthreads();
-      each([&](float y, int i) {
-        if (ckey(y, i) >= ks) ws[atomicAdd(&S.slot, 1)] = ((unsigned long long)i << 32) | fkey(y);
-      });
-      __syncthreads();
-      if (warp == 0) {
-        warp_sort(ws, nk);
-        const double qs = a.qscale;
-        const float my = m_y;
-        auto qd = [qs, my](unsigned long long key) { return qfix(prob(fkey_inv((unsigned)key), my), qs); };
-        unsigned long long S2 = 0;
-        for (int e = lane; e < nk; e += 32) S2 += qd(ws[e]);
+    csync();
+    if (S.defer) return ROW_GENERAL;
+    if (!S.done) {
+      // exact sums over the row decide among the sub-bin's elements
+      double se = 0.0, be = 0.0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) S2 += __shfl_xor_sync(FULL, S2, o);
-        const double S2d = (double)S2, rq = __dmul_rn(u, S2d), bq2 = band_q(nk, S2d);
-        unsigned long long prev, cur;
-        const int e = warp_prefix_find(ws, nk, 0ull, qd, [rq](unsigned long long A) { return (double)A >= rq; },
-                                       &prev, &cur);
-        int t;
-        if (S2 > 0 && e < nk && (double)prev < rq - bq2 && (double)cur > rq + bq2) t = (int)(ws[e] >> 32);
-        else t = nk == 0 ? 0 : warp_draw_exact(ws, nk, m_y, u, V, pv);
-        if (lane == 0) S.tok = t;
+      for (int j = 0; j < OWN; ++j) {
+        const double p = prob(yex(rc, x[j]), m_y);   // 0 for -inf
+        se += p;
+        if (est_rank(__expf(dest(rc, x[j]))) > fc) be += p;
       }
-      __syncthreads();
-      tok = S.tok;
-    } else {
-      for (int j = tid; j < NB_I; j += NT) mass[j] = 0ull;
-      __syncthreads();
-      const int ish = a.ishift;
-      each([&](float y, int i) {
-        if (ckey(y, i) >= ks) atomicAdd(&mass[i >> ish], qfix(prob(y, m_y), a.qscale));
-      });
-      __syncthreads();
-      const unsigned long long SQ2 = block_reduce(mass[tid], SumU64(), S.red64);
-      const double SQ2d = (double)SQ2, rq = __dmul_rn(u, SQ2d), bq2 = band_q(nk, SQ2d);
-      const unsigned long long target = (unsigned long long)ceil(rq);
-      if (warp == 0)
-        warp_find_bin_n<NB_I / 32, unsigned long long>([&](int j) { return mass[j]; }, target, false, &S.c,
-                                                       &S.mbefore);
-      if (tid == 0) S.slot = 0;
-      __syncthreads();
-      const int ib = S.c;
-      if (ib >= NB_I) return false;
-      each([&](float y, int i) {
-        if (ckey(y, i) >= ks && (i >> ish) == ib) ws[atomicAdd(&S.slot, 1)] = ((unsigned long long)i << 32) | fkey(y);
-      });
-      __syncthreads();
-      const int nb = S.slot;
-      if (warp == 0) {
-        warp_sort(ws, nb);
-        unsigned long long prev, cur;
-        const double qs = a.qscale;
-        const float my = m_y;
-        const int e = warp_prefix_find(
-            ws, nb, S.mbefore, [qs, my](unsigned long long key) { return qfix(prob(fkey_inv((unsigned)key), my), qs); },
-            [rq](unsigned long long A) { return (double)A >= rq; }, &prev, &cur);
-        const bool ok = SQ2 > 0 && e < nb && (double)prev < rq - bq2 && (double)cur > rq + bq2;
-        if (lane == 0) { S.defer = ok ? 0 : 1; S.tok = ok ? (int)(ws[e] >> 32) : 0; }
+      se = block_reduce(se, SumD(), S.redd);
+      be = block_reduce(be, SumD(), S.redd);
+      if (tid == 0) {
+        const double Te = thr * se, bde = 2.0 * ((4.0 * V + 16.0) * U53 * se);
+        int e = -1;
+        double prev = 0.0, curv = 0.0, run = be;
+        for (int t = 0; t < nc; ++t) {
+          if (run + wpv[t] > Te) { e = t; prev = run; curv = run + wpv[t]; break; }
+          run += wpv[t];
+        }
+        S.defer = (e >= 0 && prev <= Te - bde && curv > Te + bde) ? 0 : 1;
+        S.kp = e >= 0 ? ws[e] : KEY_MAX;
+        atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
       }
-      __syncthreads();
-      if (S.defer) return false;
-      tok = S.tok;
-      if (tid == 0) atomicAdd(&a.counters[C4S_CNT_DRAW_ROWPASS], 1ull);
+      csync();
+      if (S.defer) return ROW_GENERAL;
     }
+    kst = S.kp;
+    // survivors inside the crossing octave, added to their owners' masses
+    for (int e = tid; e < ncand; e += NT) {
+      const Cand cd = cand[e];
+      const float p = __expf(dest(rc, cd.x));
+      const int sub = est_rank(p) & 255;
+      if (sub < c2 || (sub == c2 && ckey(yex(rc, cd.x), cd.pos + ishift) >= kst)) atomicAdd(&acc2[cd.pos / OWN], p);
+    }
+    csync();
+    hi += acc2[tid];
+    Ed = 0.0;
+    for (int b = 0; b <= bc; ++b) Ed += S.oct[b] * oct_d(b);
+    if (tid == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_BINNED], 1ull);
+  }
+
+  // ---- the draw: index-order prefix over per-thread survivor masses ----
+  auto survives = [&](float xv, int i, float p) {
+    if (fc < 0) return true;
+    const int rk = est_rank(p);
+    return rk < fc || (rk == fc && ckey(yex(rc, xv), i) >= kst);
+  };
+  int tok = 0;
+  if (rc.u53 != 0ull) {
+    bool done = false;
+    for (int pass = forced ? 1 : 0; pass < 2 && !done; ++pass) {
+      const bool exact = pass == 1;
+      double loc = (double)hi;
+      if (exact) {
+        loc = 0.0;
+#pragma unroll
+        for (int j = 0; j < OWN; ++j)
+          if (survives(x[j], rc.i0 + j, __expf(dest(rc, x[j])))) loc += prob(yex(rc, x[j]), m_y);
+      }
+      if (tid == 0) S.tok = -1;
+      double Sk;
+      const double base = block_exscan_f64(loc, S.redd, &Sk);
+      // per-thread masses: <= 36-term column sums, <= 25 of them, <= 36 atomics
+      const double Ek = exact ? 0.0 : est_err(Sk, Ed, m_y, 97, V);
+      const double rq = rc.u * Sk;
+      const double bd = 2.0 * Ek + 2.0 * ((4.0 * V + 16.0) * U53 * Sk);
+      if (base < rq && base + loc >= rq) {
+        // the crossing thread sums its own survivors in index order
+        double run = 0.0;
+        float runf = 0.0f;
+        int found = -1;
+        double fprev = 0.0, fcur = 0.0;
+#pragma unroll
+        for (int j = 0; j < OWN; ++j) {
+          if (found < 0) {
+            const float p = __expf(dest(rc, x[j]));
+            if (x[j] > -INFINITY && survives(x[j], rc.i0 + j, p)) {
+              double bef, aft;
+              if (exact) { bef = run; run += prob(yex(rc, x[j]), m_y); aft = run; }
+              else { bef = (double)runf; runf += p; aft = (double)runf; }
+              if (base + aft >= rq) { found = rc.i0 + j; fprev = base + bef; fcur = base + aft; }
+            }
+          }
+        }
+        if (found >= 0) { S.tok = found; S.d1 = fprev; S.d2 = fcur; }
+      }
+      csync();
+      const bool ok = Sk > 0.0 && S.tok >= 0 && S.d1 < rq - bd && S.d2 > rq + bd;
+      const int t = S.tok;
+      csync();
+      if (ok) { tok = t; done = true; }
+      else if (!exact && tid == 0) atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
+    }
+    if (!done) return ROW_GENERAL;
   }
   if (tid == 0) {
     a.out_ids[row] = tok;
-    a.rng[row] = xs;
-    S.kp = ks;
+    a.rng[row] = rc.xs;
+    a.jobs[row].kind = JOB_NONE;
+    atomicAdd(&a.counters[C4S_CNT_DRAW_ROWPASS], 1ull);
   }
-  __syncthreads();
-  return true;
+  if (a.out_logits) write_row(a, rc, x, true, 0u, kst);
+  csync();
+  return ROW_DONE;
 }
 
-// Warp-level exclusive/inclusive prefix over ws[0..n) (blocked, 4 per lane,
-// n <= 128) of double values val(key), starting at `before`; finds the first
-// entry whose inclusive prefix satisfies pred. Whole warp must call.
-template <typename Val, typename Pred>
-__device__ __forceinline__ int warp_prefix_find_d(const unsigned long long* ws, int n, double before, Val val,
-                                                  Pred pred, double* prev_out, double* cur_out) {
-  const int lane = threadIdx.x & 31;
-  double q[4];
-  double s = 0.0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    q[j] = e < n ? val(ws[e]) : 0.0;
-    s += q[j];
-  }
-  double incl = s;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double y = __shfl_up_sync(FULL, incl, o);
-    if (lane >= o) incl += y;
-  }
-  double run = before + (incl - s);
-  int found = n;
-  double pv_ = 0.0, cv = 0.0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    if (found == n && e < n && pred(run + q[j])) { found = e; pv_ = run; cv = run + q[j]; }
-    run += q[j];
-  }
-  const unsigned bal = __ballot_sync(FULL, found < n);
-  if (bal == 0) {
-    *prev_out = __shfl_sync(FULL, run, 31);
-    *cur_out = *prev_out;
-    return n;
-  }
-  const int L = __ffs(bal) - 1;
-  *prev_out = __shfl_sync(FULL, pv_, L);
-  *cur_out = __shfl_sync(FULL, cv, L);
-  return __shfl_sync(FULL, found, L);
-}
-
-// ---------------------------------------------------------------------------
-// Row passes: thread t owns the 36 contiguous buffer positions [36t, 36t+36)
-// (element index = position - shift), read as 9 aligned float4 (conflict-free
-// in shared memory). f(x, i) is called in increasing i.
-// ---------------------------------------------------------------------------
-constexpr int OWN = 36;
-static_assert(OWN * NT >= F_MAXV + 3, "the ownership blocks cover every row position");
-
-template <typename F>
-__device__ __forceinline__ void row_pass(const float* rowbuf, int shift, int V, F&& f) {
-  const int p0 = threadIdx.x * OWN;
-#pragma unroll
-  for (int qq = 0; qq < OWN / 4; ++qq) {
-    const int pos = p0 + 4 * qq;
-    if (pos < V + shift) {
-      const float4 v = *reinterpret_cast<const float4*>(rowbuf + pos);
-      const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int i = pos + r - shift;
-        if ((unsigned)i < (unsigned)V) f(vv[r], i);
-      }
-    }
-  }
-}
-
-// fl(x / T) (IEEE float division, sampling.cpp:16) from the double product
-// x * RN(1/T): its error is below one double ulp, so rounding it to float
-// gives the correctly rounded quotient unless it lies within a few double
-// ulps of a float rounding midpoint (or outside the normal range); those
-// cases take the hardware division.
-__device__ __forceinline__ float div_exact(float x, float T, double rTd) {
-  const double q = __dmul_rn((double)x, rTd);
-  const unsigned low = (unsigned)((unsigned long long)__double_as_longlong(q) & 0x1fffffffull);
-  const double aq = fabs(q);
-  if (!(aq >= 1.0e-30 && aq <= 1.0e30) || (low - 0x0ffffffcu) <= 8u) return __fdiv_rn(x, T);
-  return __double2float_rn(q);
-}
-
-// Relative error bound of __expf(d) in units of 2^-23 (CUDA's documented
-// maximum ulp error of __expf is 2 + floor(|1.16 d|)).
-__device__ __forceinline__ float expf_ulps(float d) { return 2.0f + 1.16f * fabsf(d); }
-constexpr double ULP_F = 1.1920928955078125e-07 * 1.02;   // 2^-23, with 2% margin
-
-// ---------------------------------------------------------------------------
-// One staged, penalised row through the fast path. Returns false to defer
-// the row to the general path (nothing has been written for it then).
-// ---------------------------------------------------------------------------
-__device__ bool fast_row4(const Args& a, int row, const MetaSlot& M, const float* rowbuf, int shift, unsigned* cnt,
-                          unsigned long long* mass, unsigned char* un, unsigned long long* ws, Shared& S) {
+// One sampled or greedy row whose penalised elements are in x (this thread's
+// positions; `shift` is the row's misalignment in elements).
+__device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& M, const float (&x)[OWN], int shift,
+                                        unsigned char* work, Shared& S) {
   const int V = a.V;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int i0 = tid * OWN - shift;
   const c4s_row_params P = M.P;
-  unsigned long long* lkey = reinterpret_cast<unsigned long long*>(un);
-  double* pv = reinterpret_cast<double*>(un + LIST_CAP * 8);
+  const int k = P.top_k;
+  const bool do_k = k > 0 && k < V;
+  // top-k above 64: the two largest of each thread seed the list
+  const bool two = !P.greedy && do_k && k > 64;
 
-  // ---- pass 1: row max, thread max, first index of the thread max --------------
-  float tm = -INFINITY;
-  int ti = 0x7fffffff;
-  row_pass(rowbuf, shift, V, [&](float x, int i) {
-    if (x > tm) { tm = x; ti = i; }
-  });
+  // ---- row max and per-thread maxima ----
+  float tm = -INFINITY, t2 = -INFINITY;
+  if (two) {
+#pragma unroll
+    for (int j = 0; j < OWN; ++j) {
+      t2 = fmaxf(t2, fminf(tm, x[j]));
+      tm = fmaxf(tm, x[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < OWN; ++j) tm = fmaxf(tm, x[j]);
+  }
   {
     const unsigned km = __reduce_max_sync(FULL, fkey(tm));
     if (lane == 0) S.redu[warp] = km;
   }
-  if (tid == 0) { S.slot = 0; S.slot2 = 0; }
-  __syncthreads();
+  csync();
   unsigned kall = S.redu[0];
 #pragma unroll
   for (int w = 1; w < NWARP; ++w) kall = kall > S.redu[w] ? kall : S.redu[w];
   const float m_x = fkey_inv(kall);
-  __syncthreads();
+  csync();
 
-  // ---- greedy: first index of the max (all -inf: index 0) ----------------------
+  RowCtx rc;
+  rc.row = row; rc.V = V; rc.i0 = i0;
+  rc.T = P.temperature;
+  rc.do_t = !(rc.T == 1.0f || rc.T <= 0.0f);
+
+  // ---- greedy: first index of the max (sampling.cpp:73-76) ----
   if (P.greedy) {
-    unsigned cand = (tm == m_x && ti != 0x7fffffff) ? (unsigned)ti : 0xffffffffu;
+    unsigned cand = 0xffffffffu;
+    if (m_x > -INFINITY && tm == m_x) {
+#pragma unroll
+      for (int j = 0; j < OWN; ++j)
+        if (x[j] == m_x && (unsigned)(i0 + j) < cand) cand = (unsigned)(i0 + j);
+    }
     cand = __reduce_min_sync(FULL, cand);
     if (lane == 0) S.redu[warp] = cand;
-    __syncthreads();
+    csync();
     if (tid == 0) {
       unsigned b = S.redu[0];
       for (int w = 1; w < NWARP; ++w) b = S.redu[w] < b ? S.redu[w] : b;
       a.out_ids[row] = b == 0xffffffffu ? 0 : (int)b;
+      a.jobs[row].kind = JOB_NONE;
     }
-    if (a.out_logits) {
-      float* o = a.out_logits + (long long)row * a.out_ld;
-      row_pass(rowbuf, shift, V, [&](float x, int i) { o[i] = x; });
-    }
-    return true;
+    if (a.out_logits) write_row(a, rc, x, false, 0u, 0ull);
+    csync();
+    return ROW_DONE;
   }
 
-  // ---- sample rows: preconditions of the fast path --------------------------------
-  const float T = P.temperature;
-  const bool do_t = !(T == 1.0f || T <= 0.0f);
-  if (!(m_x > -INFINITY && m_x < INFINITY)) return false;
-  const float m_y = do_t ? __fdiv_rn(m_x, T) : m_x;
-  if (!(fabsf(m_y) < 262144.0f)) return false;
-  if (P.min_tokens_to_keep > 1) return false;
-  if (a.debug & C4S_DEBUG_FORCE_EXACT) return false;
-  const bool force_bins = (a.debug & C4S_DEBUG_FORCE_BINS) != 0;
-  const int k = P.top_k;
-  const bool do_k = k > 0 && k < V;
-  // warps whose 32 lanes all own row positions: their thread maxima bound top-k
+  // ---- sampled rows: preconditions ----
+  if (!(m_x > -INFINITY && m_x < INFINITY)) return ROW_GENERAL;
+  rc.m_x = m_x;
+  rc.m_y = rc.do_t ? __fdiv_rn(m_x, rc.T) : m_x;
+  rc.rT = rc.do_t ? __frcp_rn(rc.T) : 1.0f;
+  if (!(fabsf(rc.m_y) < 262144.0f)) return ROW_GENERAL;
+  if (P.min_tokens_to_keep != 1) return ROW_GENERAL;
+  if (a.debug & C4S_DEBUG_FORCE_EXACT) return ROW_GENERAL;
+  const bool forced = (a.debug & C4S_DEBUG_FORCE_BINS) != 0;
+  rc.thr = __dsub_rn(1.0, (double)P.top_p);
+  {
+    unsigned long long xs = M.rng;
+    xs ^= xs << 13; xs ^= xs >> 7; xs ^= xs << 17;
+    rc.xs = xs;
+    rc.u53 = xs >> 11;
+    rc.u = (double)rc.u53 * 1.1102230246251565e-16;   // (x>>11) / 2^53, exact
+  }
+  if (!do_k) {
+    if (rc.thr == 0.0) return ROW_GENERAL;
+    // the copy keeps x itself in registers: only xc's address reaches the call
+    float xc[OWN];
+#pragma unroll
+    for (int j = 0; j < OWN; ++j) xc[j] = x[j];
+    return k0_row(a, rc, xc, work, S, forced);
+  }
+
+  // ---- top-k rows: candidates >= the maxima threshold form the list ----
+  // warps whose 32 lanes all own row positions: their maxima seed the list
   const int wfull = min(NWARP, ((V + shift + OWN - 1) / OWN) >> 5);
-  if (do_k && (wfull == 0 || k > wfull * 32)) return false;
-  const double thr = __dsub_rn(1.0, (double)P.top_p);
-  const int mk = P.min_tokens_to_keep;
-  unsigned long long xs = M.rng;
-  xs ^= xs << 13; xs ^= xs >> 7; xs ^= xs << 17;
-  const unsigned long long u53 = xs >> 11;
-  const double u = (double)u53 * 1.1102230246251565e-16;
-  const double rTd = do_t ? 1.0 / (double)T : 1.0;
-  auto yex = [&](float x) { return do_t ? div_exact(x, T, rTd) : x; };   // sampling.cpp:16
-
-  float thresh_y = -INFINITY;
-  if (do_k) {
-    // ---- top-k: threshold from the thread maxima, candidates gathered ------------
-    // Each full warp has >= kw thread maxima >= its kw-th largest, so at least
-    // wfull*kw >= k elements are >= tau, the least of those over the full warps.
-    const int kw = (k + wfull - 1) / wfull;
-    unsigned key = fkey(tm);
+  if (wfull == 0 || k > wfull * (two ? 64 : 32)) return ROW_GENERAL;
+  const int kw = (k + wfull - 1) / wfull;
+  const unsigned wthr = two ? warp_kth_largest64(fkey(tm), fkey(t2), kw) : warp_kth_largest32(fkey(tm), kw);
+  // each full warp has >= kw elements >= its wthr, so >= k elements are >= tau
+  if (lane == 0) S.redu[warp] = wthr;
+  csync();
+  unsigned tkey = S.redu[0];
+  for (int w = 1; w < wfull; ++w) tkey = S.redu[w] < tkey ? S.redu[w] : tkey;
+  const float tau = fkey_inv(tkey);
+  // fl(x/T) merges x only with values at most |x| 2^-23 below it: lowering tau
+  // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
+  const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;
+  if (!(tau_lo > -INFINITY)) return ROW_GENERAL;
+  unsigned long long mask = 0ull;
 #pragma unroll
-    for (int kk = 2; kk <= 32; kk <<= 1) {
-#pragma unroll
-      for (int jj = kk >> 1; jj > 0; jj >>= 1) {
-        const unsigned o = __shfl_xor_sync(FULL, key, jj);
-        const bool keep_min = (((lane & jj) == 0) == ((lane & kk) == 0));
-        key = keep_min ? (o < key ? o : key) : (o > key ? o : key);
-      }
-    }
-    const unsigned wthr = __shfl_sync(FULL, key, 32 - kw);      // ascending: kw-th largest
-    if (lane == 0) S.redu[warp] = wthr;
-    __syncthreads();
-    unsigned tkey = S.redu[0];
-    for (int w = 1; w < wfull; ++w) tkey = S.redu[w] < tkey ? S.redu[w] : tkey;
-    const float tau = fkey_inv(tkey);
-    const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;   // below tau by 2^-18 relative
-    int cnt_t = 0;
-    row_pass(rowbuf, shift, V, [&](float x, int) { cnt_t += x >= tau_lo ? 1 : 0; });
-    int ng;
-    int wpos = block_exscan_i32(cnt_t, S.redi, &ng);
-    if (ng > LIST_CAP) return false;
-    row_pass(rowbuf, shift, V, [&](float x, int i) {
-      if (x >= tau_lo) lkey[wpos++] = ckey(yex(x), i);
-    });
-    __syncthreads();
-    int ns;
-    if (ng <= F_SORT) {
-      if (warp == 0) {
-        for (int e = lane; e < ng; e += 32) ws[e] = lkey[e];
-        __syncwarp();
-        warp_sort(ws, ng);
-        const unsigned tk2 = (unsigned)(ws[ng - k] >> 32);
-        int below = 0;
-        for (int e = lane; e < ng; e += 32) below += ((unsigned)(ws[e] >> 32) < tk2) ? 1 : 0;
-        below = __reduce_add_sync(FULL, below);
-        const int nsv = ng - below;
-        unsigned long long t4[F_SORT / 32];
-#pragma unroll
-        for (int q = 0; q < F_SORT / 32; ++q) {
-          const int e = below + lane + 32 * q;
-          t4[q] = e < ng ? ws[e] : KEY_MAX;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int q = 0; q < F_SORT / 32; ++q) {
-          const int e = lane + 32 * q;
-          if (e < nsv) { ws[e] = t4[q]; lkey[e] = t4[q]; }
-        }
-        __syncwarp();
-        int done = 0;
-        if (!force_bins) {
-          unsigned long long K;
-          const int t = warp_small_row(ws, nsv, true, m_y, thr, mk, u53, u, V, a.qscale, pv, &K);
-          if (lane == 0) { S.kp = K; a.out_ids[row] = t; a.rng[row] = xs; }
-          done = 1;
-        }
-        if (lane == 0) { S.thresh_key = tk2; S.ns = nsv; S.done = done; }
-      }
-      __syncthreads();
-      thresh_y = fkey_inv(S.thresh_key);
-      ns = S.ns;
-      if (!S.done && !list_topp_draw(a, row, ns, m_y, thr, mk, u53, u, xs, force_bins, lkey, pv, ws, mass, S))
-        return false;
-    } else {
-      // count the candidates per value bin, sort the bin of the k-th largest
-      for (int jb = tid; jb < NB_Y; jb += NT) cnt[jb] = 0u;
-      __syncthreads();
-      for (int e = tid; e < ng; e += NT) atomicAdd(&cnt[ybin(m_y, fkey_inv((unsigned)(lkey[e] >> 32)))], 1u);
-      __syncthreads();
-      if (warp == 0)
-        warp_find_bin_n<NB_Y / 32, unsigned>([&](int jb) { return cnt[jb]; }, (unsigned)k, false, &S.c,
-                                             &S.cbefore);
-      if (tid == 0) S.slot = 0;
-      __syncthreads();
-      const int cb = S.c;
-      if (cb >= NB_Y) return false;
-      const int nb = (int)cnt[cb];
-      if (nb > F_SORT) return false;
-      for (int e = tid; e < ng; e += NT) {
-        const unsigned long long kk2 = lkey[e];
-        if (ybin(m_y, fkey_inv((unsigned)(kk2 >> 32))) == cb) ws[atomicAdd(&S.slot, 1)] = kk2;
-      }
-      __syncthreads();
-      if (warp == 0) {
-        warp_sort(ws, nb);
-        const int kk = k - (int)S.cbefore;                 // 1 <= kk <= nb
-        if (lane == 0) S.thresh_key = (unsigned)(ws[nb - kk] >> 32);
-      }
-      __syncthreads();
-      const unsigned tk2 = S.thresh_key;
-      unsigned long long mine[LIST_CAP / NT];
-      int c2 = 0;
-#pragma unroll
-      for (int q = 0; q < LIST_CAP / NT; ++q) {
-        const int e = tid + q * NT;
-        mine[q] = (e < ng && (unsigned)(lkey[e] >> 32) >= tk2) ? lkey[e] : KEY_MAX;
-        c2 += mine[q] != KEY_MAX ? 1 : 0;
-      }
-      int nsv;
-      int wp = block_exscan_i32(c2, S.redi, &nsv);     // its barriers order the reads before the writes
-#pragma unroll
-      for (int q = 0; q < LIST_CAP / NT; ++q)
-        if (mine[q] != KEY_MAX) lkey[wp++] = mine[q];
-      __syncthreads();
-      thresh_y = fkey_inv(tk2);
-      ns = nsv;
-      if (!list_topp_draw(a, row, ns, m_y, thr, mk, u53, u, xs, force_bins, lkey, pv, ws, mass, S)) return false;
-    }
-  } else {
-    // ---- no top-k: float estimates of exact values --------------------------------
-    auto coarse = [&](float d) { return min(NB1 - 1, (int)(fmaxf(-d, 0.0f) * L1SCALE)); };
-    auto fine = [&](float d, float lo1) { return min(NB2 - 1, max(0, (int)((-d - lo1) * L2SCALE))); };
-    float* H = reinterpret_cast<float*>(un);
-#pragma unroll
-    for (int b = 0; b < NB1; ++b) H[b * NT + tid] = 0.0f;
-    double st = 0.0, eb = 0.0;
-    float dmin = 0.0f;
-    int nf = 0, kim = -1;
-    row_pass(rowbuf, shift, V, [&](float x, int i) {
-      if (x > -INFINITY) {
-        const float y = yex(x);
-        const float d = __fsub_rn(y, m_y);
-        const float p = __expf(d);
-        st += p;
-        eb += expf_ulps(d) * p;
-        ++nf;
-        dmin = fminf(dmin, d);
-        H[coarse(d) * NT + tid] += p;
-        if (y == m_y) kim = i;
-      }
-    });
-    const int nfa = block_reduce(nf, SumI(), S.redi);
-    if (nfa <= F_SORT && !force_bins) {
-      // few finite logits: exact list in index order
-      int cf = nf;
-      int wpos = block_exscan_i32(cf, S.redi, &cf);
-      row_pass(rowbuf, shift, V, [&](float x, int i) {
-        if (x > -INFINITY) lkey[wpos++] = ckey(yex(x), i);
-      });
-      __syncthreads();
-      if (!list_topp_draw(a, row, nfa, m_y, thr, mk, u53, u, xs, false, lkey, pv, ws, mass, S)) return false;
-    } else {
-      const int kima = block_reduce(kim, MaxI(), S.redi);
-      const double Sh = block_reduce(st, SumD(), S.redd);
-      const double Eh = block_reduce(eb, SumD(), S.redd) * ULP_F + 1e-30 * nfa;
-      const float dmn = block_reduce(dmin, MinF(), S.redf);
-      for (int bb = warp; bb < NB1; bb += NWARP) {
-        float v = 0.0f;
-#pragma unroll
-        for (int q = 0; q < NT / 32; ++q) v += H[bb * NT + lane + 32 * q];
-        v = warp_sum_f(v);
-        if (lane == 0) S.l1[bb] = v;
-      }
-      __syncthreads();
-      const unsigned long long Kk = mk <= 0 ? KEY_MAX : ckey(m_y, kima);
-      unsigned long long Kp = 0ull;
-      int status = 0;                                     // 0 decided, 1 exact pass, 2 defer
-      int nc = 0;
-      // estimate error: each prefix and the total are within Eh of the exact
-      // sums of the same terms; the reference's own rounding adds ~n ulps
-      const double Th = thr * Sh;
-      const double band = 2.0 * Eh + 2.0 * (4.0 * nfa + 16.0) * U53 * Sh;
-      if (thr < 0.0) {
-        Kp = 0ull;                                        // p > 1: nothing removed
-      } else if (thr == 0.0) {
-        if (dmn > -700.0f) Kp = 0ull;                     // p == 1: no exp() can underflow to 0
-        else status = 2;
-      } else {
-        int c1 = -1;
-        double cum = 0.0;
-        for (int b = NB1 - 1; b >= 0; --b) {
-          if (cum + (double)S.l1[b] > Th) { c1 = b; break; }
-          cum += (double)S.l1[b];
-        }
-        if (c1 < 0) {
-          if (mk >= 1 && Sh - 1.0 <= Th - band) Kp = KEY_MAX;   // only the kept maximum survives
-          else status = 2;
-        } else if (c1 == NB1 - 1) {
-          status = 2;                                     // crossing in the far tail
-        } else {
-          // level 2: float bins inside the coarse bin (localisation only)
-          float* L2p = reinterpret_cast<float*>(cnt);
-          unsigned* L2n = reinterpret_cast<unsigned*>(mass);
-          for (int jb = tid; jb < NB2; jb += NT) { L2p[jb] = 0.0f; L2n[jb] = 0u; }
-          __syncthreads();
-          const float lo1 = 2.0f * (float)c1;
-          row_pass(rowbuf, shift, V, [&](float x, int) {
-            if (x > -INFINITY) {
-              const float d = __fsub_rn(yex(x), m_y);
-              if (coarse(d) == c1) {
-                const int f = fine(d, lo1);
-                atomicAdd(&L2p[f], __expf(d));
-                atomicAdd(&L2n[f], 1u);
-              }
-            }
-          });
-          __syncthreads();
-          if (warp == 0)
-            warp_find_bin_n<NB2 / 32, float>([&](int jb) { return L2p[NB2 - 1 - jb]; }, (float)(Th - cum),
-                                             true, &S.c, &S.fbefore);
-          __syncthreads();
-          const int jc = S.c;
-          if (jc >= NB2 || (int)L2n[NB2 - 1 - jc] > F_SORT) {
-            status = 2;
-          } else {
-            const int c2 = NB2 - 1 - jc;
-            // the crossing bin's elements (exact keys) and the estimated mass below it
-            double bl = 0.0;
-            row_pass(rowbuf, shift, V, [&](float x, int i) {
-              if (x > -INFINITY) {
-                const float y = yex(x);
-                const float d = __fsub_rn(y, m_y);
-                const int cb1 = coarse(d);
-                if (cb1 > c1) {
-                  bl += __expf(d);
-                } else if (cb1 == c1) {
-                  const int f = fine(d, lo1);
-                  if (f > c2) bl += __expf(d);
-                  else if (f == c2) {
-                    const int sl = atomicAdd(&S.slot2, 1);
-                    if (sl < F_SORT) ws[sl] = ckey(y, i);
-                  }
-                }
-              }
-            });
-            const double before = block_reduce(bl, SumD(), S.redd);
-            nc = min(S.slot2, F_SORT);
-            if (warp == 0) {
-              warp_sort(ws, nc);
-              const float my = m_y;
-              double prev, cur;
-              const int e = warp_prefix_find_d(
-                  ws, nc, before, [my](unsigned long long kq) { return prob(fkey_inv((unsigned)(kq >> 32)), my); },
-                  [Th](double A) { return A > Th; }, &prev, &cur);
-              const bool ok = e < nc && prev <= Th - band && cur > Th + band;
-              if (lane == 0) { S.kp = ok ? ws[e] : 0ull; S.defer = ok ? 0 : 1; }
-            }
-            __syncthreads();
-            if (S.defer) status = 1;
-            else Kp = S.kp;
-          }
-        }
-      }
-      if (status == 1) {
-        // exact double sums over the row decide among the candidates
-        const unsigned long long klo = ws[0];
-        double se = 0.0, be = 0.0;
-        row_pass(rowbuf, shift, V, [&](float x, int i) {
-          if (x > -INFINITY) {
-            const float y = yex(x);
-            const double p = prob(y, m_y);
-            se += p;
-            if (ckey(y, i) < klo) be += p;
-          }
-        });
-        se = block_reduce(se, SumD(), S.redd);
-        be = block_reduce(be, SumD(), S.redd);
-        if (warp == 0) {
-          const float my = m_y;
-          const double Te = thr * se, bqe = 2.0 * ((4.0 * nfa + 16.0) * U53 * se);
-          double prev, cur;
-          const int e = warp_prefix_find_d(
-              ws, nc, be, [my](unsigned long long kq) { return prob(fkey_inv((unsigned)(kq >> 32)), my); },
-              [Te](double A) { return A > Te; }, &prev, &cur);
-          const bool ok = e < nc && prev <= Te - bqe && cur > Te + bqe;
-          if (lane == 0) { S.kp = ok ? ws[e] : 0ull; S.defer = ok ? 0 : 1; }
-        }
-        __syncthreads();
-        if (S.defer) return false;
-        Kp = S.kp;
-        if (tid == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
-      } else if (status == 2) {
-        return false;
-      }
-      const unsigned long long ks = Kp < Kk ? Kp : Kk;
-      if (tid == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_BINNED], 1ull);
-
-      // ---- draw: index-order prefix of the estimates, exact pass on demand ----
-      int tok = 0;
-      if (u53 != 0ull && ks != KEY_MAX) {
-        for (int pass = 0; pass < 2; ++pass) {
-          const bool exact = pass == 1;
-          double loc = 0.0, el = 0.0;
-          int nl = 0;
-          row_pass(rowbuf, shift, V, [&](float x, int i) {
-            if (x > -INFINITY) {
-              const float y = yex(x);
-              if (ckey(y, i) >= ks) {
-                const float d = __fsub_rn(y, m_y);
-                if (exact) {
-                  loc += prob(y, m_y);
-                } else {
-                  const float p = __expf(d);
-                  loc += p;
-                  el += expf_ulps(d) * p;
-                }
-                ++nl;
-              }
-            }
-          });
-          if (tid == 0) S.tok = -1;
-          double Sk;
-          const double base = block_exscan_f64(loc, S.redd, &Sk);
-          const int nk = block_reduce(nl, SumI(), S.redi);
-          const double Ek = exact ? 0.0 : block_reduce(el, SumD(), S.redd) * ULP_F;
-          const double rq = u * Sk;
-          const double bd = 2.0 * Ek + 2.0 * (4.0 * nk + 16.0) * U53 * Sk;
-          if (Sk > 0.0 && base < rq && base + loc >= rq) {
-            double run = base;
-            int found = -1;
-            double fprev = 0.0, fcur = 0.0;
-            row_pass(rowbuf, shift, V, [&](float x, int i) {
-              if (found < 0 && x > -INFINITY) {
-                const float y = yex(x);
-                if (ckey(y, i) >= ks) {
-                  const double p = exact ? prob(y, m_y) : (double)__expf(__fsub_rn(y, m_y));
-                  if (run + p >= rq) { found = i; fprev = run; fcur = run + p; }
-                  run += p;
-                }
-              }
-            });
-            if (found >= 0) { S.tok = found; S.d1 = fprev; S.d2 = fcur; }
-          }
-          __syncthreads();
-          const bool ok = (Sk == 0.0) || (S.tok >= 0 && S.d1 < rq - bd && S.d2 > rq + bd);
-          const int t = (Sk == 0.0) ? 0 : S.tok;
-          __syncthreads();
-          if (ok) { tok = t; break; }
-          if (exact) return false;
-          if (tid == 0) atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
-        }
-      }
-      if (tid == 0) {
-        a.out_ids[row] = tok;
-        a.rng[row] = xs;
-        S.kp = ks;
-      }
-      __syncthreads();
-    }
+  for (int j = 0; j < OWN; ++j)
+    if (x[j] >= tau_lo) mask |= 1ull << j;
+  int ng;
+  const int wpos = block_exscan_i32(__popcll(mask), S.redi, &ng);   // its barriers also order S.redu
+  if (ng > LCAP) return ROW_GENERAL;
+  write_keys(a.lkeys + (size_t)row * LCAP, rc, x, mask, wpos);
+  if (tid == 0) {
+    RowJob& J = a.jobs[row];
+    fill_job(J, rc, JOB_TOPK, ng, k);
+    J.tail = 0.0;
+    J.tail_err = 0.0;
+    J.ykex = 0u;
   }
-
-  // ---- processed logits (on request) ------------------------------------------------
-  if (a.out_logits) {
-    const unsigned long long kst = S.kp;
-    float* o = a.out_logits + (long long)row * a.out_ld;
-    row_pass(rowbuf, shift, V, [&](float x, int i) {
-      const float y = yex(x);
-      const bool masked = (y < thresh_y) || (y > -INFINITY && ckey(y, i) < kst);
-      o[i] = masked ? -INFINITY : y;
-    });
-  }
-  return true;
+  if (a.out_logits) write_row(a, rc, x, true, 0u, 0ull);
+  return ROW_DONE;
 }
 
 // ---------------------------------------------------------------------------
-// The fast kernel: rows blockIdx.x, +gridDim.x, ...; metadata of the next
-// row by cp.async and its logits prefetched into L2 while the current row is
-// processed. Rows the fast path declines take the general path in place.
+// The row kernel: rows blockIdx.x, +gridDim.x, ... of the chunk. Each row is
+// staged into shared memory by one bulk-async copy (its <= 3-element unaligned
+// head and tail by plain loads held in registers), penalised there, and read
+// into registers; the buffer then takes the next row's copy at once (after
+// the work of a row without top-k, which uses it as scratch). The next row's
+// metadata arrives by cp.async.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NT, 4) fast_kernel(Args a) {
-  extern __shared__ __align__(16) unsigned char dsm[];
+struct Staged {
+  int shift, body;           // body: bulk-copied elements (0: nothing in flight)
+  int hpos;                  // buffer position of this thread's plain-loaded element (-1: none)
+  float hval;
+};
+__device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf, unsigned long long* bar) {
+  const unsigned long long ga = (unsigned long long)g;
+  int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);
+  if (head > V) head = V;
+  const int body = ((V - head) >> 2) << 2;
+  const int shift = (4 - head) & 3;
+  const int tid = threadIdx.x;
+  if (tid == 0 && body > 0) {
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, (unsigned)body * 4u);
+    bulk_g2s(rowbuf + shift + head, g + head, (unsigned)body * 4u, bar);
+  }
+  Staged st{shift, body, -1, 0.0f};
+  int i = -1;
+  if (tid < 4) i = tid < head ? tid : -1;
+  else if (tid < 8) i = head + body + (tid - 4) < V ? head + body + (tid - 4) : -1;
+  if (i >= 0) {
+    st.hpos = shift + i;
+    st.hval = __ldcs(g + i);
+  }
+  return st;
+}
+
+__global__ void __launch_bounds__(NT, 4) row_kernel(Args a) {
+  extern __shared__ __align__(16) unsigned char dsm[];   // the staged row, then scratch
   __shared__ Shared S;
+  __shared__ unsigned bm[(F_MAXV + 31) / 32 + 4];        // penalty de-duplication bitmap
+  __shared__ MetaSlot meta[2];
+  float* rowbuf = reinterpret_cast<float*>(dsm);
   const int V = a.V;
-  const FastLayout L = fast_layout(V);
-  float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
-  unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
-  unsigned* cnt = reinterpret_cast<unsigned*>(dsm + L.cnt);
-  unsigned long long* mass = reinterpret_cast<unsigned long long*>(dsm + L.mass);
-  unsigned char* un = dsm + L.un;
-  unsigned long long* lkey = reinterpret_cast<unsigned long long*>(un);
-  double* pv = reinterpret_cast<double*>(un + LIST_CAP * 8);
-  unsigned long long* ws = reinterpret_cast<unsigned long long*>(dsm + L.ws);
-  MetaSlot* meta = reinterpret_cast<MetaSlot*>(dsm + L.meta);
   const int tid = threadIdx.x;
   const int G = gridDim.x;
-  const int nbitmap = (V + 31) / 32;
+  const int nbm = (V + 31) / 32;
 
   if (tid == 0) mbar_init(&S.bar, 1);
-  unsigned phase = 0;
-  bool aborted = false;
-
   int act_pend = 1;
   auto issue_meta = [&](int r, MetaSlot& ms) {
     if (r >= a.B) return;
-    const char* pp = reinterpret_cast<const char*>(a.params + (long long)r * a.params_stride);
-    if (tid < 3) cp_async8(reinterpret_cast<char*>(&ms.P) + 8 * tid, pp + 8 * tid);
+    const char* prm = reinterpret_cast<const char*>(a.params + (long long)r * a.params_stride);
+    if (tid < 3) cp_async8(reinterpret_cast<char*>(&ms.P) + 8 * tid, prm + 8 * tid);
     else if (tid == 3) { if (a.hist_off) cp_async8(&ms.off0, a.hist_off + r); else ms.off0 = 0; }
     else if (tid == 4) { if (a.hist_off) cp_async8(&ms.off1, a.hist_off + r + 1); else ms.off1 = 0; }
     else if (tid == 5) cp_async8(&ms.rng, a.rng + r);
     else if (tid == 6) act_pend = a.active ? (int)a.active[r] : 1;
   };
-
   const int r0 = blockIdx.x;
   issue_meta(r0, meta[0]);
   cp_async_commit();
   if (tid == 6 && r0 < a.B) meta[0].active = act_pend;
   cp_async_wait<0>();
-  __syncthreads();
+  csync();
+  unsigned phase = 0;
+  Staged sg{0, 0, -1, 0.0f};
+  if (r0 < a.B && meta[0].active) sg = stage_row(a.logits + (long long)r0 * a.ld, V, rowbuf, &S.bar);
 
   int j = 0;
   for (int row = r0; row < a.B; row += G, ++j) {
-    MetaSlot& cur = meta[j & 1];
+    const MetaSlot& cur = meta[j & 1];
     MetaSlot& nxt = meta[(j + 1) & 1];
     const int next = row + G;
     issue_meta(next, nxt);
     cp_async_commit();
+    if (tid == 6 && next < a.B) nxt.active = act_pend;
+    bool staged_next = false;
     if (cur.active) {
       const c4s_row_params P = cur.P;
-      const Stage sg = stage_issue(a.logits + (long long)row * a.ld, V, rowbuf, &S.bar);
-      if (tid == 0 && next < a.B) {
-        // warm L2 with the next row while this one is processed
-        const float* gn = a.logits + (long long)next * a.ld;
-        const unsigned long long gna = (unsigned long long)gn;
-        int hn = (int)(((16u - (unsigned)(gna & 15ull)) & 15u) >> 2);
-        if (hn > V) hn = V;
-        const int bn = ((V - hn) >> 2) << 2;
-        if (bn > 0) prefetch_l2(gn + hn, (unsigned)bn * 4u);
-      }
       const bool pen = a.hist_off && P.repetition_penalty != 1.0f;
       long long h0 = 0, h1 = 0;
       if (pen) {
@@ -1174,29 +1122,103 @@ __global__ void __launch_bounds__(NT, 4) fast_kernel(Args a) {
           if (tid == 0) atomicOr(a.errflags, C4S_DEVERR_HIST_RANGE);
           h0 = h1 = 0;
         }
-        for (int w = tid; w < nbitmap; w += NT) bitmap[w] = 0u;
+        for (int w = tid; w < nbm; w += NT) bm[w] = 0u;
       }
       int hid[8];
       hist_prefetch(a, h0, h1, hid);
-      if (!stage_wait(a, sg, &S.bar, phase, S)) { aborted = true; break; }
-      float* srow = rowbuf + sg.shift;
-      if (pen) penalty_apply(a, srow, V, bitmap, P.repetition_penalty, hid, h0, h1);
-      if (!fast_row4(a, row, cur, rowbuf, sg.shift, cnt, mass, un, ws, S)) {
-        // outside the fast path's assumptions: the general path, same CTA, same staged row
-        __syncthreads();
-        if (tid == 0) atomicAdd(&a.counters[C4S_CNT_DEFERRED], 1ull);
-        finish_general(a, row, P, C4S_STAGE_PENALTY | C4S_STAGE_TEMPERATURE | C4S_STAGE_TOP_K | C4S_STAGE_TOP_P,
-                       srow, cnt, mass, lkey, pv, S);
+      // the staged row (bounded wait), its plain-loaded edges, the penalty
+      if (tid == 0) {
+        bool ok = true;
+        if (sg.body > 0) ok = mbar_wait_bounded(&S.bar, phase);
+        S.abort_row = ok ? 0 : 1;
+        if (!ok) atomicOr(a.errflags, C4S_DEVERR_TIMEOUT);
       }
+      if (sg.body > 0) phase ^= 1u;
+      if (sg.hpos >= 0) rowbuf[sg.hpos] = sg.hval;
+      csync();
+      if (S.abort_row) {
+        if (tid == 0) mbar_wait_bounded(&S.bar, phase ^ 1u);   // let the copy drain (bounded)
+        break;
+      }
+      float* srow = rowbuf + sg.shift;
+      if (pen) penalty_apply(a, srow, V, bm, P.repetition_penalty, hid, h0, h1);
+      float x[OWN];
+      load_block(rowbuf, sg.shift, V, x);
+      const int shift = sg.shift;
+      csync();                                     // every thread has its elements
+      // rows without top-k use the buffer as scratch: stage the next row after them
+      const bool scratch = !P.greedy && !(P.top_k > 0 && P.top_k < V);
+      if (!scratch && next < a.B && nxt.active) {
+        sg = stage_row(a.logits + (long long)next * a.ld, V, rowbuf, &S.bar);
+        staged_next = true;
+      }
+      if (row_body(a, row, cur, x, shift, dsm, S) == ROW_GENERAL) {
+        csync();
+        if (tid == 0) {
+          a.jobs[row].kind = JOB_DEFER;
+          defer_row(a, row);
+        }
+      }
+      if (scratch) csync();                        // scratch released
     } else if (tid == 0) {
       a.out_ids[row] = -1;
+      a.jobs[row].kind = JOB_NONE;
     }
-    if (tid == 6 && next < a.B) nxt.active = act_pend;
     cp_async_wait<0>();
-    __syncthreads();                                       // next metadata visible, buffers free
+    csync();                                       // next metadata visible
+    if (!staged_next) {
+      sg = Staged{0, 0, -1, 0.0f};
+      if (next < a.B && nxt.active) sg = stage_row(a.logits + (long long)next * a.ld, V, rowbuf, &S.bar);
+    }
   }
-  cp_async_wait<0>();
-  if (aborted && tid == 0) mbar_wait_bounded(&S.bar, phase);   // let a timed-out copy drain (bounded)
+}
+
+// ---------------------------------------------------------------------------
+// The general path for the rows the row and list kernels handed back; the
+// last CTA to finish clears the hand-back list for the next launch sequence.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __shared__ Shared S;
+  const Layout L = layout_for(a.V);
+  float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
+  unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
+  unsigned* cnt = reinterpret_cast<unsigned*>(dsm + L.cnt);
+  unsigned long long* mass = reinterpret_cast<unsigned long long*>(dsm + L.mass);
+  unsigned long long* lkey = reinterpret_cast<unsigned long long*>(dsm + L.key);
+  double* pv = reinterpret_cast<double*>(dsm + L.pv);
+  if (threadIdx.x == 0) mbar_init(&S.bar, 1);
+  csync();
+  unsigned phase = 0;
+  const unsigned n = *reinterpret_cast<volatile unsigned*>(a.defer_cnt);
+  for (unsigned t = blockIdx.x; t < n; t += gridDim.x)
+    if (!general_row(a, a.defer_rows[t], rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) break;
+  csync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&a.defer_cnt[1], 1u) == gridDim.x - 1) {
+      a.defer_cnt[0] = 0u;
+      a.defer_cnt[1] = 0u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Processed logits of list rows: the row kernel wrote the tempered values;
+// mask what the list kernel's top-k threshold and K* remove.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT) mask_kernel(Args a) {
+  const int row = blockIdx.x;
+  if (row >= a.B) return;
+  const RowJob& J = a.jobs[row];
+  if ((J.kind != JOB_TOPK && J.kind != JOB_K0) || J.status != RES_DONE) return;
+  const unsigned tk = J.thresh_key;
+  const unsigned long long kst = J.kstar;
+  float* o = a.out_logits + (long long)row * a.out_ld;
+  for (int i = threadIdx.x; i < a.V; i += NT) {
+    const float y = o[i];
+    if (fkey(y) < tk || (y > -INFINITY && ckey(y, i) < kst)) o[i] = -INFINITY;
+  }
 }
 
 }  // namespace c4s

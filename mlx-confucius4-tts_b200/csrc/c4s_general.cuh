@@ -14,6 +14,8 @@ namespace c4s {
 
 enum { MODE_SAMPLE = 0, MODE_PROCESS = 1, MODE_ARGMAX = 2 };
 
+struct RowJob;                  // fast path: per-row job record (c4s_fast.cuh)
+
 struct Args {
   const float* logits;          // MODE_SAMPLE / MODE_ARGMAX input
   float* inout;                 // MODE_PROCESS rows (in place)
@@ -35,8 +37,13 @@ struct Args {
   int scratch_stride;           // keys per CTA (power of two >= V)
   unsigned* errflags;
   unsigned long long* counters;
-  unsigned* sync;               // fast kernel: [0] rows deferred, [1] CTAs finished
-  int ishift;                   // fast kernel: log2 of the draw's index-bin width
+  // fast path: per-row jobs and candidate lists of the current chunk, rows for the general path
+  RowJob* jobs;
+  unsigned long long* lkeys;    // [B][LCAP] candidate keys
+  double* lpv;                  // [B][LCAP] their probabilities
+  unsigned long long* lsb;      // [B][LCAP] sort buffer of the exact fallback
+  int* defer_rows;              // rows handed to the general path
+  unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -70,9 +77,12 @@ struct Shared {
   unsigned long long mbefore;
   double redd[NWARP];
   double d1, d2;
-  float l1[16];
-  float fbefore;
-  int rows[NT];                 // deferred-row worklist of the last CTA
+  // fast kernel (row warps)
+  int dq[8];                    // rows the list warps handed back, not yet reprocessed
+  int ndq;
+  int abort_all;                // a bounded wait gave up: stop after this row
+  double oct[32];               // octave masses of the estimate
+  float fbefore;                // mass of the sub-bins below the crossing one
 };
 
 // u = 2^-53: unit roundoff of double.
@@ -87,7 +97,36 @@ __device__ __forceinline__ double band_q(int n, double SQ) {
   return 2.0 * ((4.0 * n + 16.0) * U53 * SQ + (double)n + 2.0);
 }
 
-__device__ __forceinline__ double prob(float y, float m) {
+// IEEE division, not inlined (keeps the many call sites small).
+__device__ __noinline__ float div_call(float x, float d) { return __fdiv_rn(x, d); }
+
+// Correctly rounded x / d with rd = RN(1/d) given (one __frcp_rn per row):
+// two Newton corrections of x*rd with fused remainders (Markstein, "Computation
+// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990), then a proof check: the remainder r = x - q*d of the final
+// q is exact (FMA), and |r| < |d| * ulp(q)/2 (with a 2^-20 margin) shows that q
+// is the float nearest to x/d. Quotients it cannot prove -- near-ties, powers
+// of two (whose lower neighbour is half an ulp away), |q| outside
+// [2^-100, 2^100], d outside [2^-100, 2^100] -- come from __fdiv_rn.
+__device__ __forceinline__ float div_rn(float x, float d, float rd) {
+  float q = __fmul_rn(x, rd);
+  if (x == 0.0f) return q;                          // signed zero (the corrections would lose -0)
+  float r = __fmaf_rn(-q, d, x);
+  q = __fmaf_rn(r, rd, q);
+  r = __fmaf_rn(-q, d, x);
+  q = __fmaf_rn(r, rd, q);
+  r = __fmaf_rn(-q, d, x);
+  const unsigned bq = __float_as_uint(q) & 0x7fffffffu;
+  const float hulp = __uint_as_float((bq & 0x7f800000u) - (24u << 23));   // ulp(q) / 2
+  const float ad = fabsf(d);
+  const bool ok = bq >= 0x0d800000u && bq <= 0x71800000u && (bq & 0x007fffffu) != 0u && ad >= 7.8886e-31f &&
+                  ad <= 1.2676e30f && fabsf(r) < __fmul_rn(__fmul_rn(hulp, ad), 0.99999905f);
+  if (ok) return q;
+  return div_call(x, d);
+}
+
+// Not inlined: CUDA's exp(double) is large and is called from many sites.
+__device__ __noinline__ double prob(float y, float m) {
   return exp((double)__fsub_rn(y, m));
 }
 
@@ -102,20 +141,20 @@ __device__ float radix_kth_largest(const float* srow, int V, int k, unsigned* cn
   unsigned prefix = 0, pmask = 0, kk = (unsigned)k;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int j = threadIdx.x; j < NBIN; j += NT) cnt[j] = 0;
-    __syncthreads();
+    csync();
     for (int i = threadIdx.x; i < V; i += NT) {
       const unsigned u = fkey(srow[i]);
       if ((u & pmask) == prefix) atomicAdd(&cnt[(u >> shift) & 255u], 1u);
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x < 32)
       warp_find_bin<unsigned>([&](int j) { return cnt[255 - j]; }, kk, false, &S.c, &S.cbefore);
-    __syncthreads();
+    csync();
     const unsigned d = 255u - (unsigned)S.c;
     kk -= S.cbefore;
     prefix |= d << shift;
     pmask |= 0xffu << shift;
-    __syncthreads();
+    csync();
   }
   return fkey_inv(prefix);
 }
@@ -126,7 +165,7 @@ template <typename Pred>
 __device__ int gather_sort(const float* srow, int V, unsigned long long* lkey, Shared& S, Pred pred,
                            bool index_keys) {
   if (threadIdx.x == 0) S.slot = 0;
-  __syncthreads();
+  csync();
   for (int i = threadIdx.x; i < V; i += NT) {
     const float y = srow[i];
     if (pred(y, i)) {
@@ -134,11 +173,11 @@ __device__ int gather_sort(const float* srow, int V, unsigned long long* lkey, S
       if (s < LIST_CAP) lkey[s] = index_keys ? (unsigned long long)i : ckey(y, i);
     }
   }
-  __syncthreads();
+  csync();
   const int n = min(S.slot, LIST_CAP);
   const int np = next_pow2(max(n, 1));
   for (int p = n + threadIdx.x; p < np; p += NT) lkey[p] = KEY_MAX;
-  __syncthreads();
+  csync();
   bitonic_sort_u64(lkey, np);
   return n;
 }
@@ -153,21 +192,21 @@ __device__ int topp_exact_seq(const float* srow, const unsigned long long* K, in
   for (int base = 0; base < n; base += NT) {
     const int e = base + threadIdx.x;
     if (e < n) pv[threadIdx.x] = prob(srow[ckey_idx(K[e])], m);
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
       const int lim = min(NT, n - base);
       for (int j = 0; j < lim; ++j) sum = __dadd_rn(sum, pv[j]);
     }
-    __syncthreads();
+    csync();
   }
   if (threadIdx.x == 0) { S.dsum = sum; S.jstar = n; }
-  __syncthreads();
+  csync();
   sum = S.dsum;
   double cum = 0.0;
   for (int base = 0; base < n; base += NT) {
     const int e = base + threadIdx.x;
     if (e < n) pv[threadIdx.x] = __ddiv_rn(prob(srow[ckey_idx(K[e])], m), sum);
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
       const int lim = min(NT, n - base);
       for (int j = 0; j < lim; ++j) {
@@ -175,11 +214,11 @@ __device__ int topp_exact_seq(const float* srow, const unsigned long long* K, in
         if (!(cum <= thr)) { S.jstar = base + j; break; }
       }
     }
-    __syncthreads();
+    csync();
     if (S.jstar < n) break;
   }
   const int js = S.jstar;
-  __syncthreads();
+  csync();
   return js;
 }
 
@@ -192,10 +231,10 @@ __device__ int topp_exact_pv(int n, float p, double* pv, Shared& S) {
     for (int e = 0; e < n; ++e) sum = __dadd_rn(sum, pv[e]);
     S.dsum = sum;
   }
-  __syncthreads();
+  csync();
   const double sum = S.dsum;
   for (int e = threadIdx.x; e < n; e += NT) pv[e] = __ddiv_rn(pv[e], sum);
-  __syncthreads();
+  csync();
   if (threadIdx.x == 0) {
     double cum = 0.0;
     int js = n;
@@ -205,9 +244,9 @@ __device__ int topp_exact_pv(int n, float p, double* pv, Shared& S) {
     }
     S.jstar = js;
   }
-  __syncthreads();
+  csync();
   const int js = S.jstar;
-  __syncthreads();
+  csync();
   return js;
 }
 
@@ -217,7 +256,7 @@ __device__ unsigned long long topp_list(const Args& a, const float* srow, const 
   if (n <= 0) return 0ull;
   const double thr = __dsub_rn(1.0, (double)P.top_p);
   for (int e = threadIdx.x; e < n; e += NT) pv[e] = prob(srow[ckey_idx(K[e])], m);
-  __syncthreads();
+  csync();
   bool exact = (n <= SEQ_MAX) || (a.debug & C4S_DEBUG_FORCE_EXACT);
   int jstar = n;
   if (!exact) {
@@ -230,7 +269,7 @@ __device__ unsigned long long topp_list(const Args& a, const float* srow, const 
     const unsigned long long base = block_exscan_u64(loc, S.red64, &SQ);
     const double SQd = (double)SQ, Tq = __dmul_rn(thr, SQd), bq = band_q(n, SQd);
     if (threadIdx.x == 0) { S.jstar = n; S.u64a = SQ; S.u64b = 0; }
-    __syncthreads();
+    csync();
     unsigned long long run = base;
     for (int e = lo; e < hi; ++e) {
       const unsigned long long q = qfix(pv[e], a.qscale);
@@ -240,7 +279,7 @@ __device__ unsigned long long topp_list(const Args& a, const float* srow, const 
       }
       run += q;
     }
-    __syncthreads();
+    csync();
     jstar = S.jstar;
     if (jstar < n && lo <= jstar && jstar < hi) {
       unsigned long long r = base;
@@ -248,9 +287,9 @@ __device__ unsigned long long topp_list(const Args& a, const float* srow, const 
       S.u64a = r;
       S.u64b = r + qfix(pv[jstar], a.qscale);
     }
-    __syncthreads();
+    csync();
     const bool ok = SQ > 0 && (double)S.u64a <= Tq - bq && (jstar == n || (double)S.u64b > Tq + bq);
-    __syncthreads();
+    csync();
     if (!ok) {
       exact = true;
       if (threadIdx.x == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
@@ -286,7 +325,7 @@ __device__ unsigned long long topp_global(const Args& a, const float* srow, floa
   const unsigned long long Kp = (jstar < n) ? G[jstar] : KEY_MAX;
   const int mk = P.min_tokens_to_keep;
   const unsigned long long Kkeep = (mk <= 0) ? KEY_MAX : (mk <= n ? G[n - mk] : 0ull);
-  __syncthreads();
+  csync();
   return Kp < Kkeep ? Kp : Kkeep;
 }
 
@@ -300,7 +339,7 @@ __device__ unsigned long long topp_binned(const Args& a, const float* srow, floa
   if ((a.debug & C4S_DEBUG_FORCE_EXACT) || P.min_tokens_to_keep > 1 || !(m < INFINITY))
     return topp_global(a, srow, m, thresh, P, pv, S);
   for (int j = threadIdx.x; j < NBIN; j += NT) { cnt[j] = 0; mass[j] = 0; }
-  __syncthreads();
+  csync();
   unsigned long long kmax = 0;
   for (int i = threadIdx.x; i < V; i += NT) {
     const float y = srow[i];
@@ -349,11 +388,11 @@ __device__ unsigned long long topp_binned(const Args& a, const float* srow, floa
   // ascending value order = descending bin index
   if (threadIdx.x < 32)
     warp_find_bin<unsigned long long>([&](int j) { return mass[255 - j]; }, target, true, &S.c, &S.mbefore);
-  __syncthreads();
+  csync();
   const int c = 255 - S.c;  // S.c < NBIN because target < sq
   const unsigned long long before = S.mbefore;
   const int nc = (int)cnt[c];
-  __syncthreads();
+  csync();
   if (nc > LIST_CAP) {
     if (threadIdx.x == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
     return topp_global(a, srow, m, thresh, P, pv, S);
@@ -368,14 +407,14 @@ __device__ unsigned long long topp_binned(const Args& a, const float* srow, floa
   unsigned long long tot;
   const unsigned long long pbase = before + block_exscan_u64(loc, S.red64, &tot);
   if (threadIdx.x == 0) { S.jstar = n; S.u64a = before; S.u64b = 0; }
-  __syncthreads();
+  csync();
   unsigned long long run = pbase;
   for (int e = lo; e < hi; ++e) {
     const unsigned long long q = qfix(prob(srow[ckey_idx(lkey[e])], m), a.qscale);
     if ((double)(run + q) > Tq) { atomicMin(&S.jstar, e); break; }
     run += q;
   }
-  __syncthreads();
+  csync();
   const int jstar = S.jstar;
   if (jstar < n && lo <= jstar && jstar < hi) {
     unsigned long long r = pbase;
@@ -383,10 +422,10 @@ __device__ unsigned long long topp_binned(const Args& a, const float* srow, floa
     S.u64a = r;
     S.u64b = r + qfix(prob(srow[ckey_idx(lkey[jstar])], m), a.qscale);
   }
-  __syncthreads();
+  csync();
   const bool ok = jstar < n && (double)S.u64a <= Tq - bq && (double)S.u64b > Tq + bq;
   const unsigned long long Kp = jstar < n ? lkey[jstar] : KEY_MAX;
-  __syncthreads();
+  csync();
   if (!ok) {
     if (threadIdx.x == 0) atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
     return topp_global(a, srow, m, thresh, P, pv, S);
@@ -414,9 +453,9 @@ __device__ int draw_exact_list(const float* srow, const unsigned long long* I, i
     }
     S.tok = tok;
   }
-  __syncthreads();
+  csync();
   const int t = S.tok;
-  __syncthreads();
+  csync();
   return t;
 }
 
@@ -429,15 +468,15 @@ __device__ int draw_exact_row(const float* srow, int V, float md, double u, doub
     double p = 0.0;
     if (i < V) { const float y = srow[i]; if (D(y, i)) p = prob(y, md); }
     pv[threadIdx.x] = p;
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
       const int lim = min(NT, V - base);
       for (int j = 0; j < lim; ++j) if (pv[j] != 0.0) sum = __dadd_rn(sum, pv[j]);
     }
-    __syncthreads();
+    csync();
   }
   if (threadIdx.x == 0) { S.dsum = __dmul_rn(u, sum); S.tok = (S.dsum == 0.0) ? 0 : -1; }
-  __syncthreads();
+  csync();
   const double r = S.dsum;
   double acc = 0.0;
   for (int base = 0; base < V && S.tok < 0; base += NT) {
@@ -445,7 +484,7 @@ __device__ int draw_exact_row(const float* srow, int V, float md, double u, doub
     double p = 0.0;
     if (i < V) { const float y = srow[i]; if (D(y, i)) p = prob(y, md); }
     pv[threadIdx.x] = p;
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
       const int lim = min(NT, V - base);
       for (int j = 0; j < lim; ++j) {
@@ -454,12 +493,12 @@ __device__ int draw_exact_row(const float* srow, int V, float md, double u, doub
         if (r <= acc) { S.tok = base + j; break; }
       }
     }
-    __syncthreads();
+    csync();
   }
   if (threadIdx.x == 0 && S.tok < 0) S.tok = V - 1;
-  __syncthreads();
+  csync();
   const int t = S.tok;
-  __syncthreads();
+  csync();
   return t;
 }
 
@@ -467,7 +506,7 @@ __device__ int draw_exact_row(const float* srow, int V, float md, double u, doub
 __device__ int draw_list(const Args& a, const float* srow, const unsigned long long* I, int n, float md,
                          double u, double* pv, Shared& S) {
   for (int e = threadIdx.x; e < n; e += NT) pv[e] = prob(srow[(int)I[e]], md);
-  __syncthreads();
+  csync();
   if (n <= SEQ_MAX || (a.debug & C4S_DEBUG_FORCE_EXACT) || n == 0)
     return n == 0 ? 0 : draw_exact_list(srow, I, n, md, u, a.V, pv, S);
   const int E = (n + NT - 1) / NT;
@@ -478,7 +517,7 @@ __device__ int draw_list(const Args& a, const float* srow, const unsigned long l
   const unsigned long long base = block_exscan_u64(loc, S.red64, &SQ);
   const double SQd = (double)SQ, rq = __dmul_rn(u, SQd), bq = band_q(n, SQd);
   if (threadIdx.x == 0) { S.jstar = n; S.u64a = 0; S.u64b = 0; }
-  __syncthreads();
+  csync();
   unsigned long long run = base;
   for (int e = lo; e < hi; ++e) {
     const unsigned long long q = qfix(pv[e], a.qscale);
@@ -488,7 +527,7 @@ __device__ int draw_list(const Args& a, const float* srow, const unsigned long l
     }
     run += q;
   }
-  __syncthreads();
+  csync();
   const int js = S.jstar;
   if (js < n && lo <= js && js < hi) {
     unsigned long long r = base;
@@ -496,9 +535,9 @@ __device__ int draw_list(const Args& a, const float* srow, const unsigned long l
     S.u64a = r;
     S.u64b = r + qfix(pv[js], a.qscale);
   }
-  __syncthreads();
+  csync();
   const bool ok = SQ > 0 && js < n && (double)S.u64a < rq - bq && (double)S.u64b > rq + bq;
-  __syncthreads();
+  csync();
   if (ok) return (int)I[js];
   if (threadIdx.x == 0) atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
   return draw_exact_list(srow, I, n, md, u, a.V, pv, S);
@@ -526,7 +565,7 @@ __device__ int draw_rowpass(const Args& a, const float* srow, float md, double u
   const int n = block_reduce(nl, SumI(), S.redi);
   const double SQd = (double)SQ, rq = __dmul_rn(u, SQd), bq = band_q(n, SQd);
   if (threadIdx.x == 0) { S.tok = -1; S.u64a = 0; S.u64b = 0; }
-  __syncthreads();
+  csync();
   if (SQ > 0 && (double)base < rq && (double)(base + loc) >= rq) {
     unsigned long long run = base;
     for (int i = lo; i < hi; ++i) {
@@ -537,10 +576,10 @@ __device__ int draw_rowpass(const Args& a, const float* srow, float md, double u
       run += q;
     }
   }
-  __syncthreads();
+  csync();
   const int tok = S.tok;
   const bool ok = tok >= 0 && (double)S.u64a < rq - bq && (double)S.u64b > rq + bq;
-  __syncthreads();
+  csync();
   if (ok) return tok;
   if (threadIdx.x == 0) atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
   return draw_exact_row(srow, V, md, u, pv, S, D);
@@ -585,7 +624,7 @@ __device__ __forceinline__ bool stage_wait(const Args& a, const Stage& st, unsig
     if (!ok) atomicOr(a.errflags, C4S_DEVERR_TIMEOUT);
   }
   if (st.body > 0) phase ^= 1u;
-  __syncthreads();
+  csync();
   return S.abort_row == 0;
 }
 
@@ -614,20 +653,21 @@ __device__ __forceinline__ void hist_prefetch(const Args& a, long long h0, long 
 // de-duplicated by a zeroed shared bitmap. Ends with a CTA barrier.
 __device__ __forceinline__ void penalty_apply(const Args& a, float* srow, int V, unsigned* bitmap, float pen,
                                               const int (&hid)[8], long long h0, long long h1) {
+  const float rpen = __frcp_rn(pen);
   auto apply = [&](int t) {
     if ((unsigned)t < (unsigned)V) {
       const unsigned bit = 1u << (t & 31);
       const unsigned old = atomicOr(&bitmap[t >> 5], bit);
       if (!(old & bit)) {
         const float s = srow[t];
-        srow[t] = (s < 0.0f) ? __fmul_rn(s, pen) : __fdiv_rn(s, pen);
+        srow[t] = (s < 0.0f) ? __fmul_rn(s, pen) : div_rn(s, pen, rpen);
       }
     }
   };
 #pragma unroll
   for (int q = 0; q < 8; ++q) apply(hid[q]);
   for (long long j = h0 + threadIdx.x + 8LL * NT; j < h1; j += NT) apply(a.hist[j]);
-  __syncthreads();
+  csync();
 }
 
 // ---------------------------------------------------------------------------
@@ -636,7 +676,7 @@ __device__ __forceinline__ void penalty_apply(const Args& a, float* srow, int V,
 // processed logits. Handles every vocabulary size up to MAX_VOCAB and every
 // input the reference defines.
 // ---------------------------------------------------------------------------
-__device__ void finish_general(const Args& a, int row, const c4s_row_params& P, int st, float* srow,
+__device__ __noinline__ void finish_general(const Args& a, int row, const c4s_row_params& P, int st, float* srow,
                                unsigned* cnt, unsigned long long* mass, unsigned long long* lkey, double* pv,
                                Shared& S) {
   const int V = a.V;
@@ -657,7 +697,7 @@ __device__ void finish_general(const Args& a, int row, const c4s_row_params& P, 
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
     if ((tid & 31) == 0) { S.redf[tid >> 5] = bv; S.redi[tid >> 5] = bi; }
-    __syncthreads();
+    csync();
     if (tid == 0) {
       float b = S.redf[0];
       int ix = S.redi[0];
@@ -669,7 +709,7 @@ __device__ void finish_general(const Args& a, int row, const c4s_row_params& P, 
       float* o = a.out_logits + (long long)row * a.out_ld;
       for (int i = tid; i < V; i += NT) o[i] = srow[i];
     }
-    __syncthreads();
+    csync();
     return;
   }
 
@@ -693,18 +733,18 @@ __device__ void finish_general(const Args& a, int row, const c4s_row_params& P, 
     bool done = false;
     if (!(a.debug & C4S_DEBUG_FORCE_EXACT) && m > -INFINITY && m < INFINITY) {
       for (int j = tid; j < NBIN; j += NT) cnt[j] = 0;
-      __syncthreads();
+      csync();
       for (int i = tid; i < V; i += NT) {
         const int b = vbin(m, srow[i]);
         if (b < NBIN - 1) atomicAdd(&cnt[b], 1u);
       }
-      __syncthreads();
+      csync();
       if (tid < 32)
         warp_find_bin<unsigned>([&](int j) { return cnt[j]; }, (unsigned)P.top_k, false, &S.c, &S.cbefore);
-      __syncthreads();
+      csync();
       const int c = S.c;
       const int nle = (c < NBIN - 1) ? (int)(S.cbefore + cnt[c]) : LIST_CAP + 1;
-      __syncthreads();
+      csync();
       if (nle <= LIST_CAP) {
         const int n = gather_sort(srow, V, lkey, S, [&](float y, int) { return vbin(m, y) <= c; }, false);
         thresh = fkey_inv((unsigned)(lkey[n - P.top_k] >> 32));
@@ -756,7 +796,7 @@ __device__ void finish_general(const Args& a, int row, const c4s_row_params& P, 
       a.rng[row] = x;
       S.u64c = x >> 11;
     }
-    __syncthreads();
+    csync();
     const unsigned long long u53 = S.u64c;
     const double u = (double)u53 * 1.1102230246251565e-16;  // (x>>11) / 2^53, exact
     int tok;
@@ -775,14 +815,14 @@ __device__ void finish_general(const Args& a, int row, const c4s_row_params& P, 
         const int e = tid + q * NT;
         tmp[q] = (e < nk) ? (unsigned long long)ckey_idx(K[jf + e]) : KEY_MAX;
       }
-      __syncthreads();
+      csync();
       const int np = next_pow2(max(nk, 1));
 #pragma unroll
       for (int q = 0; q < LIST_CAP / NT; ++q) {
         const int e = tid + q * NT;
         if (e < np) lkey[e] = tmp[q];
       }
-      __syncthreads();
+      csync();
       bitonic_sort_u64(lkey, np);
       tok = draw_list(a, srow, lkey, nk, md, u, pv, S);
     } else {
@@ -811,6 +851,33 @@ __device__ void finish_general(const Args& a, int row, const c4s_row_params& P, 
       out[i] = masked ? -INFINITY : y;
     }
   }
+}
+
+// One row through the general path from global memory: stage, penalty,
+// finish_general. Returns false if the staging wait gave up.
+__device__ __noinline__ bool general_row(const Args& a, int row, float* rowbuf, unsigned* bitmap, unsigned* cnt,
+                            unsigned long long* mass, unsigned long long* lkey, double* pv, Shared& S,
+                            unsigned& phase) {
+  const int V = a.V;
+  const c4s_row_params P = a.params[(long long)row * a.params_stride];
+  const int st = a.mode == MODE_SAMPLE
+                     ? (C4S_STAGE_PENALTY | C4S_STAGE_TEMPERATURE | C4S_STAGE_TOP_K | C4S_STAGE_TOP_P)
+                     : (a.mode == MODE_PROCESS ? a.stages : 0);
+  const float* g = (a.mode == MODE_PROCESS ? a.inout : a.logits) + (long long)row * a.ld;
+  const Stage sg = stage_issue(g, V, rowbuf, &S.bar);
+  const bool pen = (st & C4S_STAGE_PENALTY) && a.hist_off && P.repetition_penalty != 1.0f;
+  long long h0, h1;
+  hist_window(a, row, pen, h0, h1);
+  int hid[8];
+  hist_prefetch(a, h0, h1, hid);
+  if (pen)
+    for (int w = threadIdx.x; w < (V + 31) / 32; w += NT) bitmap[w] = 0u;
+  if (!stage_wait(a, sg, &S.bar, phase, S)) return false;
+  float* srow = rowbuf + sg.shift;
+  if (pen) penalty_apply(a, srow, V, bitmap, P.repetition_penalty, hid, h0, h1);
+  finish_general(a, row, P, st, srow, cnt, mass, lkey, pv, S);
+  csync();
+  return true;
 }
 
 }  // namespace c4s

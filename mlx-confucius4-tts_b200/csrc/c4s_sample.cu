@@ -46,43 +46,22 @@ namespace c4s {
 __global__ void __launch_bounds__(NT, 4) rows_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ Shared S;
-  const int V = a.V;
-  const Layout L = layout_for(V);
+  const Layout L = layout_for(a.V);
   float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
   unsigned* cnt = reinterpret_cast<unsigned*>(dsm + L.cnt);
   unsigned long long* mass = reinterpret_cast<unsigned long long*>(dsm + L.mass);
   unsigned long long* lkey = reinterpret_cast<unsigned long long*>(dsm + L.key);
   double* pv = reinterpret_cast<double*>(dsm + L.pv);
-  const int tid = threadIdx.x;
-
-  if (tid == 0) mbar_init(&S.bar, 1);
-  __syncthreads();
+  if (threadIdx.x == 0) mbar_init(&S.bar, 1);
+  csync();
   unsigned phase = 0;
-
   for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
-    const c4s_row_params P = a.params[(long long)row * a.params_stride];
     if (a.mode == MODE_SAMPLE && a.active && !a.active[row]) {
-      if (tid == 0) a.out_ids[row] = -1;
+      if (threadIdx.x == 0) a.out_ids[row] = -1;
       continue;
     }
-    const int st = a.mode == MODE_SAMPLE
-                       ? (C4S_STAGE_PENALTY | C4S_STAGE_TEMPERATURE | C4S_STAGE_TOP_K | C4S_STAGE_TOP_P)
-                       : (a.mode == MODE_PROCESS ? a.stages : 0);
-    const float* g = (a.mode == MODE_PROCESS ? a.inout : a.logits) + (long long)row * a.ld;
-    const Stage sg = stage_issue(g, V, rowbuf, &S.bar);
-    const bool pen = (st & C4S_STAGE_PENALTY) && a.hist_off && P.repetition_penalty != 1.0f;
-    long long h0, h1;
-    hist_window(a, row, pen, h0, h1);
-    int hid[8];
-    hist_prefetch(a, h0, h1, hid);
-    if (pen)
-      for (int w = tid; w < (V + 31) / 32; w += NT) bitmap[w] = 0u;
-    if (!stage_wait(a, sg, &S.bar, phase, S)) return;
-    float* srow = rowbuf + sg.shift;
-    if (pen) penalty_apply(a, srow, V, bitmap, P.repetition_penalty, hid, h0, h1);
-    finish_general(a, row, P, st, srow, cnt, mass, lkey, pv, S);
-    __syncthreads();
+    if (!general_row(a, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) return;
   }
 }
 
@@ -109,9 +88,13 @@ struct c4s_ctx {
   unsigned* d_err = nullptr;
   unsigned long long* d_counters = nullptr;
   c4s_row_params* d_default_params = nullptr;  // one zeroed struct (argmax reads no field)
-  unsigned* d_sync = nullptr;                  // fast kernel: deferred rows, finished CTAs
-  int fast_occ = 0;                            // resident fast-kernel CTAs per SM (for fast_V)
-  int fast_V = -1;
+  int row_occ = 0;                             // resident row-kernel CTAs per SM
+  c4s::RowJob* d_jobs = nullptr;               // fast path: per-row jobs of one chunk
+  unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
+  double* d_lpv = nullptr;
+  unsigned long long* d_lsb = nullptr;
+  int* d_defer_rows = nullptr;                 //   rows handed to the general path
+  unsigned* d_defer_cnt = nullptr;
   int debug = 0;
   int cached_V = -1;
   int cached_occ = 0;
@@ -163,30 +146,47 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
   a.scratch_stride = ctx->scratch_stride;
   a.errflags = ctx->d_err;
   a.counters = ctx->d_counters;
-  a.sync = ctx->d_sync;
   a.debug = ctx->debug;
   int lg = 0;
   while ((1 << lg) < a.V) ++lg;
   a.qscale = std::ldexp(1.0, 62 - std::max(lg, 1));
-  int ish = 2;
-  while (((a.V + (1 << ish) - 1) >> ish) > NB_I) ++ish;
-  a.ishift = ish;
   cudaError_t e;
   if (a.mode == MODE_SAMPLE && a.V <= F_MAXV) {
-    // fast kernel: one persistent CTA per resident slot
-    const size_t fsm = fast_layout(a.V).total;
-    if (ctx->fast_V != a.V) {
+    // fast path, per chunk of K_CHUNK rows: row kernel -> list kernel -> general
+    // path for handed-back rows (-> masking of processed logits)
+    a.jobs = ctx->d_jobs;
+    a.lkeys = ctx->d_lkeys;
+    a.lpv = ctx->d_lpv;
+    a.lsb = ctx->d_lsb;
+    a.defer_rows = ctx->d_defer_rows;
+    a.defer_cnt = ctx->d_defer_cnt;
+    if (ctx->row_occ == 0) {
       int occ = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fast_kernel, NT, fsm) != cudaSuccess || occ < 1)
-        return fail(ctx, C4S_ERR_CUDA, "fast kernel occupancy");
-      ctx->fast_V = a.V;
-      ctx->fast_occ = occ;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, NT, row_smem(F_MAXV)) != cudaSuccess || occ < 1)
+        return fail(ctx, C4S_ERR_CUDA, "row kernel occupancy");
+      ctx->row_occ = occ;
     }
-    const int grid = (int)std::min<long long>((long long)a.B, (long long)std::min(ctx->fast_occ, 8) * ctx->num_sms);
-    if (grid > ctx->scratch_ctas) return fail(ctx, C4S_ERR_CAPACITY, "grid exceeds scratch slabs");
-    fast_kernel<<<grid, NT, fsm, (cudaStream_t)stream>>>(a);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "fast_kernel launch");
+    const cudaStream_t st = (cudaStream_t)stream;
+    const size_t gsm = layout_for(a.V).total;
+    for (int c0 = 0; c0 < a.B; c0 += K_CHUNK) {
+      Args ac = a;
+      ac.B = std::min(K_CHUNK, a.B - c0);
+      ac.logits = a.logits + (long long)c0 * a.ld;
+      ac.params = a.params + (long long)c0 * a.params_stride;
+      ac.rng = a.rng + c0;
+      if (a.active) ac.active = a.active + c0;
+      ac.out_ids = a.out_ids + c0;
+      if (a.out_logits) ac.out_logits = a.out_logits + (long long)c0 * a.out_ld;
+      if (a.hist_off) ac.hist_off = a.hist_off + c0;
+      const int g1 = (int)std::min<long long>(ac.B, (long long)ctx->row_occ * ctx->num_sms);
+      row_kernel<<<g1, NT, row_smem(ac.V), st>>>(ac);
+      list_kernel<<<(ac.B + LIST_WARPS - 1) / LIST_WARPS, 32 * LIST_WARPS, 0, st>>>(ac);
+      const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
+      defer_kernel<<<g3, NT, gsm, st>>>(ac);
+      if (a.out_logits) mask_kernel<<<ac.B, NT, 0, st>>>(ac);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "fast path launch");
+    }
     return C4S_OK;
   }
   const size_t smem = layout_for(a.V).total;
@@ -197,6 +197,19 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(ctx, e, "rows_kernel launch");
   return C4S_OK;
+}
+
+void free_all(c4s_ctx* ctx) {
+  cudaFree(ctx->d_scratch);
+  cudaFree(ctx->d_err);
+  cudaFree(ctx->d_counters);
+  cudaFree(ctx->d_default_params);
+  cudaFree(ctx->d_jobs);
+  cudaFree(ctx->d_lkeys);
+  cudaFree(ctx->d_lpv);
+  cudaFree(ctx->d_lsb);
+  cudaFree(ctx->d_defer_rows);
+  cudaFree(ctx->d_defer_cnt);
 }
 
 int check_common(c4s_ctx* ctx, int B, int V, long long ld) {
@@ -246,8 +259,7 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   const size_t smem_max = c4s::layout_for(c4s::MAX_VOCAB).total;
   e = cudaFuncSetAttribute(c4s::rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(c4s::fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)c4s::fast_layout(c4s::F_MAXV).total);
+    e = cudaFuncSetAttribute(c4s::defer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   int p2 = 1;
   while (p2 < max_vocab) p2 <<= 1;
@@ -256,17 +268,21 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   e = cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * p2 * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_counters, C4S_NUM_COUNTERS * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_sync, 2 * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_sync, 0, 2 * sizeof(unsigned));
+  const size_t nl = (size_t)c4s::K_CHUNK * c4s::LCAP;
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_jobs, (size_t)c4s::K_CHUNK * sizeof(c4s::RowJob));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lkeys, nl * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lpv, nl * sizeof(double));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (size_t)c4s::K_CHUNK * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, 2 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, 2 * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_default_params, 0, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_counters, 0, C4S_NUM_COUNTERS * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
-    cudaFree(ctx->d_scratch); cudaFree(ctx->d_err); cudaFree(ctx->d_counters);
-    cudaFree(ctx->d_default_params);
-    cudaFree(ctx->d_sync);
+    free_all(ctx);
     delete ctx;
     return C4S_ERR_CUDA;
   }
@@ -278,11 +294,7 @@ int c4s_destroy(c4s_ctx* ctx) {
   if (!ctx) return C4S_ERR_INVALID;
   {
     DeviceGuard dg(ctx->device);
-    cudaFree(ctx->d_scratch);
-    cudaFree(ctx->d_err);
-    cudaFree(ctx->d_counters);
-    cudaFree(ctx->d_default_params);
-    cudaFree(ctx->d_sync);
+    free_all(ctx);
   }
   delete ctx;
   return C4S_OK;
