@@ -508,13 +508,25 @@ __global__ void __launch_bounds__(32 * LIST_WARPS) list_kernel(Args a) {
 // read as -inf (never a candidate, mass 0).
 __device__ __forceinline__ void load_block(const float* rowbuf, int shift, int V, float (&x)[OWN]) {
   const int p0 = threadIdx.x * OWN;
+  const int i0 = p0 - shift;
+  const float4* r4 = reinterpret_cast<const float4*>(rowbuf + p0);
+  if (i0 >= 0 && i0 + OWN <= V) {                  // every position holds an element
 #pragma unroll
-  for (int q = 0; q < OWN / 4; ++q) {
-    const int i = p0 + 4 * q - shift;
-    const float4 v = *reinterpret_cast<const float4*>(rowbuf + p0 + 4 * q);
-    const float vv[4] = {v.x, v.y, v.z, v.w};
+    for (int q = 0; q < OWN / 4; ++q) {
+      const float4 v = r4[q];
+      x[4 * q] = v.x;
+      x[4 * q + 1] = v.y;
+      x[4 * q + 2] = v.z;
+      x[4 * q + 3] = v.w;
+    }
+  } else {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) x[4 * q + r] = (unsigned)(i + r) < (unsigned)V ? vv[r] : -INFINITY;
+    for (int q = 0; q < OWN / 4; ++q) {
+      const float4 v = r4[q];
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) x[4 * q + r] = (unsigned)(i0 + 4 * q + r) < (unsigned)V ? vv[r] : -INFINITY;
+    }
   }
 }
 
@@ -526,12 +538,12 @@ __device__ __forceinline__ float pick(const float (&x)[OWN], int j) {
   return v;
 }
 
-// Writes a row of processed logits from the registers: y, or -inf where the
-// top-k threshold key or K* removes it.
-__device__ __forceinline__ void write_row(const Args& a, const RowCtx& rc, const float (&x)[OWN], bool temper,
-                                          unsigned thresh_key, unsigned long long kst) {
+// Writes a row of processed logits from a copy of this thread's elements: y,
+// or -inf where the top-k threshold key or K* removes it. Out of line: it only
+// runs when processed logits are requested.
+__device__ __noinline__ void write_row(const Args& a, const RowCtx& rc, const float* x, bool temper,
+                                       unsigned thresh_key, unsigned long long kst) {
   float* o = a.out_logits + (long long)rc.row * a.out_ld;
-#pragma unroll
   for (int j = 0; j < OWN; ++j) {
     const int i = rc.i0 + j;
     if ((unsigned)i < (unsigned)rc.V) {
@@ -540,6 +552,14 @@ __device__ __forceinline__ void write_row(const Args& a, const RowCtx& rc, const
       o[i] = masked ? -INFINITY : y;
     }
   }
+}
+// As write_row, from the registers (through a local copy, so that x itself
+// stays in registers).
+__device__ __forceinline__ void write_row_regs(const Args& a, const RowCtx& rc, const float (&x)[OWN], bool temper) {
+  float xc[OWN];
+#pragma unroll
+  for (int j = 0; j < OWN; ++j) xc[j] = x[j];
+  write_row(a, rc, xc, temper, 0u, 0ull);
 }
 
 // Candidate of the big path: a row element of the crossing octave.
@@ -618,100 +638,37 @@ __device__ __forceinline__ void write_keys(unsigned long long* keys, const RowCt
   }
 }
 
+// As write_keys, from a local copy of the elements (indexable).
+__device__ __forceinline__ void write_keys_mem(unsigned long long* keys, const RowCtx& rc, const float* x,
+                                           unsigned long long mask, int wpos) {
+  while (mask) {
+    const int j = __ffsll((long long)mask) - 1;
+    mask &= mask - 1ull;
+    keys[wpos++] = ckey(yex(rc, x[j]), rc.i0 + j);
+  }
+}
+
 enum { ROW_DONE = 0, ROW_GENERAL = 1 };
 
-// Rows without top-k (top-p over the whole row, sampling.cpp:42-71, and the
-// draw). One pass builds an octave histogram of the estimates (private
-// per-thread columns, no atomics) and locates the octave of the top-p
-// crossing. If the octaves down to it hold at most LCAP elements they become
-// a list job whose tail (the deeper octaves) is an estimate with a proven
-// bound that the list kernel checks exactly. Otherwise the row kernel
-// finishes the row: sub-bins and candidates of the crossing octave, an exact
-// sort of the crossing sub-bin, then the draw over per-thread survivor masses.
-__device__ __noinline__ int k0_row(const Args& a, const RowCtx& rc, const float (&x)[OWN], unsigned char* work,
-                                   Shared& S, bool forced) {
+// Octave totals of a row without top-k and its crossing octave.
+struct K0Oct {
+  double Se, Ee, Th, rnd, cum, Eb;
+  int bc;                          // crossing octave; -1: top_p > 1, everything is kept
+};
+
+// The big path of a row without top-k, after its octave histogram (columns
+// still in the work area): sub-bins and candidates of the crossing octave, an
+// exact sort of the crossing sub-bin, then the draw over per-thread survivor
+// masses. Out of line: only rows whose crossing list would be too long.
+__device__ __noinline__ int k0_big(const Args& a, const RowCtx& rc, const float* x, unsigned char* work, Shared& S,
+                                   bool forced, const K0Oct& O) {
   const int V = rc.V, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = rc.row;
   const float m_y = rc.m_y;
   const double thr = rc.thr;
-
-  // ---- octave histogram of the estimates ----
-  float* Hc = reinterpret_cast<float*>(work);
-#pragma unroll
-  for (int b = 0; b <= NOCT; ++b) Hc[b * NT + tid] = 0.0f;
-#pragma unroll
-  for (int j = 0; j < OWN; ++j) {
-    const float p = __expf(dest(rc, x[j]));
-    Hc[(est_rank(p) >> 8) * NT + tid] += p;
-  }
-  csync();
-  for (int b = warp; b <= NOCT; b += NWARP) {
-    double v = 0.0;
-#pragma unroll
-    for (int q = 0; q < NT / 32; ++q) v += (double)Hc[b * NT + lane + 32 * q];
-    v = warp_sum_d(v);
-    if (lane == 0) S.oct[b] = v;
-  }
-  csync();
-  double Se = 0.0, Ee = 0.0;
-  for (int b = 0; b <= NOCT; ++b) {
-    Se += S.oct[b];
-    Ee += S.oct[b] * oct_d(b);
-  }
-  const double Th = thr * Se;
-  const double es = est_err(Se, Ee, m_y, 36, V);
-  const double rnd = 2.0 * ((4.0 * V + 16.0) * U53 * Se);
-  int bc = -1;                     // crossing octave; -1: top_p > 1, everything is kept
-  double cum = 0.0, Eb = 0.0;      // estimated mass (and |d| mass) of the octaves below it
-  if (thr > 0.0) {
-    for (int b = NOCT; b >= 0; --b) {
-      if (cum + S.oct[b] > Th) { bc = b; break; }
-      cum += S.oct[b];
-      Eb += S.oct[b] * oct_d(b);
-    }
-    if (bc < 0 || bc == NOCT) return ROW_GENERAL;
-  }
-
-  // ---- list job: octaves 0..bl, the deeper ones an estimated tail ----
-  if (thr > 0.0 && !forced) {
-    int bl = bc;
-    for (;;) {
-      double tl = 0.0, et = 0.0;
-      for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
-      if (tl + 2.0 * est_err(tl, et, m_y, 36, V) + thr * es + rnd < Th) break;
-      if (++bl >= NOCT) break;
-    }
-    double nb = 0.0;                              // count bound: p~ > 2^-(b+1) in octave b
-    for (int b = 0; b <= bl && b < NOCT; ++b) nb += S.oct[b] * exp2((double)(b + 1));
-    if (bl < NOCT && nb <= 2.0 * LCAP) {
-      unsigned long long mask = 0ull;
-      float xmx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < OWN; ++j) {
-        if ((est_rank(__expf(dest(rc, x[j]))) >> 8) <= bl) mask |= 1ull << j;
-        else xmx = fmaxf(xmx, x[j]);
-      }
-      int ng;
-      const int wpos = block_exscan_i32(__popcll(mask), S.redi, &ng);
-      if (ng <= LCAP) {
-        write_keys(a.lkeys + (size_t)row * LCAP, rc, x, mask, wpos);
-        const float xm = block_reduce(xmx, MaxF(), S.redf);
-        if (tid == 0) {
-          RowJob& J = a.jobs[row];
-          double tl = 0.0, et = 0.0;
-          for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
-          fill_job(J, rc, JOB_K0, ng, 0);
-          J.tail = tl;
-          J.tail_err = est_err(tl, et, m_y, 36, V);
-          J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
-        }
-        if (a.out_logits) write_row(a, rc, x, true, 0u, 0ull);
-        return ROW_DONE;
-      }
-    }
-  }
-
-  // ---- the row kernel finishes the row ----
+  const float* Hc = reinterpret_cast<const float*>(work);
+  const int bc = O.bc;
+  const double Se = O.Se, Ee = O.Ee, Th = O.Th, rnd = O.rnd, cum = O.cum, Eb = O.Eb;
   // survivor mass of this thread's elements in the octaves above the crossing one
   float hi = 0.0f;
   {
@@ -910,6 +867,103 @@ __device__ __noinline__ int k0_row(const Args& a, const RowCtx& rc, const float 
   return ROW_DONE;
 }
 
+// Rows without top-k (top-p over the whole row, sampling.cpp:42-71, and the
+// draw). One pass builds an octave histogram of the estimates (private
+// per-thread columns, no atomics) and locates the octave of the top-p
+// crossing. If the octaves down to it hold at most LCAP elements they become
+// a list job whose tail (the deeper octaves) is an estimate with a proven
+// bound that the list kernel checks exactly. Otherwise the row kernel
+// finishes the row: sub-bins and candidates of the crossing octave, an exact
+// sort of the crossing sub-bin, then the draw over per-thread survivor masses.
+__device__ __noinline__ int k0_row(const Args& a, const RowCtx& rc, const float* x, unsigned char* work,
+                                   Shared& S, bool forced) {
+  const int V = rc.V, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = rc.row;
+  const float m_y = rc.m_y;
+  const double thr = rc.thr;
+
+  // ---- octave histogram of the estimates ----
+  float* Hc = reinterpret_cast<float*>(work);
+#pragma unroll
+  for (int b = 0; b <= NOCT; ++b) Hc[b * NT + tid] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < OWN; ++j) {
+    const float p = __expf(dest(rc, x[j]));
+    Hc[(est_rank(p) >> 8) * NT + tid] += p;
+  }
+  csync();
+  for (int b = warp; b <= NOCT; b += NWARP) {
+    double v = 0.0;
+#pragma unroll
+    for (int q = 0; q < NT / 32; ++q) v += (double)Hc[b * NT + lane + 32 * q];
+    v = warp_sum_d(v);
+    if (lane == 0) S.oct[b] = v;
+  }
+  csync();
+  double Se = 0.0, Ee = 0.0;
+  for (int b = 0; b <= NOCT; ++b) {
+    Se += S.oct[b];
+    Ee += S.oct[b] * oct_d(b);
+  }
+  const double Th = thr * Se;
+  const double es = est_err(Se, Ee, m_y, 36, V);
+  const double rnd = 2.0 * ((4.0 * V + 16.0) * U53 * Se);
+  int bc = -1;                     // crossing octave; -1: top_p > 1, everything is kept
+  double cum = 0.0, Eb = 0.0;      // estimated mass (and |d| mass) of the octaves below it
+  if (thr > 0.0) {
+    for (int b = NOCT; b >= 0; --b) {
+      if (cum + S.oct[b] > Th) { bc = b; break; }
+      cum += S.oct[b];
+      Eb += S.oct[b] * oct_d(b);
+    }
+    if (bc < 0 || bc == NOCT) return ROW_GENERAL;
+  }
+
+  // ---- list job: octaves 0..bl, the deeper ones an estimated tail ----
+  if (thr > 0.0 && !forced) {
+    int bl = bc;
+    for (;;) {
+      double tl = 0.0, et = 0.0;
+      for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
+      if (tl + 2.0 * est_err(tl, et, m_y, 36, V) + thr * es + rnd < Th) break;
+      if (++bl >= NOCT) break;
+    }
+    double nb = 0.0;                              // count bound: p~ > 2^-(b+1) in octave b
+    for (int b = 0; b <= bl && b < NOCT; ++b) nb += S.oct[b] * exp2((double)(b + 1));
+    if (bl < NOCT && nb <= 2.0 * LCAP) {
+      unsigned long long mask = 0ull;
+      float xmx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < OWN; ++j) {
+        if ((est_rank(__expf(dest(rc, x[j]))) >> 8) <= bl) mask |= 1ull << j;
+        else xmx = fmaxf(xmx, x[j]);
+      }
+      int ng;
+      const int wpos = block_exscan_i32(__popcll(mask), S.redi, &ng);
+      if (ng <= LCAP) {
+        write_keys_mem(a.lkeys + (size_t)row * LCAP, rc, x, mask, wpos);
+        const float xm = block_reduce(xmx, MaxF(), S.redf);
+        if (tid == 0) {
+          RowJob& J = a.jobs[row];
+          double tl = 0.0, et = 0.0;
+          for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
+          fill_job(J, rc, JOB_K0, ng, 0);
+          J.tail = tl;
+          J.tail_err = est_err(tl, et, m_y, 36, V);
+          J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
+        }
+        if (a.out_logits) write_row(a, rc, x, true, 0u, 0ull);
+        return ROW_DONE;
+      }
+    }
+  }
+
+  // ---- the row kernel finishes the row ----
+  K0Oct O;
+  O.Se = Se; O.Ee = Ee; O.Th = Th; O.rnd = rnd; O.cum = cum; O.Eb = Eb; O.bc = bc;
+  return k0_big(a, rc, x, work, S, forced, O);
+}
+
 // One sampled or greedy row whose penalised elements are in x (this thread's
 // positions; `shift` is the row's misalignment in elements).
 __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& M, const float (&x)[OWN], int shift,
@@ -968,7 +1022,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
       a.out_ids[row] = b == 0xffffffffu ? 0 : (int)b;
       a.jobs[row].kind = JOB_NONE;
     }
-    if (a.out_logits) write_row(a, rc, x, false, 0u, 0ull);
+    if (a.out_logits) write_row_regs(a, rc, x, false);
     csync();
     return ROW_DONE;
   }
@@ -1030,7 +1084,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     J.tail_err = 0.0;
     J.ykex = 0u;
   }
-  if (a.out_logits) write_row(a, rc, x, true, 0u, 0ull);
+  if (a.out_logits) write_row_regs(a, rc, x, true);
   return ROW_DONE;
 }
 
