@@ -42,8 +42,8 @@ namespace c4s {
 
 constexpr int F_MAXV = 9212;              // widest row the fast path takes
 constexpr int OWN = 36;                   // row positions per row-kernel thread
-constexpr int LCAP = 512;                 // candidates per list
-constexpr int K_CHUNK = 8192;             // rows per launch sequence (list storage)
+constexpr int LCAP = 2048;                // candidates per list
+constexpr int K_CHUNK = 4096;             // rows per launch sequence (list storage)
 constexpr int NOCT = 24;                  // octaves of the estimate; bin NOCT = the rest
 constexpr int BIG_SORT = 128;             // crossing sub-bin capacity (one warp sort)
 constexpr int CAND_CAP = 2048;            // crossing-octave candidates
@@ -666,16 +666,14 @@ __device__ __noinline__ int k0_big(const Args& a, const RowCtx& rc, const float*
   const int row = rc.row;
   const float m_y = rc.m_y;
   const double thr = rc.thr;
-  const float* Hc = reinterpret_cast<const float*>(work);
   const int bc = O.bc;
   const double Se = O.Se, Ee = O.Ee, Th = O.Th, rnd = O.rnd, cum = O.cum, Eb = O.Eb;
   // survivor mass of this thread's elements in the octaves above the crossing one
   float hi = 0.0f;
-  {
-    const int btop = bc < 0 ? NOCT + 1 : bc;
-    for (int b = 0; b < btop; ++b) hi += Hc[b * NT + tid];
+  for (int j = 0; j < OWN; ++j) {
+    const float p = __expf(dest(rc, x[j]));
+    if (bc < 0 || (est_rank(p) >> 8) < bc) hi += p;
   }
-  csync();                                        // the columns are read before the area is reused
   unsigned long long kst = 0ull;
   int fc = -1;                                    // crossing rank: octave * 256 + sub-bin
   double Ed = Ee;                                 // |d| mass bound of the survivors
@@ -867,101 +865,14 @@ __device__ __noinline__ int k0_big(const Args& a, const RowCtx& rc, const float*
   return ROW_DONE;
 }
 
-// Rows without top-k (top-p over the whole row, sampling.cpp:42-71, and the
-// draw). One pass builds an octave histogram of the estimates (private
-// per-thread columns, no atomics) and locates the octave of the top-p
-// crossing. If the octaves down to it hold at most LCAP elements they become
-// a list job whose tail (the deeper octaves) is an estimate with a proven
-// bound that the list kernel checks exactly. Otherwise the row kernel
-// finishes the row: sub-bins and candidates of the crossing octave, an exact
-// sort of the crossing sub-bin, then the draw over per-thread survivor masses.
-__device__ __noinline__ int k0_row(const Args& a, const RowCtx& rc, const float* x, unsigned char* work,
-                                   Shared& S, bool forced) {
-  const int V = rc.V, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = rc.row;
-  const float m_y = rc.m_y;
-  const double thr = rc.thr;
-
-  // ---- octave histogram of the estimates ----
-  float* Hc = reinterpret_cast<float*>(work);
-#pragma unroll
-  for (int b = 0; b <= NOCT; ++b) Hc[b * NT + tid] = 0.0f;
-#pragma unroll
-  for (int j = 0; j < OWN; ++j) {
-    const float p = __expf(dest(rc, x[j]));
-    Hc[(est_rank(p) >> 8) * NT + tid] += p;
-  }
-  csync();
-  for (int b = warp; b <= NOCT; b += NWARP) {
-    double v = 0.0;
-#pragma unroll
-    for (int q = 0; q < NT / 32; ++q) v += (double)Hc[b * NT + lane + 32 * q];
-    v = warp_sum_d(v);
-    if (lane == 0) S.oct[b] = v;
-  }
-  csync();
-  double Se = 0.0, Ee = 0.0;
-  for (int b = 0; b <= NOCT; ++b) {
-    Se += S.oct[b];
-    Ee += S.oct[b] * oct_d(b);
-  }
-  const double Th = thr * Se;
-  const double es = est_err(Se, Ee, m_y, 36, V);
-  const double rnd = 2.0 * ((4.0 * V + 16.0) * U53 * Se);
-  int bc = -1;                     // crossing octave; -1: top_p > 1, everything is kept
-  double cum = 0.0, Eb = 0.0;      // estimated mass (and |d| mass) of the octaves below it
-  if (thr > 0.0) {
-    for (int b = NOCT; b >= 0; --b) {
-      if (cum + S.oct[b] > Th) { bc = b; break; }
-      cum += S.oct[b];
-      Eb += S.oct[b] * oct_d(b);
-    }
-    if (bc < 0 || bc == NOCT) return ROW_GENERAL;
-  }
-
-  // ---- list job: octaves 0..bl, the deeper ones an estimated tail ----
-  if (thr > 0.0 && !forced) {
-    int bl = bc;
-    for (;;) {
-      double tl = 0.0, et = 0.0;
-      for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
-      if (tl + 2.0 * est_err(tl, et, m_y, 36, V) + thr * es + rnd < Th) break;
-      if (++bl >= NOCT) break;
-    }
-    double nb = 0.0;                              // count bound: p~ > 2^-(b+1) in octave b
-    for (int b = 0; b <= bl && b < NOCT; ++b) nb += S.oct[b] * exp2((double)(b + 1));
-    if (bl < NOCT && nb <= 2.0 * LCAP) {
-      unsigned long long mask = 0ull;
-      float xmx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < OWN; ++j) {
-        if ((est_rank(__expf(dest(rc, x[j]))) >> 8) <= bl) mask |= 1ull << j;
-        else xmx = fmaxf(xmx, x[j]);
-      }
-      int ng;
-      const int wpos = block_exscan_i32(__popcll(mask), S.redi, &ng);
-      if (ng <= LCAP) {
-        write_keys_mem(a.lkeys + (size_t)row * LCAP, rc, x, mask, wpos);
-        const float xm = block_reduce(xmx, MaxF(), S.redf);
-        if (tid == 0) {
-          RowJob& J = a.jobs[row];
-          double tl = 0.0, et = 0.0;
-          for (int b = bl + 1; b <= NOCT; ++b) { tl += S.oct[b]; et += S.oct[b] * oct_d(b); }
-          fill_job(J, rc, JOB_K0, ng, 0);
-          J.tail = tl;
-          J.tail_err = est_err(tl, et, m_y, 36, V);
-          J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
-        }
-        if (a.out_logits) write_row(a, rc, x, true, 0u, 0ull);
-        return ROW_DONE;
-      }
-    }
-  }
-
-  // ---- the row kernel finishes the row ----
-  K0Oct O;
-  O.Se = Se; O.Ee = Ee; O.Th = Th; O.rnd = rnd; O.cum = cum; O.Eb = Eb; O.bc = bc;
-  return k0_big(a, rc, x, work, S, forced, O);
+// Fixed-point octave mass of an estimate p (its octave b = est_rank(p) >> 8):
+// p * 2^(b+20), truncated, from the float's bits. Truncation loses less than
+// 2^-(b+20) per element, i.e. below 2^-19 of any element in octaves < NOCT.
+__device__ __forceinline__ unsigned oct_fix(float p, int b) {
+  const unsigned u = __float_as_uint(p);
+  const int sh = 130 - (int)(u >> 23) - b;        // 23 - 20 - (exponent + b)
+  const unsigned m = (u & 0x007fffffu) | 0x00800000u;
+  return (u == 0u || sh > 31) ? 0u : (m >> max(sh, 0));
 }
 
 // One sampled or greedy row whose penalised elements are in x (this thread's
@@ -1045,12 +956,99 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     rc.u = (double)rc.u53 * 1.1102230246251565e-16;   // (x>>11) / 2^53, exact
   }
   if (!do_k) {
+    // ---- rows without top-k (top-p over the whole row, sampling.cpp:42-71) ----
     if (rc.thr == 0.0) return ROW_GENERAL;
+    // octave histogram of the estimates: per-warp fixed-point bins (exact adds)
+    unsigned* Hw = reinterpret_cast<unsigned*>(work);
+    Hw[warp * 32 + lane] = 0u;
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < OWN; ++j) {
+      const float p = __expf(dest(rc, x[j]));
+      const int b = est_rank(p) >> 8;
+      atomicAdd(&Hw[warp * 32 + b], oct_fix(p, b));
+    }
+    csync();
+    // every warp: lane b holds octave b's mass; suffix sums give the mass below
+    // each octave, ballots the crossing octave and the list's last octave
+    double o = 0.0;
+    if (lane <= NOCT) {
+      unsigned long long qs = 0ull;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) qs += Hw[w * 32 + lane];
+      o = ldexp((double)qs, -(lane + 20));
+    }
+    const double w = o * oct_d(lane <= NOCT ? lane : NOCT);
+    double suf = o, wsuf = w;                       // sums over octaves >= lane
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const double t1 = __shfl_down_sync(FULL, suf, off), t2 = __shfl_down_sync(FULL, wsuf, off);
+      if (lane + off < 32) { suf += t1; wsuf += t2; }
+    }
+    double pre = o * ldexp(1.0, lane + 1);          // count bound of octaves <= lane
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const double t = __shfl_up_sync(FULL, pre, off);
+      if (lane >= off) pre += t;
+    }
+    const double Se = __shfl_sync(FULL, suf, 0), Ee = __shfl_sync(FULL, wsuf, 0);
+    const double below = __shfl_down_sync(FULL, suf, 1), wbelow = __shfl_down_sync(FULL, wsuf, 1);
+    const double blw = lane < 31 ? below : 0.0, wblw = lane < 31 ? wbelow : 0.0;   // octaves > lane
+    K0Oct O;
+    O.Se = Se;
+    O.Ee = Ee;
+    O.Th = rc.thr * Se;
+    O.rnd = 2.0 * ((4.0 * V + 16.0) * U53 * Se);
+    const double es = est_err(Se, Ee, rc.m_y, 33, V);
+    O.bc = -1;
+    O.cum = 0.0;
+    O.Eb = 0.0;
+    int bl = -1;
+    if (rc.thr > 0.0) {
+      // crossing octave: suffix sum (from the deep end) first exceeds Th
+      const unsigned cr = __ballot_sync(FULL, lane <= NOCT && suf > O.Th);
+      O.bc = cr ? 31 - __clz(cr) : -1;
+      if (O.bc < 0 || O.bc == NOCT) return ROW_GENERAL;
+      O.cum = __shfl_sync(FULL, blw, O.bc);
+      O.Eb = __shfl_sync(FULL, wblw, O.bc);
+      // the list: octaves 0..bl, bl >= bc the first whose tail is clearly below Th
+      const bool okl = lane >= O.bc && lane < NOCT &&
+                       blw + 2.0 * est_err(blw, wblw, rc.m_y, 33, V) + rc.thr * es + O.rnd < O.Th;
+      const unsigned lb = __ballot_sync(FULL, okl);
+      bl = lb ? __ffs(lb) - 1 : -1;
+    }
+    const double nb = bl >= 0 ? __shfl_sync(FULL, pre, bl) : 1e300;
+    if (bl >= 0 && !forced && nb <= 2.0 * LCAP) {
+      unsigned long long mask = 0ull;
+      float xmx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < OWN; ++j) {
+        if ((est_rank(__expf(dest(rc, x[j]))) >> 8) <= bl) mask |= 1ull << j;
+        else xmx = fmaxf(xmx, x[j]);
+      }
+      int ng;
+      const int wpos = block_exscan_i32(__popcll(mask), S.redi, &ng);
+      if (ng <= LCAP) {
+        write_keys(a.lkeys + (size_t)row * LCAP, rc, x, mask, wpos);
+        const float xm = block_reduce(xmx, MaxF(), S.redf);
+        const double tl = __shfl_sync(FULL, blw, bl), et = __shfl_sync(FULL, wblw, bl);
+        if (tid == 0) {
+          RowJob& J = a.jobs[row];
+          fill_job(J, rc, JOB_K0, ng, 0);
+          J.tail = tl;
+          J.tail_err = est_err(tl, et, rc.m_y, 33, V);
+          J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
+        }
+        if (a.out_logits) write_row_regs(a, rc, x, true);
+        return ROW_DONE;
+      }
+    }
+    csync();                                        // the bins are read before the area is reused
     // the copy keeps x itself in registers: only xc's address reaches the call
     float xc[OWN];
 #pragma unroll
     for (int j = 0; j < OWN; ++j) xc[j] = x[j];
-    return k0_row(a, rc, xc, work, S, forced);
+    return k0_big(a, rc, xc, work, S, forced, O);
   }
 
   // ---- top-k rows: candidates >= the maxima threshold form the list ----
@@ -1146,7 +1144,11 @@ __global__ void __launch_bounds__(NT, 4) row_kernel(Args a) {
     else if (tid == 5) cp_async8(&ms.rng, a.rng + r);
     else if (tid == 6) act_pend = a.active ? (int)a.active[r] : 1;
   };
+  // rows are handed out dynamically (the first G statically): a CTA that
+  // meets slow rows takes fewer of them
+  unsigned* row_ctr = a.defer_cnt + 2;
   const int r0 = blockIdx.x;
+  if (tid == 0) S.nrow[0] = G + (int)atomicAdd(row_ctr, 1u);
   issue_meta(r0, meta[0]);
   cp_async_commit();
   if (tid == 6 && r0 < a.B) meta[0].active = act_pend;
@@ -1157,10 +1159,10 @@ __global__ void __launch_bounds__(NT, 4) row_kernel(Args a) {
   if (r0 < a.B && meta[0].active) sg = stage_row(a.logits + (long long)r0 * a.ld, V, rowbuf, &S.bar);
 
   int j = 0;
-  for (int row = r0; row < a.B; row += G, ++j) {
+  for (int row = r0; row < a.B; ++j) {
     const MetaSlot& cur = meta[j & 1];
     MetaSlot& nxt = meta[(j + 1) & 1];
-    const int next = row + G;
+    const int next = S.nrow[j & 1];
     issue_meta(next, nxt);
     cp_async_commit();
     if (tid == 6 && next < a.B) nxt.active = act_pend;
@@ -1218,12 +1220,14 @@ __global__ void __launch_bounds__(NT, 4) row_kernel(Args a) {
       a.out_ids[row] = -1;
       a.jobs[row].kind = JOB_NONE;
     }
+    if (tid == 0) S.nrow[(j + 1) & 1] = next < a.B ? G + (int)atomicAdd(row_ctr, 1u) : a.B;   // the row after next
     cp_async_wait<0>();
     csync();                                       // next metadata visible
     if (!staged_next) {
       sg = Staged{0, 0, -1, 0.0f};
       if (next < a.B && nxt.active) sg = stage_row(a.logits + (long long)next * a.ld, V, rowbuf, &S.bar);
     }
+    row = next;
   }
 }
 
@@ -1253,6 +1257,7 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
     if (atomicAdd(&a.defer_cnt[1], 1u) == gridDim.x - 1) {
       a.defer_cnt[0] = 0u;
       a.defer_cnt[1] = 0u;
+      a.defer_cnt[2] = 0u;                          // the row kernel's row counter
     }
   }
 }

@@ -43,7 +43,7 @@ struct Args {
   double* lpv;                  // [B][LCAP] their probabilities
   unsigned long long* lsb;      // [B][LCAP] sort buffer of the exact fallback
   int* defer_rows;              // rows handed to the general path
-  unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done
+  unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done, [2] row counter
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -82,6 +82,7 @@ struct Shared {
   int ndq;
   int abort_all;                // a bounded wait gave up: stop after this row
   double oct[32];               // octave masses of the estimate
+  int nrow[2];                  // row kernel: the next row of this CTA (by iteration parity)
   float fbefore;                // mass of the sub-bins below the crossing one
 };
 

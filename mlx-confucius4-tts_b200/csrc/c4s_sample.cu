@@ -274,8 +274,8 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lpv, nl * sizeof(double));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (size_t)c4s::K_CHUNK * sizeof(int));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, 2 * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, 2 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, 4 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, 4 * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_default_params, 0, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(unsigned));
