@@ -165,6 +165,30 @@ int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors,
                    uint64_t* counters /* [C4S_NUM_COUNTERS] or NULL */,
                    int32_t reset, void* stream);
 
+/* c4s_sample without a context, for callers that must not allocate device
+ * memory at all. No counterpart in the reference (whose sampling stage has no
+ * device state); it exists so that a caller can sample before, or without,
+ * creating a context.
+ *   - Same arguments and results as c4s_sample (no processed logits); it runs
+ *     the general kernel on at most 16 CTAs.
+ *   - Scratch is a file-scope device array of C4S_STATIC_MAX_VOCAB * 16 keys
+ *     (2 MiB): V above C4S_STATIC_MAX_VOCAB returns C4S_ERR_CAPACITY.
+ *   - Nothing is allocated, by this call or the library. The first call on a
+ *     device (the calling thread's current device) looks up the array's device
+ *     address and sets the kernel's shared-memory attribute; make that first
+ *     call before any stream capture.
+ *   - All calls on a device share the array: calls that overlap in time (on
+ *     different streams or threads) race and must be serialised by the caller.
+ *   - The device error flags and path counters that the kernel writes are
+ *     cleared (stream-ordered) at the start of every call; they are not
+ *     reported: validate history offsets before calling.                    */
+#define C4S_STATIC_MAX_VOCAB 16384
+int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld,
+                      const int32_t* d_hist, const int64_t* d_hist_off,
+                      int64_t hist_total, const c4s_row_params* d_params,
+                      int32_t params_stride, uint64_t* d_rng,
+                      const uint8_t* d_active, int32_t* d_out_ids, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -33,6 +33,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/c4s_sampling.h"
@@ -64,6 +65,15 @@ __global__ void __launch_bounds__(NT, 4) rows_kernel(Args a) {
     if (!general_row(a, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) return;
   }
 }
+
+// Scratch of c4s_sample_static(), at file scope so that the entry point
+// allocates nothing: STATIC_CTAS slabs of the general path's exact top-p sort
+// (up to STATIC_MAX_VOCAB keys each, 2 MiB in all), and the error-flag word and
+// path counters that the kernel writes.
+constexpr int STATIC_CTAS = 16;
+constexpr int STATIC_MAX_VOCAB = 16384;
+static __device__ __align__(256) unsigned long long g_static_scratch[(size_t)STATIC_CTAS * STATIC_MAX_VOCAB];
+static __device__ __align__(256) unsigned long long g_static_status[1 + C4S_NUM_COUNTERS];
 
 __global__ void seed_kernel(unsigned long long* s, int B, unsigned long long seed, long long off) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -381,6 +391,66 @@ int c4s_argmax(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V, int64_
   a.out_ids = d_out_ids;
   a.mode = c4s::MODE_ARGMAX;
   return launch_rows(ctx, a, stream);
+}
+
+int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld, const int32_t* d_hist,
+                      const int64_t* d_hist_off, int64_t hist_total, const c4s_row_params* d_params,
+                      int32_t params_stride, uint64_t* d_rng, const uint8_t* d_active, int32_t* d_out_ids,
+                      void* stream) {
+  if (B < 0 || V < 1 || ld < V) return C4S_ERR_INVALID;
+  if (V > C4S_STATIC_MAX_VOCAB) return C4S_ERR_CAPACITY;   // the scratch slabs hold next_pow2(V) keys
+  if (B == 0) return C4S_OK;
+  if (!d_logits || !d_params || !d_rng || !d_out_ids) return C4S_ERR_INVALID;
+  if (params_stride != 0 && params_stride != 1) return C4S_ERR_INVALID;
+  if (d_hist_off && (!d_hist && hist_total > 0)) return C4S_ERR_INVALID;
+  if (hist_total < 0 || ((uintptr_t)d_logits & 3)) return C4S_ERR_INVALID;
+  static_assert(C4S_STATIC_MAX_VOCAB == c4s::STATIC_MAX_VOCAB, "header and scratch agree");
+  // Once per device, with that device current: the scratch's device address
+  // and the general kernel's shared-memory attribute (no allocation).
+  static std::mutex mu;
+  static unsigned long long* scratch_of[64] = {};
+  static unsigned long long* status_of[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return C4S_ERR_CUDA;
+  unsigned long long* scratch = nullptr;
+  unsigned long long* status = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!scratch_of[dev]) {
+      unsigned long long *p = nullptr, *q = nullptr;
+      if (cudaGetSymbolAddress((void**)&p, c4s::g_static_scratch) != cudaSuccess) return C4S_ERR_CUDA;
+      if (cudaGetSymbolAddress((void**)&q, c4s::g_static_status) != cudaSuccess) return C4S_ERR_CUDA;
+      if (cudaFuncSetAttribute(c4s::rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)c4s::layout_for(c4s::MAX_VOCAB).total) != cudaSuccess)
+        return C4S_ERR_CUDA;
+      status_of[dev] = q;
+      scratch_of[dev] = p;
+    }
+    scratch = scratch_of[dev];
+    status = status_of[dev];
+  }
+  // the error flags and counters start at zero on every call
+  if (cudaMemsetAsync(status, 0, sizeof(c4s::g_static_status), (cudaStream_t)stream) != cudaSuccess)
+    return C4S_ERR_CUDA;
+  c4s::Args a{};
+  a.logits = d_logits;
+  a.B = B; a.V = V; a.ld = ld;
+  a.hist = d_hist; a.hist_off = reinterpret_cast<const long long*>(d_hist_off); a.hist_total = hist_total;
+  a.params = d_params; a.params_stride = params_stride;
+  a.rng = reinterpret_cast<unsigned long long*>(d_rng);
+  a.active = d_active;
+  a.out_ids = d_out_ids;
+  a.mode = c4s::MODE_SAMPLE;
+  int lg = 0;
+  while ((1 << lg) < V) ++lg;
+  a.qscale = std::ldexp(1.0, 62 - std::max(lg, 1));
+  a.scratch = scratch;
+  a.scratch_stride = 1 << lg;
+  a.errflags = reinterpret_cast<unsigned*>(status);
+  a.counters = status + 1;
+  const int grid = std::min(B, c4s::STATIC_CTAS);
+  c4s::rows_kernel<<<grid, c4s::NT, c4s::layout_for(V).total, (cudaStream_t)stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? C4S_OK : C4S_ERR_CUDA;
 }
 
 int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors, uint64_t* counters, int32_t reset, void* stream) {
