@@ -44,7 +44,7 @@ constexpr int F_MAXV = 9212;              // widest row the fast path takes
 constexpr int OWN = 36;                   // row positions per row-kernel thread
 constexpr int LCAP = 2048;                // candidates per list
 constexpr int K_CHUNK = 4096;             // rows per launch sequence (list storage)
-constexpr int NOCT = 24;                  // octaves of the estimate; bin NOCT = the rest
+constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int BIG_SORT = 128;             // crossing sub-bin capacity (one warp sort)
 constexpr int CAND_CAP = 2048;            // crossing-octave candidates
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
@@ -1016,6 +1016,16 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
                        blw + 2.0 * est_err(blw, wblw, rc.m_y, 33, V) + rc.thr * es + O.rnd < O.Th;
       const unsigned lb = __ballot_sync(FULL, okl);
       bl = lb ? __ffs(lb) - 1 : -1;
+      if (bl >= 0) {
+        // go deeper while the list stays short, until the tail is below Th/64:
+        // the list kernel's decision band (which scales with the tail) then
+        // rarely reaches the crossing element
+        const unsigned small = __ballot_sync(FULL, lane >= bl && lane < NOCT && blw <= O.Th * 0.015625);
+        const unsigned fits = __ballot_sync(FULL, lane >= bl && lane < NOCT && pre <= 0.5 * LCAP);
+        const int bt = small ? __ffs(small) - 1 : NOCT - 1;
+        const int bf = fits ? 31 - __clz(fits) : bl;
+        bl = max(bl, min(bt, bf));
+      }
     }
     const double nb = bl >= 0 ? __shfl_sync(FULL, pre, bl) : 1e300;
     if (bl >= 0 && !forced && nb <= 2.0 * LCAP) {
@@ -1122,7 +1132,7 @@ __device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf
   return st;
 }
 
-__global__ void __launch_bounds__(NT, 4) row_kernel(Args a) {
+__global__ void __launch_bounds__(NT, 2) row_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char dsm[];   // the staged row, then scratch
   __shared__ Shared S;
   __shared__ unsigned bm[(F_MAXV + 31) / 32 + 4];        // penalty de-duplication bitmap
