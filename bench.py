@@ -115,6 +115,21 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def profiled_traffic(B):
+    """DRAM bytes (read + write) of one row-kernel launch at B rows, from the
+    committed ncu summary of the same workload (scaled by rows if B differs)."""
+    path = os.path.join(ROOT, "profiles", "row_kernel_config2_dram.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    _, v, rows = line.split()
+                    return float(v) * B / float(rows)
+    except OSError:
+        pass
+    return None
+
+
 def phys_index(local):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -276,10 +291,27 @@ def run_ours(args):
     value = rows_total / (ms / 1e3)
     err, counters = ctx.status(reset=True)
 
-    # ---- roofline of the sampling kernel (the only kernel in the timed region) ----
+    # ---- per-kernel device time: the same K steps again with CUDA events between
+    # the launches (row kernel -> list kernel -> general path, per 4096-row chunk) ----
+    ctx.kernel_timing(True)
+    ctx.kernel_times(reset=True)
+    for s in range(args.steps):
+        step(s)
+    kt = ctx.kernel_times(reset=True)
+    ctx.kernel_timing(False)
+    launches_per_step = sum(n for _, n in kt.values()) // args.steps
+    kernels = {k: {"ms_per_launch": ms / max(n, 1), "launches": n,
+                   "share": ms / max(sum(m for m, _ in kt.values()), 1e-12)} for k, (ms, n) in kt.items()}
+
+    # ---- roofline of the dominant kernel: the row kernel moves every logit,
+    # history id and per-row record (the list and general kernels only touch
+    # candidate lists) ----
     alg_bytes = float(np.mean([p["bytes"] for p in pool]))
     hbm_peak, peak_kind = peaks()
-    achieved_gbs = alg_bytes / (ms_per_step / 1e3) / 1e9
+    row_ms = kernels["row_kernel"]["ms_per_launch"]
+    achieved_gbs = alg_bytes / (row_ms / 1e3) / 1e9
+    step_gbs = alg_bytes / (ms_per_step / 1e3) / 1e9
+    traffic = profiled_traffic(B)
 
     # ---- e2e through the public host-buffer API ----
     e2e = None
@@ -378,11 +410,13 @@ def run_ours(args):
             "b1_p50_us": None if b1 is None else b1["graph_p50_us"],
             "b1": b1,
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved_gbs / hbm_peak, "traffic": None,
-                         "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes},
+                         "frac": achieved_gbs / hbm_peak, "traffic": traffic,
+                         "kernel": "row_kernel", "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes,
+                         "whole_step_achieved": step_gbs, "whole_step_frac": step_gbs / hbm_peak},
+            "kernels": kernels,
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "device_errors": err,
             "path_counters": counters,

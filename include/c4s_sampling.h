@@ -76,6 +76,7 @@ typedef struct c4s_row_params {
  * can check them on ordinary inputs.                                        */
 #define C4S_DEBUG_FORCE_EXACT 1 /* exact sequential sums; radix-select top-k   */
 #define C4S_DEBUG_FORCE_BINS 2  /* binned top-p and row-pass draw paths        */
+#define C4S_DEBUG_FORCE_REFINE 4 /* no-top-k list rows: exact tail in the general kernel */
 
 /* Device-side error bits reported by c4s_get_status().                     */
 #define C4S_DEVERR_HIST_RANGE 1u /* a row's history offsets were out of range */
@@ -164,6 +165,16 @@ int c4s_argmax(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V,
 int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors,
                    uint64_t* counters /* [C4S_NUM_COUNTERS] or NULL */,
                    int32_t reset, void* stream);
+
+/* Measurement only; no counterpart in the reference. While enabled, every
+ * c4s_sample call that takes the fast path records CUDA events on its stream
+ * around its three kernels (row, list, general; per chunk of 4096 rows).
+ * c4s_kernel_times waits for them and returns the summed device times in
+ * milliseconds and the number of launches of each kernel in ms[3] /
+ * launches[3]; reset forgets the recorded calls. Not for use while a stream
+ * is being captured.                                                        */
+int c4s_kernel_timing(c4s_ctx* ctx, int32_t enable);
+int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset);
 
 /* c4s_sample without a context, for callers that must not allocate device
  * memory at all. No counterpart in the reference (whose sampling stage has no

@@ -52,7 +52,7 @@ static_assert(OWN * NT >= F_MAXV + 3, "the ownership blocks cover every row posi
 static_assert(OWN <= 64, "per-thread candidate masks are 64 bits");
 
 enum { JOB_NONE = 0, JOB_TOPK = 1, JOB_K0 = 2, JOB_DEFER = 3 };
-enum { RES_DONE = 0, RES_DEFER = 1 };
+enum { RES_DONE = 0, RES_DEFER = 1, RES_REFINE = 2 };
 
 // Per-row job record: written by the row kernel, finished by the list kernel.
 struct __align__(16) RowJob {
@@ -234,12 +234,150 @@ __device__ __forceinline__ void defer_row(const Args& a, int row) {
 // List kernel: one warp per row
 // ===========================================================================
 
-// Warp bitonic sort (ascending) of np (power of two, <= LCAP) keys.
-__device__ void warp_bitonic(unsigned long long* b, int np) {
-  const int lane = threadIdx.x & 31;
+// Reduction scratch of a list job run by a whole CTA.
+struct LRed {
+  double d[NWARP];
+  unsigned long long q[NWARP];
+  int i[NWARP];
+  int e;
+  double x, y;
+};
+
+// A list job runs on one warp (short lists) or on the whole CTA (long ones);
+// LG<CTA> gives its group size, rank, barrier and group-wide reductions. All
+// members of the group call each function; every member gets the same result.
+template <bool CTA>
+struct LG {
+  static constexpr int N = CTA ? NT : 32;
+  __device__ static int rank() { return CTA ? (int)threadIdx.x : (int)(threadIdx.x & 31); }
+  __device__ static void sync() {
+    if (CTA) csync(); else __syncwarp();
+  }
+  __device__ static double sum(double v, LRed& R) {
+    v = warp_sum_d(v);
+    if (!CTA) return v;
+    if ((threadIdx.x & 31) == 0) R.d[threadIdx.x >> 5] = v;
+    csync();
+    double s = 0.0;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) s += R.d[w];
+    csync();
+    return s;
+  }
+  __device__ static int add(int v, LRed& R) {
+    v = __reduce_add_sync(FULL, v);
+    if (!CTA) return v;
+    if ((threadIdx.x & 31) == 0) R.i[threadIdx.x >> 5] = v;
+    csync();
+    int s = 0;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) s += R.i[w];
+    csync();
+    return s;
+  }
+  __device__ static unsigned long long qmin(unsigned long long v, LRed& R) {
+    v = warp_min_u64(v);
+    if (!CTA) return v;
+    if ((threadIdx.x & 31) == 0) R.q[threadIdx.x >> 5] = v;
+    csync();
+    unsigned long long s = R.q[0];
+#pragma unroll
+    for (int w = 1; w < NWARP; ++w) s = R.q[w] < s ? R.q[w] : s;
+    csync();
+    return s;
+  }
+  __device__ static unsigned long long qmax(unsigned long long v, LRed& R) {
+    v = warp_max_u64(v);
+    if (!CTA) return v;
+    if ((threadIdx.x & 31) == 0) R.q[threadIdx.x >> 5] = v;
+    csync();
+    unsigned long long s = R.q[0];
+#pragma unroll
+    for (int w = 1; w < NWARP; ++w) s = R.q[w] > s ? R.q[w] : s;
+    csync();
+    return s;
+  }
+  // Exclusive scan in rank order; *tot gets the group total.
+  __device__ static int exscan_i(int v, LRed& R, int* tot) {
+    const int lane = threadIdx.x & 31;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(FULL, x, o);
+      if (lane >= o) x += y;
+    }
+    if (!CTA) {
+      *tot = __shfl_sync(FULL, x, 31);
+      return x - v;
+    }
+    const int warp = threadIdx.x >> 5;
+    if (lane == 31) R.i[warp] = x;
+    csync();
+    int base = 0, t = 0;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) {
+      if (w < warp) base += R.i[w];
+      t += R.i[w];
+    }
+    csync();
+    *tot = t;
+    return base + x - v;
+  }
+  __device__ static double exscan_d(double v, LRed& R, double* tot) {
+    const int lane = threadIdx.x & 31;
+    double x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(FULL, x, o);
+      if (lane >= o) x += y;
+    }
+    if (!CTA) {
+      *tot = __shfl_sync(FULL, x, 31);
+      return x - v;
+    }
+    const int warp = threadIdx.x >> 5;
+    if (lane == 31) R.d[warp] = x;
+    csync();
+    double base = 0.0, t = 0.0;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) {
+      if (w < warp) base += R.d[w];
+      t += R.d[w];
+    }
+    csync();
+    *tot = t;
+    return base + x - v;
+  }
+  // Value of rank `src` (uniform) to every member.
+  __device__ static int bcast_i(int v, int src, LRed& R) {
+    if (!CTA) return __shfl_sync(FULL, v, src);
+    if ((int)threadIdx.x == src) R.e = v;
+    csync();
+    const int r = R.e;
+    csync();
+    return r;
+  }
+  __device__ static void bcast_2d(double& a, double& b, int src, LRed& R) {
+    if (!CTA) {
+      a = __shfl_sync(FULL, a, src);
+      b = __shfl_sync(FULL, b, src);
+      return;
+    }
+    if ((int)threadIdx.x == src) { R.x = a; R.y = b; }
+    csync();
+    a = R.x;
+    b = R.y;
+    csync();
+  }
+};
+
+// Ascending bitonic sort of np (power of two) keys by the group.
+template <bool CTA>
+__device__ void group_bitonic(unsigned long long* b, int np) {
+  using G = LG<CTA>;
   for (int k = 2; k <= np; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = lane; i < np; i += 32) {
+      for (int i = G::rank(); i < np; i += G::N) {
         const int ixj = i ^ j;
         if (ixj > i) {
           const unsigned long long x = b[i], y = b[ixj];
@@ -247,76 +385,229 @@ __device__ void warp_bitonic(unsigned long long* b, int np) {
           if ((x > y) == up) { b[i] = y; b[ixj] = x; }
         }
       }
-      __syncwarp();
+      G::sync();
     }
   }
 }
 
-// One list job. keys[0..n): ckey(y, i) of the candidates in index order
-// (list position = index order); pv: their probabilities by position (zero
-// for candidates that top-k removes); sb: sort buffer of the exact fallback.
-__device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const unsigned long long* keys, double* pv,
-                                      unsigned long long* sb) {
+// Radix searches of a list job over the value keys that share `prefix` above
+// bit b0 (8 bits per pass, histogram `hist` of 256 bins in shared memory).
+// topk: the largest v with count(vkey >= v) >= k, i.e. the k-th largest key.
+template <bool CTA>
+__device__ __forceinline__ unsigned radix_kth(const unsigned* __restrict__ vk, int n, unsigned prefix, int b0, int k,
+                                              unsigned long long* __restrict__ hist, LRed& R) {
+  using G = LG<CTA>;
+  unsigned* h = reinterpret_cast<unsigned*>(hist);
   const int lane = threadIdx.x & 31;
+  int need = k;
+  for (int hi = b0; hi >= 0;) {
+    const int w = hi + 1 < 8 ? hi + 1 : 8;
+    const int lo = hi - w + 1;
+    const unsigned pmask = hi >= 31 ? 0u : ~((2u << hi) - 1u);
+    for (int i = G::rank(); i < 256; i += G::N) h[i] = 0u;
+    G::sync();
+    for (int e = G::rank(); e < n; e += G::N) {
+      const unsigned v = vk[e];
+      if ((v & pmask) == prefix) atomicAdd(&h[(v >> lo) & 255u], 1u);
+    }
+    G::sync();
+    if (!CTA || threadIdx.x < 32) {
+      // lane l holds bins 8l..8l+7; suffix counts C(d) = #(digits >= d)
+      unsigned c[8], s = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { c[j] = h[8 * lane + j]; s += c[j]; }
+      unsigned above = s;                             // inclusive suffix over lanes >= lane
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_down_sync(FULL, above, o);
+        if (lane + o < 32) above += y;
+      }
+      unsigned run = above - s;                       // digits above this lane's bins
+      int q = 0, dl = -1;
+      unsigned nneed = 0u;
+#pragma unroll
+      for (int j = 7; j >= 0; --j) {
+        run += c[j];                                  // C(8 lane + j)
+        if (run >= (unsigned)need) {
+          ++q;
+          if (dl < 0) { dl = 8 * lane + j; nneed = (unsigned)need - (run - c[j]); }
+        }
+      }
+      // the qualifying digits are 0..d*; d* is the largest, found on one lane
+      const int D = __reduce_add_sync(FULL, q);
+      const int ds = D > 0 ? D - 1 : 0;
+      const unsigned src = __ballot_sync(FULL, dl == ds);
+      const int sl = src ? __ffs(src) - 1 : 0;
+      const unsigned nn = __shfl_sync(FULL, D > 0 ? nneed : (unsigned)need, sl);
+      if (CTA) {
+        if (threadIdx.x == 0) { R.e = ds; R.i[0] = (int)nn; }
+      } else {
+        prefix |= (unsigned)ds << lo;
+        need = (int)nn;
+      }
+    }
+    if (CTA) {
+      csync();
+      prefix |= (unsigned)R.e << lo;
+      need = R.i[0];
+      csync();
+    }
+    hi = lo - 1;
+  }
+  return prefix;
+}
+
+// mass: the largest v with base + sum(pv[e] : vkey(e) < v) <= Th (v = prefix if
+// none), where base is the mass below the searched range. The bins add p in
+// 2^-52 fixed point (native 64-bit shared atomics; p <= 1 and n <= 2048); the
+// search only has to land on the crossing value, which the caller then checks
+// with double sums and their error band.
+template <bool CTA>
+__device__ __forceinline__ unsigned radix_mass(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
+                                               unsigned prefix, int b0, double base, double Th,
+                                               unsigned long long* __restrict__ hist, LRed& R) {
+  using G = LG<CTA>;
+  unsigned long long* h = hist;
+  const int lane = threadIdx.x & 31;
+  for (int hi = b0; hi >= 0;) {
+    const int w = hi + 1 < 8 ? hi + 1 : 8;
+    const int lo = hi - w + 1;
+    const unsigned pmask = hi >= 31 ? 0u : ~((2u << hi) - 1u);
+    for (int i = G::rank(); i < 256; i += G::N) h[i] = 0ull;
+    G::sync();
+    for (int e = G::rank(); e < n; e += G::N) {
+      const unsigned v = vk[e];
+      const double p = pv[e];
+      if ((v & pmask) == prefix && p != 0.0)
+        atomicAdd(&h[(v >> lo) & 255u], __double2ull_rn(p * 4503599627370496.0));
+    }
+    G::sync();
+    if (!CTA || threadIdx.x < 32) {
+      // lane l holds bins 8l..8l+7; E(d) = mass of digits < d
+      double m[8], s = 0.0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { m[j] = (double)h[8 * lane + j] * 2.220446049250313e-16; s += m[j]; }
+      double incl = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += y;
+      }
+      double run = incl - s;
+      int q = 0;
+      double ed = 0.0;
+      int dl = -1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (base + run <= Th) { ++q; dl = 8 * lane + j; ed = run; }
+        run += m[j];
+      }
+      const int D = __reduce_add_sync(FULL, q);
+      const int ds = D > 0 ? D - 1 : 0;
+      const unsigned src = __ballot_sync(FULL, dl == ds);
+      const int sl = src ? __ffs(src) - 1 : 0;
+      const double e = __shfl_sync(FULL, ed, sl);
+      if (CTA) {
+        if (threadIdx.x == 0) { R.e = ds; R.x = D > 0 ? e : 0.0; }
+      } else {
+        prefix |= (unsigned)ds << lo;
+        base += D > 0 ? e : 0.0;
+      }
+    }
+    if (CTA) {
+      csync();
+      prefix |= (unsigned)R.e << lo;
+      base += R.x;
+      csync();
+    }
+    hi = lo - 1;
+  }
+  return prefix;
+}
+
+// One list job. keys[0..n) (global): ckey(y, i) of the candidates in index
+// order (list position = index order). The job stages their value keys into
+// vk[] and computes their probabilities into pv[] (zero for candidates that
+// top-k removes), both in shared memory, so that its passes stay on chip;
+// pvg / sb (global) serve the rare exact fallback. Run by one warp (CTA =
+// false) or by the whole CTA (long lists). With `refine` (the general kernel,
+// after replacing an estimated tail by the exact one) a row that cannot be
+// decided is not handed back: the caller finishes it on the general path.
+// Returns whether the row is finished.
+template <bool CTA>
+__device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
+                                         const unsigned long long* __restrict__ keys, unsigned long long* sb,
+                                         unsigned* __restrict__ vk, double* __restrict__ pv,
+                                         unsigned long long* __restrict__ hist, bool refine, LRed& R) {
+  using G = LG<CTA>;
+  const int r0 = G::rank();
+  constexpr int GN = G::N;
   const int n = J.n, V = a.V, k = J.k;
   const float m_y = J.m_y;
   const bool k0 = J.kind == JOB_K0;
   const bool forced = (a.debug & C4S_DEBUG_FORCE_BINS) != 0;
-  auto vkey = [&](int e) { return (unsigned)(keys[e] >> 32); };
-  auto hand_back = [&]() {
-    if (lane == 0) {
-      J.status = RES_DEFER;
+  auto hand_back = [&](int st) {
+    if (r0 == 0 && !refine) {
+      J.status = st;
       defer_row(a, row);
     }
   };
-  unsigned vmin = 0xffffffffu, vmax = 0u;
-  for (int e = lane; e < n; e += 32) {
-    const unsigned v = vkey(e);
-    vmin = min(vmin, v);
-    vmax = max(vmax, v);
+  // stage the value keys: eight loads in flight per member
+  unsigned long long vmin = ~0ull, vmax = 0ull;
+  for (int e0 = r0; e0 < n; e0 += 8 * GN) {
+    unsigned v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = e0 + q * GN;
+      v[q] = e < n ? (unsigned)(__ldcg(keys + e) >> 32) : 0u;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = e0 + q * GN;
+      if (e < n) {
+        vk[e] = v[q];
+        vmin = v[q] < vmin ? v[q] : vmin;
+        vmax = v[q] > vmax ? v[q] : vmax;
+      }
+    }
   }
-  vmin = __reduce_min_sync(FULL, vmin);
-  vmax = __reduce_max_sync(FULL, vmax);
+  vmin = G::qmin(vmin, R);
+  vmax = G::qmax(vmax, R);
+  G::sync();
   // no-top-k list: everything below it must be strictly smaller in value
-  if (k0 && J.ykex >= vmin) { hand_back(); return; }
+  if (k0 && J.ykex >= vmin) { hand_back(RES_DEFER); return false; }
+  if (k0 && !refine && (a.debug & C4S_DEBUG_FORCE_REFINE)) { hand_back(RES_REFINE); return false; }
 
   // ---- top-k threshold: the k-th largest value key (sampling.cpp:30-40) ----
-  unsigned tk = vmin;
+  unsigned tk = (unsigned)vmin;
   if (k > 0 && k < n && vmin != vmax) {
-    const int b0 = 31 - __clz(vmin ^ vmax);
-    unsigned v = b0 >= 31 ? 0u : (vmax & ~((2u << b0) - 1u));
-    for (int b = b0; b >= 0; --b) {
-      const unsigned c = v | (1u << b);
-      int cnt = 0;
-      for (int e = lane; e < n; e += 32) cnt += vkey(e) >= c ? 1 : 0;
-      if (__reduce_add_sync(FULL, cnt) >= k) v = c;
-    }
-    tk = v;
+    const int b0 = 31 - __clz((unsigned)(vmin ^ vmax));
+    const unsigned v = b0 >= 31 ? 0u : ((unsigned)vmax & ~((2u << b0) - 1u));
+    tk = radix_kth<CTA>(vk, n, v, b0, k, hist, R);
   }
 
   // ---- exact probabilities of the survivors (sampling.cpp:52-55) ----
   double ps = 0.0;
   int ns = 0;
-  unsigned smin = 0xffffffffu;
-  unsigned long long kmax = 0ull;
-  for (int e = lane; e < n; e += 32) {
-    const unsigned v = vkey(e);
+  unsigned long long smin = ~0ull, elast = 0ull;
+#pragma unroll 4
+  for (int e = r0; e < n; e += GN) {
+    const unsigned v = vk[e];
     double p = 0.0;
     if (v >= tk) {
-      p = prob(fkey_inv(v), m_y);
+      p = exp((double)__fsub_rn(fkey_inv(v), m_y));    // prob(): the reference's exp((double)(y - max))
       ++ns;
-      smin = min(smin, v);
-      const unsigned long long kk = keys[e];
-      kmax = kk > kmax ? kk : kmax;
+      smin = v < smin ? v : smin;
     }
+    if (v == (unsigned)vmax) elast = e;               // last (largest-index) maximum
     pv[e] = p;
     ps += p;
   }
-  ps = warp_sum_d(ps);
-  ns = __reduce_add_sync(FULL, ns);
-  smin = __reduce_min_sync(FULL, smin);
-  kmax = warp_max_u64(kmax);
-  __syncwarp();
+  ps = G::sum(ps, R);
+  ns = G::add(ns, R);
+  smin = G::qmin(smin, R);
+  const unsigned long long kmax = keys[G::qmax(elast, R)];   // the largest survivor key
+  G::sync();
 
   // ---- top-p (sampling.cpp:42-71) ----
   const double thr = J.thr;
@@ -328,53 +619,50 @@ __device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const u
     kst = 0ull;                                       // p > 1: nothing removed
   } else if (thr == 0.0) {
     unsigned long long mk0 = KEY_MAX;                 // p == 1: only zero probabilities go
-    for (int e = lane; e < n; e += 32)
-      if (vkey(e) >= tk && pv[e] > 0.0) mk0 = keys[e] < mk0 ? keys[e] : mk0;
-    kst = warp_min_u64(mk0);
+    for (int e = r0; e < n; e += GN)
+      if (vk[e] >= tk && pv[e] > 0.0) mk0 = keys[e] < mk0 ? keys[e] : mk0;
+    kst = G::qmin(mk0, R);
   } else {
     const double Th = thr * St;
     // G(c) = tail + sum of p over value keys < c (removed candidates have p = 0);
     // the largest c with G(c) <= Th is the value of the crossing element
-    const int b0 = (smin == vmax) ? -1 : 31 - __clz(smin ^ vmax);
-    unsigned v = b0 < 0 ? smin : (b0 >= 31 ? 0u : (vmax & ~((2u << b0) - 1u)));
-    for (int b = b0; b >= 0; --b) {
-      const unsigned c = v | (1u << b);
-      double g = 0.0;
-      for (int e = lane; e < n; e += 32) g += vkey(e) < c ? pv[e] : 0.0;
-      if (tail + warp_sum_d(g) <= Th) v = c;
-    }
-    double G = 0.0, Mg = 0.0;
+    const unsigned smin32 = (unsigned)smin, vmax32 = (unsigned)vmax;
+    const int b0 = (smin32 == vmax32) ? -1 : 31 - __clz(smin32 ^ vmax32);
+    unsigned v = b0 < 0 ? smin32 : (b0 >= 31 ? 0u : (vmax32 & ~((2u << b0) - 1u)));
+    v = radix_mass<CTA>(vk, pv, n, v, b0, tail, Th, hist, R);
+    double Gs = 0.0, Mg = 0.0;
     int cg = 0;
-    for (int e = lane; e < n; e += 32) {
-      const unsigned ve = vkey(e);
-      if (ve < v) G += pv[e];
+    for (int e = r0; e < n; e += GN) {
+      const unsigned ve = vk[e];
+      if (ve < v) Gs += pv[e];
       else if (ve == v && ve >= tk) { Mg += pv[e]; ++cg; }
     }
-    G = tail + warp_sum_d(G);
-    Mg = warp_sum_d(Mg);
-    cg = __reduce_add_sync(FULL, cg);
-    if (cg > 0 && G <= Th && G + Mg > Th) {
+    Gs = tail + G::sum(Gs, R);
+    Mg = G::sum(Mg, R);
+    cg = G::add(cg, R);
+    if (cg > 0 && Gs <= Th && Gs + Mg > Th) {
       // crossing inside the value group v; equal values have equal p and
-      // keep index order
+      // keep index order: the t-th member of the group in index order
       const double pg = Mg / cg;
       int t = 1;
       if (cg > 1) {
-        const double q = floor((Th - G) / pg) + 1.0;
+        const double q = floor((Th - Gs) / pg) + 1.0;
         t = (int)fmin(fmax(q, 1.0), (double)cg);
       }
       int es = 0, acc = 0;
-      for (int e0 = 0; e0 < n; e0 += 32) {
-        const int e = e0 + lane;
-        unsigned bal = __ballot_sync(FULL, e < n && vkey(e) == v);
-        const int c = __popc(bal);
-        if (t <= acc + c) {
-          for (int r = acc + 1; r < t; ++r) bal &= bal - 1u;
-          es = e0 + __ffs(bal) - 1;
+      for (int e0 = 0; e0 < n; e0 += GN) {
+        const int e = e0 + r0;
+        const bool m = e < n && vk[e] == v;
+        int tot;
+        const int before = G::exscan_i(m ? 1 : 0, R, &tot);
+        if (t <= acc + tot) {
+          const bool me = m && acc + before + 1 == t;
+          es = (int)G::qmin(me ? (unsigned long long)e : ~0ull, R);
           break;
         }
-        acc += c;
+        acc += tot;
       }
-      const double before = G + (double)(t - 1) * pg, cur = G + (double)t * pg;
+      const double before = Gs + (double)(t - 1) * pg, cur = Gs + (double)t * pg;
       const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
       kst = keys[es];
       exact_tp = !(before <= Th - bd && cur > Th + bd);
@@ -385,25 +673,29 @@ __device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const u
     exact_tp = exact_tp || forced;
   }
   if (exact_tp) {
-    if (k0) { hand_back(); return; }                  // the tail is only estimated here
+    if (k0) {                                         // the tail is exact only after a refine
+      if (!refine) hand_back(RES_REFINE);
+      return false;
+    }
     // the reference's sequential sums over the survivors in ascending order
     int base = 0;
-    for (int e0 = 0; e0 < n; e0 += 32) {
-      const int e = e0 + lane;
-      const bool sv = e < n && vkey(e) >= tk;
-      const unsigned bal = __ballot_sync(FULL, sv);
-      if (sv) sb[base + __popc(bal & ((1u << lane) - 1u))] = keys[e];
-      base += __popc(bal);
+    for (int e0 = 0; e0 < n; e0 += GN) {
+      const int e = e0 + r0;
+      const bool sv = e < n && vk[e] >= tk;
+      int tot;
+      const int pos = G::exscan_i(sv ? 1 : 0, R, &tot);
+      if (sv) sb[base + pos] = keys[e];
+      base += tot;
     }
     int np = 1;
     while (np < ns) np <<= 1;
-    for (int s = ns + lane; s < np; s += 32) sb[s] = KEY_MAX;
-    __syncwarp();
-    warp_bitonic(sb, np);
-    for (int s = lane; s < ns; s += 32) pv[s] = prob(fkey_inv((unsigned)(sb[s] >> 32)), m_y);
-    __syncwarp();
+    for (int s = ns + r0; s < np; s += GN) sb[s] = KEY_MAX;
+    G::sync();
+    group_bitonic<CTA>(sb, np);
+    for (int s = r0; s < ns; s += GN) pv[s] = prob(fkey_inv((unsigned)(sb[s] >> 32)), m_y);
+    G::sync();
     int js = ns;
-    if (lane == 0) {
+    if (r0 == 0) {
       double sum = 0.0;
       for (int s = 0; s < ns; ++s) sum = __dadd_rn(sum, pv[s]);
       double cum = 0.0;
@@ -413,49 +705,50 @@ __device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const u
       }
       atomicAdd(&a.counters[C4S_CNT_TOPP_EXACT_FALLBACK], 1ull);
     }
-    js = __shfl_sync(FULL, js, 0);
+    js = G::bcast_i(js, 0, R);
     kst = js < ns ? sb[js] : KEY_MAX;
-    __syncwarp();
+    G::sync();
     // probabilities by position again, for the draw
-    for (int e = lane; e < n; e += 32) pv[e] = vkey(e) >= tk ? prob(fkey_inv(vkey(e)), m_y) : 0.0;
-    __syncwarp();
+    for (int e = r0; e < n; e += GN) pv[e] = vk[e] >= tk ? prob(fkey_inv(vk[e]), m_y) : 0.0;
+    G::sync();
   }
   kst = kst < kmax ? kst : kmax;                      // min_tokens_to_keep = 1
 
   // ---- the draw (text2semantic.cpp:150-165); index order = position order ----
-  auto kept = [&](int e) { return e < n && vkey(e) >= tk && keys[e] >= kst; };
+  // keys[e] >= kst, read from global memory only for the value tied with kst
+  const unsigned kv = (unsigned)(kst >> 32);
+  auto kept = [&](int e) {
+    if (e >= n) return false;
+    const unsigned v = vk[e];
+    return v >= tk && (v > kv || (v == kv && keys[e] >= kst));
+  };
   int tok = 0;
   if (J.u53 != 0ull) {
     const double u = J.u;
     double s2 = 0.0;
     int nk = 0;
-    for (int e = lane; e < n; e += 32)
+    for (int e = r0; e < n; e += GN)
       if (kept(e)) { s2 += pv[e]; ++nk; }
-    s2 = warp_sum_d(s2);
-    nk = __reduce_add_sync(FULL, nk);
+    s2 = G::sum(s2, R);
+    nk = G::add(nk, R);
     const double r = u * s2;
     double carry = 0.0, prev = 0.0, cur = 0.0;
     int found = -1;
-    for (int e0 = 0; e0 < n; e0 += 32) {
-      const int e = e0 + lane;
+    for (int e0 = 0; e0 < n; e0 += GN) {
+      const int e = e0 + r0;
       const bool kp = kept(e);
       const double x = kp ? pv[e] : 0.0;
-      double incl = x;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const double y = __shfl_up_sync(FULL, incl, o);
-        if (lane >= o) incl += y;
-      }
-      incl += carry;
-      const unsigned bal = __ballot_sync(FULL, kp && incl >= r);
-      if (bal) {
-        const int L = __ffs(bal) - 1;
-        found = e0 + L;
-        prev = __shfl_sync(FULL, incl - x, L);
-        cur = __shfl_sync(FULL, incl, L);
+      double tot;
+      const double incl = carry + G::exscan_d(x, R, &tot) + x;
+      const unsigned long long hit = G::qmin(kp && incl >= r ? (unsigned long long)e : ~0ull, R);
+      if (hit != ~0ull) {
+        found = (int)hit;
+        prev = incl - x;
+        cur = incl;
+        G::bcast_2d(prev, cur, found - e0, R);
         break;
       }
-      carry = __shfl_sync(FULL, incl, 31);
+      carry += tot;
     }
     const double bd2 = 2.0 * ((4.0 * nk + 16.0) * U53 * s2);
     if (!forced && found >= 0 && prev < r - bd2 && cur > r + bd2) {
@@ -463,7 +756,7 @@ __device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const u
     } else {
       // the reference's sequential sums in index order
       int t = V - 1;
-      if (lane == 0) {
+      if (r0 == 0) {
         double sum = 0.0;
         for (int e = 0; e < n; ++e)
           if (kept(e)) sum = __dadd_rn(sum, pv[e]);
@@ -477,26 +770,63 @@ __device__ __noinline__ void list_job(const Args& a, int row, RowJob& J, const u
         }
         atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
       }
-      tok = __shfl_sync(FULL, t, 0);
+      tok = G::bcast_i(t, 0, R);
     }
   }
-  if (lane == 0) {
+  if (r0 == 0) {
     a.out_ids[row] = tok;
     a.rng[row] = J.xs;
     J.kstar = kst;
     J.thresh_key = k > 0 ? tk : 0u;
     J.status = RES_DONE;
   }
+  G::sync();
+  return true;
 }
 
-__global__ void __launch_bounds__(32 * LIST_WARPS) list_kernel(Args a) {
-  const int row = blockIdx.x * LIST_WARPS + (threadIdx.x >> 5);
-  if (row >= a.B) return;
-  RowJob& J = a.jobs[row];
-  const int kind = J.kind;
-  if (kind != JOB_TOPK && kind != JOB_K0) return;
-  const size_t o = (size_t)row * LCAP;
-  list_job(a, row, J, a.lkeys + o, a.lpv + o, a.lsb + o);
+// List kernel dynamic shared memory: per warp a list of up to LW_CAP entries
+// (staged value keys, probabilities) and a radix histogram; once the warps are
+// done, the same area holds one long list (up to LCAP) worked by the whole CTA.
+constexpr int LW_CAP = 1024;                  // longest list one warp takes
+constexpr size_t LW_VK = 0, LW_PV = (size_t)LW_CAP * 4, LW_HIST = LW_PV + (size_t)LW_CAP * 8;
+constexpr size_t LW_BYTES = LW_HIST + 256 * 8;            // per warp
+constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)LCAP * 8;
+constexpr size_t LIST_SMEM = (size_t)LIST_WARPS * LW_BYTES;
+static_assert(LB_HIST + 256 * 8 <= LIST_SMEM, "a long list fits the warps' areas");
+
+// Short lists: one warp each. Long lists (the row kernel queued them): CTAs
+// take them one at a time from a shared counter once their warps are done.
+__global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
+  static_assert(32 * LIST_WARPS == NT, "the list kernel's CTA barrier counts NT threads");
+  extern __shared__ __align__(16) unsigned char lsm[];
+  __shared__ LRed R;
+  __shared__ int next;
+  const int w = threadIdx.x >> 5;
+  const int row = blockIdx.x * LIST_WARPS + w;
+  if (row < a.B) {
+    RowJob& J = a.jobs[row];
+    const int kind = J.kind;
+    if ((kind == JOB_TOPK || kind == JOB_K0) && J.n <= LW_CAP) {
+      unsigned char* wa = lsm + (size_t)w * LW_BYTES;
+      const size_t o = (size_t)row * LCAP;
+      list_job<false>(a, row, J, a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
+                      reinterpret_cast<double*>(wa + LW_PV), reinterpret_cast<unsigned long long*>(wa + LW_HIST),
+                      false, R);
+    }
+  }
+  const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
+  for (;;) {
+    csync();                                        // the warps' lists are done with the area
+    if (threadIdx.x == 0) next = (int)atomicAdd(&a.defer_cnt[4], 1u);
+    csync();
+    const int t = next;
+    if (t >= (int)nbig) break;
+    const int r = a.big_rows[t];
+    const size_t o = (size_t)r * LCAP;
+    list_job<true>(a, r, a.jobs[r], a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(lsm + LB_VK),
+                   reinterpret_cast<double*>(lsm + LB_PV), reinterpret_cast<unsigned long long*>(lsm + LB_HIST),
+                   false, R);
+  }
 }
 
 // ===========================================================================
@@ -625,6 +955,11 @@ __device__ __forceinline__ void fill_job(RowJob& J, const RowCtx& rc, int kind, 
   J.u53 = rc.u53;
   J.xs = rc.xs;
   J.kstar = 0ull;
+}
+
+// A list longer than one list-kernel warp takes goes to the CTA-wide queue.
+__device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
+  if (n > LW_CAP) a.big_rows[atomicAdd(&a.defer_cnt[3], 1u)] = row;
 }
 
 // Writes the keys of this thread's candidates (bit j of mask: position j)
@@ -1045,6 +1380,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
         if (tid == 0) {
           RowJob& J = a.jobs[row];
           fill_job(J, rc, JOB_K0, ng, 0);
+          queue_long_list(a, row, ng);
           J.tail = tl;
           J.tail_err = est_err(tl, et, rc.m_y, 33, V);
           J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
@@ -1088,6 +1424,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
   if (tid == 0) {
     RowJob& J = a.jobs[row];
     fill_job(J, rc, JOB_TOPK, ng, k);
+    queue_long_list(a, row, ng);
     J.tail = 0.0;
     J.tail_err = 0.0;
     J.ykex = 0u;
@@ -1245,9 +1582,66 @@ __global__ void __launch_bounds__(NT, 2) row_kernel(Args a) {
 // The general path for the rows the row and list kernels handed back; the
 // last CTA to finish clears the hand-back list for the next launch sequence.
 // ---------------------------------------------------------------------------
+// A no-top-k row whose top-p decision fell inside the band of its estimated
+// tail: the exact tail mass (sum of exp((double)(y - m_y)) over the elements
+// below the list, re-associated; its rounding is inside the list's double-sum
+// band) replaces the estimate and the list job runs again on warp 0.
+// Returns 1 if the row is finished, 0 if it needs the general path, -1 if the
+// staging wait gave up.
+__device__ __noinline__ int refine_k0(const Args& a, int row, float* rowbuf, unsigned* bitmap, Shared& S,
+                                      LRed& R, unsigned long long* hist, unsigned* vk_area, double* pv_area,
+                                      unsigned& phase) {
+  const int V = a.V;
+  const int tid = threadIdx.x;
+  const c4s_row_params P = a.params[(long long)row * a.params_stride];
+  const Stage sg = stage_issue(a.logits + (long long)row * a.ld, V, rowbuf, &S.bar);
+  const bool pen = a.hist_off && P.repetition_penalty != 1.0f;
+  long long h0, h1;
+  hist_window(a, row, pen, h0, h1);
+  int hid[8];
+  hist_prefetch(a, h0, h1, hid);
+  if (pen)
+    for (int w = tid; w < (V + 31) / 32; w += NT) bitmap[w] = 0u;
+  if (!stage_wait(a, sg, &S.bar, phase, S)) return -1;
+  float* srow = rowbuf + sg.shift;
+  if (pen) penalty_apply(a, srow, V, bitmap, P.repetition_penalty, hid, h0, h1);
+  RowJob& J = a.jobs[row];
+  const float T = P.temperature;
+  const bool do_t = !(T == 1.0f || T <= 0.0f);
+  const float rT = do_t ? __frcp_rn(T) : 1.0f;
+  const unsigned ykex = J.ykex;
+  const float m_y = J.m_y;
+  double t = 0.0;
+  for (int i = tid; i < V; i += NT) {
+    const float y = do_t ? div_rn(srow[i], T, rT) : srow[i];
+    if (fkey(y) <= ykex) t += prob(y, m_y);
+  }
+  double tail;
+  block_exscan_f64(t, S.redd, &tail);
+  if (tid == 0) {
+    J.tail = tail;
+    J.tail_err = 0.0;
+  }
+  csync();
+  // the staged list: value keys in the sort-key area (2 LIST_CAP entries), its
+  // probabilities in the row buffer (free once the tail is summed) or in the
+  // probability area (LIST_CAP entries)
+  const int n = J.n;
+  double* pvs = nullptr;
+  if ((size_t)n * 8 <= align_up((size_t)(V + 4) * 4, 16)) pvs = reinterpret_cast<double*>(rowbuf);
+  else if (n <= LIST_CAP) pvs = pv_area;
+  if (pvs == nullptr || n > 2 * LIST_CAP) return 0;
+  const size_t o = (size_t)row * LCAP;
+  const bool done = list_job<true>(a, row, J, a.lkeys + o, a.lsb + o, vk_area, pvs, hist, true, R);
+  csync();
+  return done ? 1 : 0;
+}
+
 __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ Shared S;
+  __shared__ LRed R;
+  __shared__ unsigned long long lhist[256];
   const Layout L = layout_for(a.V);
   float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
@@ -1259,8 +1653,15 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   csync();
   unsigned phase = 0;
   const unsigned n = *reinterpret_cast<volatile unsigned*>(a.defer_cnt);
-  for (unsigned t = blockIdx.x; t < n; t += gridDim.x)
-    if (!general_row(a, a.defer_rows[t], rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) break;
+  for (unsigned t = blockIdx.x; t < n; t += gridDim.x) {
+    const int row = a.defer_rows[t];
+    if (a.jobs[row].kind == JOB_K0 && a.jobs[row].status == RES_REFINE) {
+      const int r = refine_k0(a, row, rowbuf, bitmap, S, R, lhist, reinterpret_cast<unsigned*>(lkey), pv, phase);
+      if (r < 0) break;
+      if (r > 0) continue;
+    }
+    if (!general_row(a, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) break;
+  }
   csync();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -1268,6 +1669,8 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
       a.defer_cnt[0] = 0u;
       a.defer_cnt[1] = 0u;
       a.defer_cnt[2] = 0u;                          // the row kernel's row counter
+      a.defer_cnt[3] = 0u;                          // long lists queued for the list kernel
+      a.defer_cnt[4] = 0u;                          //   and the list kernel's ticket
     }
   }
 }

@@ -43,7 +43,9 @@ struct Args {
   double* lpv;                  // [B][LCAP] their probabilities
   unsigned long long* lsb;      // [B][LCAP] sort buffer of the exact fallback
   int* defer_rows;              // rows handed to the general path
-  unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done, [2] row counter
+  int* big_rows;                // rows whose lists the list kernel works with a whole CTA
+  unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done, [2] row counter,
+                                // [3] long lists queued, [4] list-kernel ticket
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

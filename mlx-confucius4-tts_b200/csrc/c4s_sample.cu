@@ -34,6 +34,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "../../include/c4s_sampling.h"
@@ -103,9 +104,12 @@ struct c4s_ctx {
   unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
   double* d_lpv = nullptr;
   unsigned long long* d_lsb = nullptr;
-  int* d_defer_rows = nullptr;                 //   rows handed to the general path
+  int* d_defer_rows = nullptr;                 //   rows handed to the general path, then long lists
   unsigned* d_defer_cnt = nullptr;
   int debug = 0;
+  bool timing = false;                         // c4s_kernel_timing: events between fast-path launches
+  std::vector<cudaEvent_t> tev;                //   4 per recorded chunk (before row, after row/list/defer)
+  size_t tev_used = 0;
   int cached_V = -1;
   int cached_occ = 0;
   std::string last_error;
@@ -147,6 +151,20 @@ int occupancy(c4s_ctx* ctx, int V, size_t smem) {
   return occ;
 }
 
+// Four timing events for the next recorded chunk (nullptr if they cannot be made).
+cudaEvent_t* timing_slot(c4s_ctx* ctx) {
+  if (ctx->tev_used + 4 > ctx->tev.size()) {
+    for (int i = 0; i < 4; ++i) {
+      cudaEvent_t e;
+      if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+      ctx->tev.push_back(e);
+    }
+  }
+  cudaEvent_t* ev = ctx->tev.data() + ctx->tev_used;
+  ctx->tev_used += 4;
+  return ev;
+}
+
 int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
   using namespace c4s;
   if (a.B == 0) return C4S_OK;
@@ -169,6 +187,7 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     a.lpv = ctx->d_lpv;
     a.lsb = ctx->d_lsb;
     a.defer_rows = ctx->d_defer_rows;
+    a.big_rows = ctx->d_defer_rows + K_CHUNK;
     a.defer_cnt = ctx->d_defer_cnt;
     if (ctx->row_occ == 0) {
       int occ = 0;
@@ -189,10 +208,15 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       if (a.out_logits) ac.out_logits = a.out_logits + (long long)c0 * a.out_ld;
       if (a.hist_off) ac.hist_off = a.hist_off + c0;
       const int g1 = (int)std::min<long long>(ac.B, (long long)ctx->row_occ * ctx->num_sms);
+      cudaEvent_t* ev = ctx->timing ? timing_slot(ctx) : nullptr;
+      if (ev) cudaEventRecord(ev[0], st);
       row_kernel<<<g1, NT, row_smem(ac.V), st>>>(ac);
-      list_kernel<<<(ac.B + LIST_WARPS - 1) / LIST_WARPS, 32 * LIST_WARPS, 0, st>>>(ac);
+      if (ev) cudaEventRecord(ev[1], st);
+      list_kernel<<<(ac.B + LIST_WARPS - 1) / LIST_WARPS, 32 * LIST_WARPS, LIST_SMEM, st>>>(ac);
+      if (ev) cudaEventRecord(ev[2], st);
       const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
       defer_kernel<<<g3, NT, gsm, st>>>(ac);
+      if (ev) cudaEventRecord(ev[3], st);
       if (a.out_logits) mask_kernel<<<ac.B, NT, 0, st>>>(ac);
       e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(ctx, e, "fast path launch");
@@ -210,6 +234,9 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
 }
 
 void free_all(c4s_ctx* ctx) {
+  for (cudaEvent_t e : ctx->tev) cudaEventDestroy(e);
+  ctx->tev.clear();
+  ctx->tev_used = 0;
   cudaFree(ctx->d_scratch);
   cudaFree(ctx->d_err);
   cudaFree(ctx->d_counters);
@@ -270,6 +297,8 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   e = cudaFuncSetAttribute(c4s::rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::defer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c4s::LIST_SMEM);
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   int p2 = 1;
   while (p2 < max_vocab) p2 <<= 1;
@@ -283,9 +312,9 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lkeys, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lpv, nl * sizeof(double));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (size_t)c4s::K_CHUNK * sizeof(int));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, 4 * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, 4 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, 2 * (size_t)c4s::K_CHUNK * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, 8 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, 8 * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_default_params, 0, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(unsigned));
@@ -314,8 +343,32 @@ const char* c4s_last_error(const c4s_ctx* ctx) { return ctx ? ctx->last_error.c_
 
 int c4s_set_debug(c4s_ctx* ctx, int32_t flags) {
   if (!ctx) return C4S_ERR_INVALID;
-  if (flags & ~(C4S_DEBUG_FORCE_EXACT | C4S_DEBUG_FORCE_BINS)) return fail(ctx, C4S_ERR_INVALID, "unknown debug flag");
+  if (flags & ~(C4S_DEBUG_FORCE_EXACT | C4S_DEBUG_FORCE_BINS | C4S_DEBUG_FORCE_REFINE)) return fail(ctx, C4S_ERR_INVALID, "unknown debug flag");
   ctx->debug = flags;
+  return C4S_OK;
+}
+
+int c4s_kernel_timing(c4s_ctx* ctx, int32_t enable) {
+  if (!ctx) return C4S_ERR_INVALID;
+  ctx->timing = enable != 0;
+  return C4S_OK;
+}
+
+int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset) {
+  if (!ctx || !ms || !launches) return C4S_ERR_INVALID;
+  DeviceGuard dg(ctx->device);
+  for (int k = 0; k < 3; ++k) { ms[k] = 0.0; launches[k] = 0; }
+  for (size_t c = 0; c + 4 <= ctx->tev_used; c += 4) {
+    for (int k = 0; k < 3; ++k) {
+      if (cudaEventSynchronize(ctx->tev[c + k + 1]) != cudaSuccess) return fail(ctx, C4S_ERR_CUDA, "timing event");
+      float t = 0.0f;
+      if (cudaEventElapsedTime(&t, ctx->tev[c + k], ctx->tev[c + k + 1]) != cudaSuccess)
+        return fail(ctx, C4S_ERR_CUDA, "timing event");
+      ms[k] += t;
+      launches[k] += 1;
+    }
+  }
+  if (reset) ctx->tev_used = 0;
   return C4S_OK;
 }
 

@@ -35,6 +35,7 @@ STAGE_TOP_P = 8
 STAGE_ALL = 15
 DEBUG_FORCE_EXACT = 1
 DEBUG_FORCE_BINS = 2
+DEBUG_FORCE_REFINE = 4
 COUNTER_NAMES = ("topp_exact_fallback", "draw_exact_fallback", "topk_radix",
                  "topp_binned", "draw_rowpass", "deferred")
 MAX_VOCAB = 32768
@@ -78,6 +79,8 @@ def library() -> C.CDLL:
                 "c4s_process": ([vp, vp, i32, i32, i64, vp, vp, i64, vp, i32, i32, vp], C.c_int),
                 "c4s_argmax": ([vp, vp, i32, i32, i64, vp, vp], C.c_int),
                 "c4s_get_status": ([vp, vp, vp, i32, vp], C.c_int),
+                "c4s_kernel_timing": ([vp, i32], C.c_int),
+                "c4s_kernel_times": ([vp, vp, vp, i32], C.c_int),
             }
             for name, (args, res) in sig.items():
                 f = getattr(L, name)
@@ -154,6 +157,17 @@ class SamplingContext:
         if rc not in (0, -4, -5):
             self._check(rc, "c4s_get_status")
         return int(err.value), counters
+
+    def kernel_timing(self, enable: bool):
+        """Record CUDA events around the fast path's kernels of later calls."""
+        self._check(self.lib.c4s_kernel_timing(self._h, int(enable)), "c4s_kernel_timing")
+
+    def kernel_times(self, reset: bool = True):
+        """{kernel: (summed device ms, launches)} of the calls recorded so far."""
+        ms = (C.c_double * 3)()
+        n = (C.c_int64 * 3)()
+        self._check(self.lib.c4s_kernel_times(self._h, ms, n, int(reset)), "c4s_kernel_times")
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(("row_kernel", "list_kernel", "defer_kernel"))}
 
     # -- batched entry points -----------------------------------------------------
     def seed_states(self, B: int, seed: int, row_offset: int = 0, out=None, stream=None):

@@ -178,9 +178,10 @@ def test_config2_full_batch(ctx, oracle, wl):
     assert np.array_equal(rg2, ro2)
 
 
-@pytest.mark.parametrize("flags", [1, 2, 3])
+@pytest.mark.parametrize("flags", [1, 2, 3, 4])
 def test_forced_slow_paths(c4s, oracle, wl, flags):
-    """The exact fallbacks and the binned paths, forced on ordinary rows."""
+    """The exact fallbacks, the binned paths and the exact-tail refinement of
+    rows without top-k, forced on ordinary rows."""
     ctx = c4s.SamplingContext(max_vocab=8194, device=0)
     ctx.set_debug(flags)
     b = wl.config2(seed=7, B=384)
@@ -196,6 +197,8 @@ def test_forced_slow_paths(c4s, oracle, wl, flags):
         assert cnt["topp_binned"] > 0 and cnt["draw_rowpass"] > 0
     if flags & 1:
         assert cnt["topk_radix"] > 0
+    if flags & 4:
+        assert cnt["deferred"] > 0
 
 
 def test_path_counters_and_no_errors(ctx, wl):
