@@ -18,11 +18,12 @@ constexpr int MAX_VOCAB = 32768;      // row must fit in shared memory
 constexpr unsigned FULL = 0xffffffffu;
 constexpr unsigned long long KEY_MAX = ~0ull;
 
-// Barrier of the row-processing group: the NT threads of warps 0..NWARP-1.
-// It is named barrier 1, so warps outside the group (the fast kernel's list
-// warps) never take part; in a CTA of exactly NT threads it acts like
-// __syncthreads(). Orders shared-memory accesses among the participants.
-__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+// CTA barrier of the NT threads (named barrier 1). It is the non-aligned
+// form (barrier.sync, not bar.sync = barrier.sync.aligned): a warp may reach
+// it with its lanes diverged (e.g. right after a branch only lane 0 takes,
+// such as a bounded wait on an mbarrier), which the aligned form leaves
+// undefined. Orders shared- and global-memory accesses among the participants.
+__device__ __forceinline__ void csync() { asm volatile("barrier.sync 1, %0;" ::"n"(NT) : "memory"); }
 
 // ---------------------------------------------------------------------------
 // Keys. fkey() maps a float to a uint32 whose unsigned order is the float
@@ -229,32 +230,21 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
       : "memory");
   return ok != 0;
 }
-// As mbar_try_wait, but a thread whose phase is not complete may be suspended
-// in hardware for up to `ns` nanoseconds (it resumes as soon as the phase
-// completes), so waiting warps take no issue slots.
-__device__ __forceinline__ bool mbar_try_wait_sleep(unsigned long long* bar, unsigned phase, unsigned ns) {
-  unsigned ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait (about 2 s of wall time); false if it gave up. Each poll may
-// sleep up to 20 us in hardware until the phase completes.
+// Bounded wait (about 2 s of wall time); false if it gave up. Polls with a
+// 128 ns back-off.
 __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned phase) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (unsigned it = 0; it < (1u << 30); ++it) {
-    if (mbar_try_wait_sleep(bar, phase, 20000u)) return true;
+    // back off between polls: a spinning warp takes issue slots from the
+    // resident CTAs that have work
+    __nanosleep(128);
+    if (mbar_try_wait(bar, phase)) return true;
     if ((it & 15u) == 15u && globaltimer_ns() - t0 > 2000000000ull) return false;
   }
   return false;

@@ -41,6 +41,7 @@
 #include "c4s_device.cuh"
 #include "c4s_general.cuh"
 #include "c4s_fast.cuh"
+#include "c4s_row.cuh"
 
 namespace c4s {
 
@@ -191,7 +192,7 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     a.defer_cnt = ctx->d_defer_cnt;
     if (ctx->row_occ == 0) {
       int occ = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, NT, row_smem(F_MAXV)) != cudaSuccess || occ < 1)
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, RT, R_SMEM) != cudaSuccess || occ < 1)
         return fail(ctx, C4S_ERR_CUDA, "row kernel occupancy");
       ctx->row_occ = occ;
     }
@@ -210,7 +211,7 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       const int g1 = (int)std::min<long long>(ac.B, (long long)ctx->row_occ * ctx->num_sms);
       cudaEvent_t* ev = ctx->timing ? timing_slot(ctx) : nullptr;
       if (ev) cudaEventRecord(ev[0], st);
-      row_kernel<<<g1, NT, row_smem(ac.V), st>>>(ac);
+      row_kernel<<<g1, RT, R_SMEM, st>>>(ac);
       if (ev) cudaEventRecord(ev[1], st);
       list_kernel<<<(ac.B + LIST_WARPS - 1) / LIST_WARPS, 32 * LIST_WARPS, LIST_SMEM, st>>>(ac);
       if (ev) cudaEventRecord(ev[2], st);
@@ -299,6 +300,14 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
     e = cudaFuncSetAttribute(c4s::defer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c4s::LIST_SMEM);
+  // the row kernel keeps five rows in flight per SM only with the largest
+  // shared-memory carveout
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::row_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::list_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   int p2 = 1;
   while (p2 < max_vocab) p2 <<= 1;

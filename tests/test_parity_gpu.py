@@ -207,9 +207,10 @@ def test_path_counters_and_no_errors(ctx, wl):
     gpu_sample(ctx, b, torch)
     err, cnt = ctx.status(reset=True)
     assert err == 0
-    # rows handed to the general path are rare (only an undecided double-
-    # precision band or inputs outside the fast path's assumptions)
-    assert cnt["deferred"] <= 2
+    # rows handed to the general path are rare: rows without top-k whose
+    # candidate list would exceed the list capacity (about 1% of config-2
+    # rows), undecided double-precision bands, inputs outside the fast path
+    assert cnt["deferred"] <= b.B // 50
 
 
 # ---------------------------------------------------------------------------
