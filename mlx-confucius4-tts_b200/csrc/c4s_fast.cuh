@@ -29,7 +29,8 @@
 namespace c4s {
 
 constexpr int F_MAXV = 9212;              // widest row the fast path takes
-constexpr int LCAP = 2048;                // candidates per list
+constexpr int LCAP = 9216;                // candidates per list (>= F_MAXV: a list can hold a whole row)
+constexpr int LIST_DEEP = 1024;           // rows without top-k: lists go deeper only up to this length
 constexpr int K_CHUNK = 4096;             // rows per launch sequence (list storage)
 constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
@@ -382,72 +383,29 @@ __device__ __forceinline__ unsigned radix_kth(const unsigned* __restrict__ vk, i
   return prefix;
 }
 
-// mass: the largest v with base + sum(pv[e] : vkey(e) < v) <= Th (v = prefix if
-// none), where base is the mass below the searched range. The bins add p in
-// 2^-52 fixed point (native 64-bit shared atomics; p <= 1 and n <= 2048); the
-// search only has to land on the crossing value, which the caller then checks
-// with double sums and their error band.
+// The largest v with base + sum(pv[e] : vk[e] < v) <= Th (v = prefix if
+// none), by bisection over the key bits below b0 under `prefix`; base is the
+// mass below the searched range. One pass over the staged list per bit (no
+// atomics: contended 64-bit shared-memory adds are slow). The search only has
+// to land on the crossing value, which the caller checks with double sums and
+// their error band.
 template <bool CTA>
-__device__ __forceinline__ unsigned radix_mass(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
-                                               unsigned prefix, int b0, double base, double Th,
-                                               unsigned long long* __restrict__ hist, LRed& R) {
+__device__ __forceinline__ unsigned bisect_mass(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
+                                                unsigned prefix, int b0, double base, double Th, LRed& R) {
   using G = LG<CTA>;
-  unsigned long long* h = hist;
-  const int lane = threadIdx.x & 31;
-  for (int hi = b0; hi >= 0;) {
-    const int w = hi + 1 < 8 ? hi + 1 : 8;
-    const int lo = hi - w + 1;
-    const unsigned pmask = hi >= 31 ? 0u : ~((2u << hi) - 1u);
-    for (int i = G::rank(); i < 256; i += G::N) h[i] = 0ull;
-    G::sync();
-    for (int e = G::rank(); e < n; e += G::N) {
-      const unsigned v = vk[e];
-      const double p = pv[e];
-      if ((v & pmask) == prefix && p != 0.0)
-        atomicAdd(&h[(v >> lo) & 255u], __double2ull_rn(p * 4503599627370496.0));
+  unsigned v = prefix;
+  for (int b = b0; b >= 0; --b) {
+    const unsigned c = v | (1u << b);
+    double g0 = 0.0, g1 = 0.0;
+    int e = G::rank();
+    for (; e + G::N < n; e += 2 * G::N) {
+      g0 += vk[e] < c ? pv[e] : 0.0;
+      g1 += vk[e + G::N] < c ? pv[e + G::N] : 0.0;
     }
-    G::sync();
-    if (!CTA || threadIdx.x < 32) {
-      // lane l holds bins 8l..8l+7; E(d) = mass of digits < d
-      double m[8], s = 0.0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) { m[j] = (double)h[8 * lane + j] * 2.220446049250313e-16; s += m[j]; }
-      double incl = s;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const double y = __shfl_up_sync(FULL, incl, o);
-        if (lane >= o) incl += y;
-      }
-      double run = incl - s;
-      int q = 0;
-      double ed = 0.0;
-      int dl = -1;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (base + run <= Th) { ++q; dl = 8 * lane + j; ed = run; }
-        run += m[j];
-      }
-      const int D = __reduce_add_sync(FULL, q);
-      const int ds = D > 0 ? D - 1 : 0;
-      const unsigned src = __ballot_sync(FULL, dl == ds);
-      const int sl = src ? __ffs(src) - 1 : 0;
-      const double e = __shfl_sync(FULL, ed, sl);
-      if (CTA) {
-        if (threadIdx.x == 0) { R.e = ds; R.x = D > 0 ? e : 0.0; }
-      } else {
-        prefix |= (unsigned)ds << lo;
-        base += D > 0 ? e : 0.0;
-      }
-    }
-    if (CTA) {
-      csync();
-      prefix |= (unsigned)R.e << lo;
-      base += R.x;
-      csync();
-    }
-    hi = lo - 1;
+    if (e < n) g0 += vk[e] < c ? pv[e] : 0.0;
+    if (base + G::sum(g0 + g1, R) <= Th) v = c;
   }
-  return prefix;
+  return v;
 }
 
 // One list job. keys[0..n) (global): ckey(x, i) of the candidates' penalised,
@@ -554,6 +512,65 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     for (int e = r0; e < n; e += GN)
       if (vk[e] >= tk && pv[e] > 0.0) mk0 = ykey(e) < mk0 ? ykey(e) : mk0;
     kst = G::qmin(mk0, R);
+  } else if (!CTA && ns <= 64) {
+    // few survivors: sort them in registers (two per lane) by (value,
+    // position) -- positions are in index order, so this is the canonical
+    // (value, index) order -- and find the crossing on a prefix scan
+    const double Th = thr * St;
+    const int lane = r0;
+    int base = 0;
+    for (int e0 = 0; e0 < n; e0 += 32) {
+      const int e = e0 + lane;
+      const bool sv = e < n && vk[e] >= tk;
+      const unsigned bal = __ballot_sync(FULL, sv);
+      if (sv) hist[base + __popc(bal & ((1u << lane) - 1u))] = ((unsigned long long)vk[e] << 32) | (unsigned)e;
+      base += __popc(bal);
+    }
+    for (int i = ns + lane; i < 64; i += 32) hist[i] = KEY_MAX;
+    __syncwarp();
+    unsigned long long v0 = hist[2 * lane], v1 = hist[2 * lane + 1];
+    __syncwarp();
+#pragma unroll
+    for (int k2 = 2; k2 <= 64; k2 <<= 1) {
+#pragma unroll
+      for (int jj = k2 >> 1; jj > 0; jj >>= 1) {
+        if (jj == 1) {
+          const bool up = ((2 * lane) & k2) == 0;
+          const unsigned long long lo = v0 < v1 ? v0 : v1, hi = v0 < v1 ? v1 : v0;
+          v0 = up ? lo : hi;
+          v1 = up ? hi : lo;
+        } else {
+          const int lj = jj >> 1;
+          const unsigned long long o0 = __shfl_xor_sync(FULL, v0, lj), o1 = __shfl_xor_sync(FULL, v1, lj);
+          const int q0 = 2 * lane, q1 = 2 * lane + 1;
+          const bool m0 = ((q0 & jj) == 0) == ((q0 & k2) == 0);
+          const bool m1 = ((q1 & jj) == 0) == ((q1 & k2) == 0);
+          v0 = m0 ? (o0 < v0 ? o0 : v0) : (o0 > v0 ? o0 : v0);
+          v1 = m1 ? (o1 < v1 ? o1 : v1) : (o1 > v1 ? o1 : v1);
+        }
+      }
+    }
+    const double p0 = v0 != KEY_MAX ? pv[(int)(v0 & 0xffffffffull)] : 0.0;
+    const double p1 = v1 != KEY_MAX ? pv[(int)(v1 & 0xffffffffull)] : 0.0;
+    double tot;
+    const double pre = tail + G::exscan_d(p0 + p1, R, &tot);
+    const bool x0 = pre + p0 > Th, x1 = pre + p0 + p1 > Th;
+    const unsigned cb = __ballot_sync(FULL, x0 || x1);
+    if (cb) {
+      const int L = __ffs(cb) - 1;
+      const bool first = __shfl_sync(FULL, x0, L);
+      const double bl0 = __shfl_sync(FULL, pre, L), pl0 = __shfl_sync(FULL, p0, L), pl1 = __shfl_sync(FULL, p1, L);
+      const unsigned long long kj = first ? __shfl_sync(FULL, v0, L) : __shfl_sync(FULL, v1, L);
+      const double before = first ? bl0 : bl0 + pl0;
+      const double cur = first ? bl0 + pl0 : bl0 + pl0 + pl1;
+      const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
+      kst = ykey((int)(kj & 0xffffffffull));
+      exact_tp = !(before <= Th - bd && cur > Th + bd);
+    } else {
+      kst = KEY_MAX;                                  // no crossing: only the kept maximum
+      exact_tp = true;
+    }
+    exact_tp = exact_tp || forced;
   } else {
     const double Th = thr * St;
     // G(c) = tail + sum of p over value keys < c (removed candidates have p = 0);
@@ -561,7 +578,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     const unsigned smin32 = (unsigned)smin, vmax32 = (unsigned)vmax;
     const int b0 = (smin32 == vmax32) ? -1 : 31 - __clz(smin32 ^ vmax32);
     unsigned v = b0 < 0 ? smin32 : (b0 >= 31 ? 0u : (vmax32 & ~((2u << b0) - 1u)));
-    v = radix_mass<CTA>(vk, pv, n, v, b0, tail, Th, hist, R);
+    v = bisect_mass<CTA>(vk, pv, n, v, b0, tail, Th, R);
     double Gs = 0.0, Mg = 0.0;
     int cg = 0;
     for (int e = r0; e < n; e += GN) {
@@ -656,31 +673,37 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
   };
   int tok = 0;
   if (J.u53 != 0ull) {
+    // each member sums a contiguous range of positions; one exclusive scan of
+    // those sums locates the member whose range the prefix crosses r in, and
+    // that member scans its range
     const double u = J.u;
-    double s2 = 0.0;
-    int nk = 0;
-    for (int e = r0; e < n; e += GN)
-      if (kept(e)) { s2 += pv[e]; ++nk; }
-    s2 = G::sum(s2, R);
-    nk = G::add(nk, R);
+    const int L = (n + GN - 1) / GN;
+    const int e_lo = min(r0 * L, n), e_hi = min(e_lo + L, n);
+    double sm = 0.0;
+    int cm = 0;
+    for (int e = e_lo; e < e_hi; ++e)
+      if (kept(e)) { sm += pv[e]; ++cm; }
+    double s2;
+    const double base = G::exscan_d(sm, R, &s2);
+    const int nk = G::add(cm, R);
     const double r = u * s2;
-    double carry = 0.0, prev = 0.0, cur = 0.0;
-    int found = -1;
-    for (int e0 = 0; e0 < n; e0 += GN) {
-      const int e = e0 + r0;
-      const bool kp = kept(e);
-      const double x = kp ? pv[e] : 0.0;
-      double tot;
-      const double incl = carry + G::exscan_d(x, R, &tot) + x;
-      const unsigned long long hit = G::qmin(kp && incl >= r ? (unsigned long long)e : ~0ull, R);
-      if (hit != ~0ull) {
-        found = (int)hit;
-        prev = incl - x;
-        cur = incl;
-        G::bcast_2d(prev, cur, found - e0, R);
-        break;
+    int fe = -1;
+    double prev = 0.0, cur = 0.0;
+    if (base < r && base + sm >= r) {
+      double acc = base;
+      for (int e = e_lo; e < e_hi; ++e) {
+        if (kept(e)) {
+          const double nx = acc + pv[e];
+          if (nx >= r) { fe = e; prev = acc; cur = nx; break; }
+          acc = nx;
+        }
       }
-      carry += tot;
+    }
+    const unsigned long long hit = G::qmin(fe >= 0 ? (unsigned long long)fe : ~0ull, R);
+    int found = -1;
+    if (hit != ~0ull) {
+      found = (int)hit;
+      G::bcast_2d(prev, cur, found / L, R);
     }
     const double bd2 = 2.0 * ((4.0 * nk + 16.0) * U53 * s2);
     if (!forced && found >= 0 && prev < r - bd2 && cur > r + bd2) {
@@ -914,14 +937,21 @@ __device__ __noinline__ int refine_k0(const Args& a, int row, float* rowbuf, uns
     J.tail_err = 0.0;
   }
   csync();
-  // the staged list: value keys in the sort-key area (2 LIST_CAP entries), its
-  // probabilities in the row buffer (free once the tail is summed) or in the
-  // probability area (LIST_CAP entries)
+  // the staged list: probabilities in the row buffer (free once the tail is
+  // summed) and value keys in the sort-key and probability areas (4 LIST_CAP
+  // entries; they are adjacent), or -- rows too short for that -- keys in the
+  // sort-key area (2 LIST_CAP) and probabilities in the probability area
   const int n = J.n;
   double* pvs = nullptr;
-  if ((size_t)n * 8 <= align_up((size_t)(V + 4) * 4, 16)) pvs = reinterpret_cast<double*>(rowbuf);
-  else if (n <= LIST_CAP) pvs = pv_area;
-  if (pvs == nullptr || n > 2 * LIST_CAP) return 0;
+  int vcap = 0;
+  if ((size_t)n * 8 <= align_up((size_t)(V + 4) * 4, 16)) {
+    pvs = reinterpret_cast<double*>(rowbuf);
+    vcap = 4 * LIST_CAP;
+  } else if (n <= LIST_CAP) {
+    pvs = pv_area;
+    vcap = 2 * LIST_CAP;
+  }
+  if (pvs == nullptr || n > vcap) return 0;
   const size_t o = (size_t)row * LCAP;
   const bool done = list_job<true>(a, row, J, a.lkeys + o, a.lsb + o, vk_area, pvs, hist, true, R);
   csync();

@@ -40,7 +40,6 @@ struct Args {
   // fast path: per-row jobs and candidate lists of the current chunk, rows for the general path
   RowJob* jobs;
   unsigned long long* lkeys;    // [B][LCAP] candidate keys
-  double* lpv;                  // [B][LCAP] their probabilities
   unsigned long long* lsb;      // [B][LCAP] sort buffer of the exact fallback
   int* defer_rows;              // rows handed to the general path
   int* big_rows;                // rows whose lists the list kernel works with a whole CTA

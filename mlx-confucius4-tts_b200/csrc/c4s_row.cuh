@@ -346,7 +346,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
       // the list kernel's decision band (which scales with the tail) then
       // rarely reaches the crossing element
       const unsigned small = __ballot_sync(FULL, lane >= bl && lane < NOCT && blw <= Th * 0.015625);
-      const unsigned fits = __ballot_sync(FULL, lane >= bl && lane < NOCT && pre <= 0.5 * LCAP);
+      const unsigned fits = __ballot_sync(FULL, lane >= bl && lane < NOCT && pre <= 0.5 * LIST_DEEP);
       const int bt = small ? __ffs(small) - 1 : NOCT - 1;
       const int bf = fits ? 31 - __clz(fits) : bl;
       bl = max(bl, min(bt, bf));

@@ -103,7 +103,6 @@ struct c4s_ctx {
   int row_occ = 0;                             // resident row-kernel CTAs per SM
   c4s::RowJob* d_jobs = nullptr;               // fast path: per-row jobs of one chunk
   unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
-  double* d_lpv = nullptr;
   unsigned long long* d_lsb = nullptr;
   int* d_defer_rows = nullptr;                 //   rows handed to the general path, then long lists
   unsigned* d_defer_cnt = nullptr;
@@ -185,7 +184,6 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     // path for handed-back rows (-> masking of processed logits)
     a.jobs = ctx->d_jobs;
     a.lkeys = ctx->d_lkeys;
-    a.lpv = ctx->d_lpv;
     a.lsb = ctx->d_lsb;
     a.defer_rows = ctx->d_defer_rows;
     a.big_rows = ctx->d_defer_rows + K_CHUNK;
@@ -244,7 +242,6 @@ void free_all(c4s_ctx* ctx) {
   cudaFree(ctx->d_default_params);
   cudaFree(ctx->d_jobs);
   cudaFree(ctx->d_lkeys);
-  cudaFree(ctx->d_lpv);
   cudaFree(ctx->d_lsb);
   cudaFree(ctx->d_defer_rows);
   cudaFree(ctx->d_defer_cnt);
@@ -319,7 +316,6 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   const size_t nl = (size_t)c4s::K_CHUNK * c4s::LCAP;
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_jobs, (size_t)c4s::K_CHUNK * sizeof(c4s::RowJob));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lkeys, nl * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lpv, nl * sizeof(double));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, 2 * (size_t)c4s::K_CHUNK * sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, 8 * sizeof(unsigned));
