@@ -106,17 +106,9 @@ __device__ __forceinline__ double block_exscan_f64(double v, double* red, double
   return wbase + x - v;
 }
 
-// Octave/sub-bin rank of an estimate p in (0, 1]: ((0x3F800000 - bits(p)) >>
-// 15) = 256 b + s, where octave b holds p in (2^-(b+1), 2^-b] and the 256
-// sub-bins s split it linearly in p; a larger rank is a smaller p. Clamped to
-// the last (open) octave NOCT.
-__device__ __forceinline__ int est_rank(float p) {
-  const int r = (int)(0x3F800000u - __float_as_uint(p)) >> 15;
-  return min(max(r, 0), NOCT * 256 + 255);
-}
-// |d| = |y - m_y| of an element whose estimate lies in octave b is below
-// (b+1) ln 2 (up to the estimate's own tiny error); the open octave holds
-// everything down to the clamp at -200.
+// |d| = |y - m_y| of an element in octave b is below (b+1) ln 2 (up to the
+// estimate's own tiny error); the open octave NOCT holds everything down to
+// the clamp at -200.
 __device__ __forceinline__ double oct_d(int b) { return b < NOCT ? 0.6932 * (b + 1) : 200.0; }
 
 // Everything one sampled row's passes need.
@@ -853,9 +845,11 @@ __device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
 
 enum { ROW_DONE = 0, ROW_GENERAL = 1 };
 
-// Fixed-point octave mass of an estimate p (its octave b = est_rank(p) >> 8):
-// p * 2^(b+20), truncated, from the float's bits. Truncation loses less than
-// 2^-(b+20) per element, i.e. below 2^-19 of any element in octaves < NOCT.
+// Fixed-point octave mass of an estimate p in octave b (p <= 2^-b up to a
+// few ulps): p * 2^(b+20), truncated, from the float's bits (below 2^21, so
+// a bin's u32 sum over at most 2^10 elements cannot overflow). Truncation
+// loses less than 2^-(b+20) per element, i.e. below 2^-19 of any element in
+// octaves < NOCT.
 __device__ __forceinline__ unsigned oct_fix(float p, int b) {
   const unsigned u = __float_as_uint(p);
   const int sh = 130 - (int)(u >> 23) - b;        // 23 - 20 - (exponent + b)

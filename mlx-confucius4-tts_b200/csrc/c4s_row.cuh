@@ -127,6 +127,26 @@ __device__ __forceinline__ int rblock_base(int cnt, RShared& S, int* total) {
   return base;
 }
 
+// Octave of an element without top-k: b(x) = min(trunc(-t log2 e), NOCT) for
+// t = RN(x RN(1/T) - m_y), the one-FMA estimate of y - m_y. Every step is
+// monotone in x, so the elements in octaves <= bl are exactly those >= some
+// x*, and the list and its tail are separated by one comparison. An element
+// in octave b < NOCT has |t| < (b+1) ln 2, as oct_d() assumes.
+__device__ __forceinline__ float oct_t(const RowCtx& rc, float x) { return fmaf(x, rc.rT, -rc.m_y); }
+__device__ __forceinline__ int oct_of_t(float t) { return (int)fminf(t * -1.4426950408889634f, (float)NOCT); }
+
+// The smallest x with oct(x) <= bl (it exists: oct(m_x) = 0), by bisection
+// over the float order between -inf (octave NOCT > bl) and m_x.
+__device__ __forceinline__ float list_threshold(const RowCtx& rc, int bl) {
+  unsigned lo = fkey(-INFINITY), hi = fkey(rc.m_x);
+  while (hi - lo > 1u) {
+    const unsigned mid = lo + ((hi - lo) >> 1);
+    if (oct_of_t(oct_t(rc, fkey_inv(mid))) <= bl) hi = mid;
+    else lo = mid;
+  }
+  return fkey_inv(hi);
+}
+
 __device__ __forceinline__ void defer_to_general(const Args& a, int row) {
   if (threadIdx.x == 0) {
     a.jobs[row].kind = JOB_DEFER;
@@ -294,9 +314,9 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     const float4 v = rload(rb, g, rslot(g, q));
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float p = __expf(dest(rc, f4c(v, c)));
-      const int b = est_rank(p) >> 8;
-      const unsigned m = oct_fix(p, b);
+      const float t = oct_t(rc, f4c(v, c));
+      const int b = oct_of_t(t);
+      const unsigned m = oct_fix(__expf(fmaxf(t, -200.0f)), b);
       if (m) atomicAdd(&hrep[b], m);
     }
   }
@@ -355,9 +375,9 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
   if (bl < 0) return ROW_GENERAL;
   const double nb = __shfl_sync(FULL, pre, bl);
   if (nb > 2.0 * LCAP) return ROW_GENERAL;
-  // the list: elements whose estimate lies in octaves <= bl, in index order
-  const int blc = bl;
-  auto in_list = [&](float x) { return x > -INFINITY && (est_rank(__expf(dest(rc, x))) >> 8) <= blc; };
+  // the list: elements in octaves <= bl, i.e. >= x*, in index order
+  const float xs = list_threshold(rc, bl);
+  auto in_list = [&](float x) { return x >= xs; };
   int cnt = 0;
   float xmx = -INFINITY;                            // the largest element below the list
 #pragma unroll 2
