@@ -89,6 +89,7 @@ typedef struct c4s_row_params {
 #define C4S_CNT_TOPP_BINNED 3         /* top-p over more survivors than one warp sorts */
 #define C4S_CNT_DRAW_ROWPASS 4        /* draw over more survivors than one warp sorts */
 #define C4S_CNT_DEFERRED 5            /* rows the fast kernel left to the general path */
+#define C4S_CNT_EXACT_TAIL 6          /* rows without top-k decided after an exact tail sum */
 #define C4S_NUM_COUNTERS 8
 
 typedef struct c4s_ctx c4s_ctx;

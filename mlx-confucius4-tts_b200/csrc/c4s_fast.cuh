@@ -34,6 +34,7 @@ constexpr int LIST_DEEP = 1024;           // rows without top-k: lists go deeper
 constexpr int K_CHUNK = 4096;             // rows per launch sequence (list storage)
 constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
+constexpr int RQ_CAP = 16;                // list kernel: rows of one CTA waiting for an exact tail
 
 enum { JOB_NONE = 0, JOB_TOPK = 1, JOB_K0 = 2, JOB_DEFER = 3 };
 enum { RES_DONE = 0, RES_DEFER = 1, RES_REFINE = 2 };
@@ -414,7 +415,7 @@ template <bool CTA>
 __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
                                          const unsigned long long* __restrict__ keys, unsigned long long* sb,
                                          unsigned* __restrict__ vk, double* __restrict__ pv,
-                                         unsigned long long* __restrict__ hist, bool refine, LRed& R) {
+                                         unsigned long long* __restrict__ hist, bool refine, LRed& R, int* rq) {
   using G = LG<CTA>;
   const int r0 = G::rank();
   constexpr int GN = G::N;
@@ -422,10 +423,14 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
   const float m_y = J.m_y;
   const bool k0 = J.kind == JOB_K0;
   const bool forced = (a.debug & C4S_DEBUG_FORCE_BINS) != 0;
+  // rq: the list kernel CTA's queue of rows that need an exact tail
+  // (rq[0] = count, capacity RQ_CAP); elsewhere they go to the general kernel
   auto hand_back = [&](int st) {
     if (r0 == 0 && !refine) {
       J.status = st;
-      defer_row(a, row);
+      const int slot = (st == RES_REFINE && rq != nullptr) ? atomicAdd(&rq[0], 1) : RQ_CAP;
+      if (slot < RQ_CAP) rq[1 + slot] = row;
+      else defer_row(a, row);
     }
   };
   auto ykey = [&](int e) { return ((unsigned long long)vk[e] << 32) | (keys[e] & 0xffffffffull); };
@@ -741,13 +746,72 @@ constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)
 constexpr size_t LIST_SMEM = (size_t)LIST_WARPS * LW_BYTES;
 static_assert(LB_HIST + 256 * 8 <= LIST_SMEM, "a long list fits the warps' areas");
 
+// A row without top-k whose top-p crossing fell inside the band of its
+// estimated tail, in the list kernel (whole CTA): the exact tail mass (sum of
+// exp((double)(y - m_y)) over every element below the list, each penalised
+// and tempered as the reference does, re-associated: its rounding is inside
+// the list's double-sum band) replaces the estimate and the list job runs
+// again. A row still undecided goes to the general kernel.
+__device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm, unsigned* vk, double* pv,
+                                            unsigned long long* hist, LRed& R) {
+  const int V = a.V, tid = threadIdx.x;
+  RowJob& J = a.jobs[row];
+  const c4s_row_params P = a.params[(long long)row * a.params_stride];
+  bool pen = a.hist_off && P.repetition_penalty != 1.0f;
+  long long h0 = 0, h1 = 0;
+  if (pen) {
+    h0 = a.hist_off[row];
+    h1 = a.hist_off[row + 1];
+    if (h0 < 0 || h1 < h0 || h1 > a.hist_total) pen = false;   // the row kernel flagged it
+  }
+  for (int w = tid; w < (V + 31) / 32; w += NT) bm[w] = 0u;
+  csync();
+  if (pen)
+    for (long long j = h0 + tid; j < h1; j += NT) {
+      const int t = a.hist[j];
+      if ((unsigned)t < (unsigned)V) atomicOr(&bm[t >> 5], 1u << (t & 31));
+    }
+  csync();
+  const float pp = P.repetition_penalty, rpen = __frcp_rn(pp);
+  const float T = J.T;
+  const bool do_t = T != 1.0f;
+  const float rT = do_t ? __frcp_rn(T) : 1.0f;
+  const unsigned ykex = J.ykex;
+  const float m_y = J.m_y;
+  const float* g = a.logits + (long long)row * a.ld;
+  double t = 0.0;
+  for (int i = tid; i < V; i += NT) {
+    float x = g[i];
+    if (pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
+    const float y = do_t ? div_rn(x, T, rT) : x;
+    if (fkey(y) <= ykex) t += exp((double)__fsub_rn(y, m_y));
+  }
+  const double tail = LG<true>::sum(t, R);
+  if (tid == 0) {
+    J.tail = tail;
+    J.tail_err = 0.0;
+    atomicAdd(&a.counters[C4S_CNT_EXACT_TAIL], 1ull);
+  }
+  csync();
+  const size_t o = (size_t)row * LCAP;
+  if (!list_job<true>(a, row, J, a.lkeys + o, a.lsb + o, vk, pv, hist, true, R, nullptr) && tid == 0) {
+    J.status = RES_DEFER;
+    defer_row(a, row);
+  }
+}
+
 // Short lists: one warp each. Long lists (the row kernel queued them): CTAs
-// take them one at a time from a shared counter once their warps are done.
+// take them one at a time from a shared counter once their warps are done,
+// after the rows of their own that need an exact tail.
 __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   static_assert(32 * LIST_WARPS == NT, "the list kernel's CTA barrier counts NT threads");
   extern __shared__ __align__(16) unsigned char lsm[];
   __shared__ LRed R;
   __shared__ int next;
+  __shared__ int rq[1 + RQ_CAP];
+  __shared__ unsigned bm[(F_MAXV + 31) / 32 + 1];
+  if (threadIdx.x == 0) rq[0] = 0;
+  csync();
   const int w = threadIdx.x >> 5;
   const int row = blockIdx.x * LIST_WARPS + w;
   if (row < a.B) {
@@ -758,21 +822,30 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
       const size_t o = (size_t)row * LCAP;
       list_job<false>(a, row, J, a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
                       reinterpret_cast<double*>(wa + LW_PV), reinterpret_cast<unsigned long long*>(wa + LW_HIST),
-                      false, R);
+                      false, R, rq);
     }
   }
   const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
+  unsigned* bvk = reinterpret_cast<unsigned*>(lsm + LB_VK);
+  double* bpv = reinterpret_cast<double*>(lsm + LB_PV);
+  unsigned long long* bh = reinterpret_cast<unsigned long long*>(lsm + LB_HIST);
   for (;;) {
     csync();                                        // the warps' lists are done with the area
+    const int nq = min(rq[0], RQ_CAP);
+    if (nq > 0) {
+      const int r = rq[nq];
+      csync();
+      if (threadIdx.x == 0) rq[0] = nq - 1;
+      refine_in_list(a, r, bm, bvk, bpv, bh, R);
+      continue;
+    }
     if (threadIdx.x == 0) next = (int)atomicAdd(&a.defer_cnt[4], 1u);
     csync();
     const int t = next;
     if (t >= (int)nbig) break;
     const int r = a.big_rows[t];
     const size_t o = (size_t)r * LCAP;
-    list_job<true>(a, r, a.jobs[r], a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(lsm + LB_VK),
-                   reinterpret_cast<double*>(lsm + LB_PV), reinterpret_cast<unsigned long long*>(lsm + LB_HIST),
-                   false, R);
+    list_job<true>(a, r, a.jobs[r], a.lkeys + o, a.lsb + o, bvk, bpv, bh, false, R, rq);
   }
 }
 
@@ -890,73 +963,9 @@ __device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf
 // The general path for the rows the row and list kernels handed back; the
 // last CTA to finish clears the hand-back list for the next launch sequence.
 // ---------------------------------------------------------------------------
-// A no-top-k row whose top-p decision fell inside the band of its estimated
-// tail: the exact tail mass (sum of exp((double)(y - m_y)) over the elements
-// below the list, re-associated; its rounding is inside the list's double-sum
-// band) replaces the estimate and the list job runs again on warp 0.
-// Returns 1 if the row is finished, 0 if it needs the general path, -1 if the
-// staging wait gave up.
-__device__ __noinline__ int refine_k0(const Args& a, int row, float* rowbuf, unsigned* bitmap, Shared& S,
-                                      LRed& R, unsigned long long* hist, unsigned* vk_area, double* pv_area,
-                                      unsigned& phase) {
-  const int V = a.V;
-  const int tid = threadIdx.x;
-  const c4s_row_params P = a.params[(long long)row * a.params_stride];
-  const Stage sg = stage_issue(a.logits + (long long)row * a.ld, V, rowbuf, &S.bar);
-  const bool pen = a.hist_off && P.repetition_penalty != 1.0f;
-  long long h0, h1;
-  hist_window(a, row, pen, h0, h1);
-  int hid[8];
-  hist_prefetch(a, h0, h1, hid);
-  if (pen)
-    for (int w = tid; w < (V + 31) / 32; w += NT) bitmap[w] = 0u;
-  if (!stage_wait(a, sg, &S.bar, phase, S)) return -1;
-  float* srow = rowbuf + sg.shift;
-  if (pen) penalty_apply(a, srow, V, bitmap, P.repetition_penalty, hid, h0, h1);
-  RowJob& J = a.jobs[row];
-  const float T = P.temperature;
-  const bool do_t = !(T == 1.0f || T <= 0.0f);
-  const float rT = do_t ? __frcp_rn(T) : 1.0f;
-  const unsigned ykex = J.ykex;
-  const float m_y = J.m_y;
-  double t = 0.0;
-  for (int i = tid; i < V; i += NT) {
-    const float y = do_t ? div_rn(srow[i], T, rT) : srow[i];
-    if (fkey(y) <= ykex) t += prob(y, m_y);
-  }
-  double tail;
-  block_exscan_f64(t, S.redd, &tail);
-  if (tid == 0) {
-    J.tail = tail;
-    J.tail_err = 0.0;
-  }
-  csync();
-  // the staged list: probabilities in the row buffer (free once the tail is
-  // summed) and value keys in the sort-key and probability areas (4 LIST_CAP
-  // entries; they are adjacent), or -- rows too short for that -- keys in the
-  // sort-key area (2 LIST_CAP) and probabilities in the probability area
-  const int n = J.n;
-  double* pvs = nullptr;
-  int vcap = 0;
-  if ((size_t)n * 8 <= align_up((size_t)(V + 4) * 4, 16)) {
-    pvs = reinterpret_cast<double*>(rowbuf);
-    vcap = 4 * LIST_CAP;
-  } else if (n <= LIST_CAP) {
-    pvs = pv_area;
-    vcap = 2 * LIST_CAP;
-  }
-  if (pvs == nullptr || n > vcap) return 0;
-  const size_t o = (size_t)row * LCAP;
-  const bool done = list_job<true>(a, row, J, a.lkeys + o, a.lsb + o, vk_area, pvs, hist, true, R);
-  csync();
-  return done ? 1 : 0;
-}
-
 __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ Shared S;
-  __shared__ LRed R;
-  __shared__ unsigned long long lhist[256];
   const Layout L = layout_for(a.V);
   float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
@@ -970,11 +979,6 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   const unsigned n = *reinterpret_cast<volatile unsigned*>(a.defer_cnt);
   for (unsigned t = blockIdx.x; t < n; t += gridDim.x) {
     const int row = a.defer_rows[t];
-    if (a.jobs[row].kind == JOB_K0 && a.jobs[row].status == RES_REFINE) {
-      const int r = refine_k0(a, row, rowbuf, bitmap, S, R, lhist, reinterpret_cast<unsigned*>(lkey), pv, phase);
-      if (r < 0) break;
-      if (r > 0) continue;
-    }
     if (!general_row(a, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) break;
   }
   csync();

@@ -37,7 +37,7 @@ DEBUG_FORCE_EXACT = 1
 DEBUG_FORCE_BINS = 2
 DEBUG_FORCE_REFINE = 4
 COUNTER_NAMES = ("topp_exact_fallback", "draw_exact_fallback", "topk_radix",
-                 "topp_binned", "draw_rowpass", "deferred")
+                 "topp_binned", "draw_rowpass", "deferred", "exact_tail")
 MAX_VOCAB = 32768
 
 _STATUS = {0: "ok", -1: "invalid argument", -2: "CUDA error", -3: "capacity exceeded",

@@ -198,7 +198,7 @@ def test_forced_slow_paths(c4s, oracle, wl, flags):
     if flags & 1:
         assert cnt["topk_radix"] > 0
     if flags & 4:
-        assert cnt["deferred"] > 0
+        assert cnt["exact_tail"] > 0
 
 
 def test_path_counters_and_no_errors(ctx, wl):
