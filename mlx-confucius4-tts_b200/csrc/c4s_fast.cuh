@@ -156,6 +156,7 @@ __device__ __forceinline__ void defer_row(const Args& a, int row) {
 // Reduction scratch of a list job run by a whole CTA.
 struct LRed {
   double d[NWARP];
+  double d3[NWARP][3];
   unsigned long long q[NWARP];
   int i[NWARP];
   int e;
@@ -182,6 +183,23 @@ struct LG {
     for (int w = 0; w < NWARP; ++w) s += R.d[w];
     csync();
     return s;
+  }
+  // Three sums at once (one pair of barriers in a CTA).
+  __device__ static void sum3(double& x, double& y, double& z, LRed& R) {
+    x = warp_sum_d(x);
+    y = warp_sum_d(y);
+    z = warp_sum_d(z);
+    if (!CTA) return;
+    if ((threadIdx.x & 31) == 0) {
+      R.d3[threadIdx.x >> 5][0] = x;
+      R.d3[threadIdx.x >> 5][1] = y;
+      R.d3[threadIdx.x >> 5][2] = z;
+    }
+    csync();
+    x = y = z = 0.0;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) { x += R.d3[w][0]; y += R.d3[w][1]; z += R.d3[w][2]; }
+    csync();
   }
   __device__ static int add(int v, LRed& R) {
     v = __reduce_add_sync(FULL, v);
@@ -387,6 +405,26 @@ __device__ __forceinline__ unsigned bisect_mass(const unsigned* __restrict__ vk,
                                                 unsigned prefix, int b0, double base, double Th, LRed& R) {
   using G = LG<CTA>;
   unsigned v = prefix;
+  if (CTA) {
+    // two bits per step: three thresholds, one pair of CTA barriers
+    for (int b = b0; b >= 0; b -= 2) {
+      const int lo = b >= 1 ? b - 1 : 0;
+      const unsigned c0 = v | (1u << lo), c1 = v | (2u << lo), c2 = v | (3u << lo);
+      double g0 = 0.0, g1 = 0.0, g2 = 0.0;
+      for (int e = G::rank(); e < n; e += G::N) {
+        const unsigned x = vk[e];
+        const double p = pv[e];
+        g0 += x < c0 ? p : 0.0;
+        g1 += x < c1 ? p : 0.0;
+        g2 += x < c2 ? p : 0.0;
+      }
+      G::sum3(g0, g1, g2, R);
+      if (lo < b && base + g2 <= Th) v = c2;
+      else if (lo < b && base + g1 <= Th) v = c1;
+      else if (base + g0 <= Th) v = c0;
+    }
+    return v;
+  }
   for (int b = b0; b >= 0; --b) {
     const unsigned c = v | (1u << b);
     double g0 = 0.0, g1 = 0.0;
@@ -780,11 +818,18 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
   const float m_y = J.m_y;
   const float* g = a.logits + (long long)row * a.ld;
   double t = 0.0;
-  for (int i = tid; i < V; i += NT) {
-    float x = g[i];
-    if (pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
-    const float y = do_t ? div_rn(x, T, rT) : x;
-    if (fkey(y) <= ykex) t += exp((double)__fsub_rn(y, m_y));
+  for (int i0 = tid; i0 < V; i0 += 8 * NT) {
+    float xv[8];                                    // eight loads in flight per thread
+#pragma unroll
+    for (int q = 0; q < 8; ++q) xv[q] = i0 + q * NT < V ? __ldcs(g + i0 + q * NT) : -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = i0 + q * NT;
+      float x = xv[q];
+      if (i < V && pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
+      const float y = do_t ? div_rn(x, T, rT) : x;
+      if (x > -INFINITY && fkey(y) <= ykex) t += exp((double)__fsub_rn(y, m_y));
+    }
   }
   const double tail = LG<true>::sum(t, R);
   if (tid == 0) {
