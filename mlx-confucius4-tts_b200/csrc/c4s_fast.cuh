@@ -845,9 +845,11 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
   }
 }
 
-// Short lists: one warp each. Long lists (the row kernel queued them): CTAs
-// take them one at a time from a shared counter once their warps are done,
-// after the rows of their own that need an exact tail.
+// Persistent: first the long lists (the row kernel queued them; one CTA
+// each, so the longest work starts at once), then the short lists, one warp
+// each, handed out row by row; between them each CTA refines the rows of its
+// own that need an exact tail. Counters: defer_cnt[4] long-list ticket,
+// defer_cnt[5] row ticket (the general kernel resets them).
 __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   static_assert(32 * LIST_WARPS == NT, "the list kernel's CTA barrier counts NT threads");
   extern __shared__ __align__(16) unsigned char lsm[];
@@ -856,42 +858,50 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   __shared__ int rq[1 + RQ_CAP];
   __shared__ unsigned bm[(F_MAXV + 31) / 32 + 1];
   if (threadIdx.x == 0) rq[0] = 0;
-  csync();
-  const int w = threadIdx.x >> 5;
-  const int row = blockIdx.x * LIST_WARPS + w;
-  if (row < a.B) {
+  const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
+  unsigned* bvk = reinterpret_cast<unsigned*>(lsm + LB_VK);
+  double* bpv = reinterpret_cast<double*>(lsm + LB_PV);
+  unsigned long long* bh = reinterpret_cast<unsigned long long*>(lsm + LB_HIST);
+  // the CTA's queued refinements, then the next long list; false when none is left
+  auto cta_work = [&]() -> bool {
+    for (;;) {
+      csync();                                      // the area is free
+      const int nq = min(rq[0], RQ_CAP);
+      if (nq > 0) {
+        const int r = rq[nq];
+        csync();
+        if (threadIdx.x == 0) rq[0] = nq - 1;
+        refine_in_list(a, r, bm, bvk, bpv, bh, R);
+        continue;
+      }
+      if (threadIdx.x == 0) next = (int)atomicAdd(&a.defer_cnt[4], 1u);
+      csync();
+      const int t = next;
+      if (t >= (int)nbig) return false;
+      const int r = a.big_rows[t];
+      const size_t o = (size_t)r * LCAP;
+      list_job<true>(a, r, a.jobs[r], a.lkeys + o, a.lsb + o, bvk, bpv, bh, false, R, rq);
+    }
+  };
+  cta_work();
+  // short lists: each warp takes rows one at a time
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned char* wa = lsm + (size_t)w * LW_BYTES;
+  for (;;) {
+    int row = 0;
+    if (lane == 0) row = (int)atomicAdd(&a.defer_cnt[5], 1u);
+    row = __shfl_sync(FULL, row, 0);
+    if (row >= a.B) break;
     RowJob& J = a.jobs[row];
     const int kind = J.kind;
     if ((kind == JOB_TOPK || kind == JOB_K0) && J.n <= LW_CAP) {
-      unsigned char* wa = lsm + (size_t)w * LW_BYTES;
       const size_t o = (size_t)row * LCAP;
       list_job<false>(a, row, J, a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
                       reinterpret_cast<double*>(wa + LW_PV), reinterpret_cast<unsigned long long*>(wa + LW_HIST),
                       false, R, rq);
     }
   }
-  const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
-  unsigned* bvk = reinterpret_cast<unsigned*>(lsm + LB_VK);
-  double* bpv = reinterpret_cast<double*>(lsm + LB_PV);
-  unsigned long long* bh = reinterpret_cast<unsigned long long*>(lsm + LB_HIST);
-  for (;;) {
-    csync();                                        // the warps' lists are done with the area
-    const int nq = min(rq[0], RQ_CAP);
-    if (nq > 0) {
-      const int r = rq[nq];
-      csync();
-      if (threadIdx.x == 0) rq[0] = nq - 1;
-      refine_in_list(a, r, bm, bvk, bpv, bh, R);
-      continue;
-    }
-    if (threadIdx.x == 0) next = (int)atomicAdd(&a.defer_cnt[4], 1u);
-    csync();
-    const int t = next;
-    if (t >= (int)nbig) break;
-    const int r = a.big_rows[t];
-    const size_t o = (size_t)r * LCAP;
-    list_job<true>(a, r, a.jobs[r], a.lkeys + o, a.lsb + o, bvk, bpv, bh, false, R, rq);
-  }
+  cta_work();                                       // refinements found on the short lists
 }
 
 // ===========================================================================
@@ -1035,6 +1045,7 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
       a.defer_cnt[2] = 0u;                          // the row kernel's row counter
       a.defer_cnt[3] = 0u;                          // long lists queued for the list kernel
       a.defer_cnt[4] = 0u;                          //   and the list kernel's ticket
+      a.defer_cnt[5] = 0u;                          //   and its row ticket
     }
   }
 }

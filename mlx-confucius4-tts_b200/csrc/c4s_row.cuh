@@ -402,13 +402,13 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
   for (int w = 1; w < RWARP; ++w) kx = kx > S.redu[w] ? kx : S.redu[w];
   const float xm = fkey_inv(kx);
   write_list(keys, base, rb, g, in_list);
-  const double tl = __shfl_sync(FULL, blw, bl), et = __shfl_sync(FULL, wblw, bl);   // whole warp
+  const double tl = __shfl_sync(FULL, blw, bl), tl_err = est_err(tl, __shfl_sync(FULL, wblw, bl), rc.m_y, 33, V);
   if (tid == 0) {
     RowJob& J = a.jobs[row];
     fill_job(J, rc, JOB_K0, ng, 0);
     queue_long_list(a, row, ng);
     J.tail = tl;
-    J.tail_err = est_err(tl, et, rc.m_y, 33, V);
+    J.tail_err = tl_err;
     J.ykex = xm > -INFINITY ? fkey(yex(rc, xm)) : 0u;
   }
   if (a.out_logits) write_row_smem(a, rb, g, rc, true);

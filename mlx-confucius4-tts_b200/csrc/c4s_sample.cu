@@ -211,7 +211,8 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       if (ev) cudaEventRecord(ev[0], st);
       row_kernel<<<g1, RT, R_SMEM, st>>>(ac);
       if (ev) cudaEventRecord(ev[1], st);
-      list_kernel<<<(ac.B + LIST_WARPS - 1) / LIST_WARPS, 32 * LIST_WARPS, LIST_SMEM, st>>>(ac);
+      const int g2 = (int)std::min<long long>((ac.B + LIST_WARPS - 1) / LIST_WARPS, 2LL * ctx->num_sms);
+      list_kernel<<<g2, 32 * LIST_WARPS, LIST_SMEM, st>>>(ac);
       if (ev) cudaEventRecord(ev[2], st);
       const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
       defer_kernel<<<g3, NT, gsm, st>>>(ac);
