@@ -327,6 +327,58 @@ __device__ void group_bitonic(unsigned long long* b, int np) {
   }
 }
 
+// Ascending bitonic sort of 32*SL keys held SL per lane (lane l: positions
+// SL*l .. SL*l+SL-1), in registers: within-lane stages by compare-exchange,
+// the others by shuffles. Whole warp calls.
+template <int SL>
+__device__ __forceinline__ void warp_sort_regs(unsigned (&v)[SL]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32 * SL; k <<= 1) {
+#pragma unroll
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      if (jj < SL) {
+#pragma unroll
+        for (int j = 0; j < SL; ++j) {
+          const int p = j ^ jj;
+          if (p > j) {
+            const bool up = ((SL * lane + j) & k) == 0;
+            const unsigned lo = min(v[j], v[p]), hi = max(v[j], v[p]);
+            v[j] = up ? lo : hi;
+            v[p] = up ? hi : lo;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < SL; ++j) {
+          const unsigned o = __shfl_xor_sync(FULL, v[j], jj / SL);
+          const int i = SL * lane + j;
+          const bool keep_min = ((i & jj) == 0) == ((i & k) == 0);
+          v[j] = keep_min ? min(v[j], o) : max(v[j], o);
+        }
+      }
+    }
+  }
+}
+
+// The k-th largest of n <= 32*SL value keys staged in vk (one warp).
+template <int SL>
+__device__ __forceinline__ unsigned warp_kth_sorted(const unsigned* vk, int n, int k) {
+  const int lane = threadIdx.x & 31;
+  unsigned v[SL];
+#pragma unroll
+  for (int j = 0; j < SL; ++j) {
+    const int e = SL * lane + j;
+    v[j] = e < n ? vk[e] : 0u;                     // padding sorts first
+  }
+  warp_sort_regs<SL>(v);
+  const int pos = 32 * SL - k;
+  unsigned r = 0u;
+#pragma unroll
+  for (int j = 0; j < SL; ++j) r = (pos % SL == j) ? v[j] : r;
+  return __shfl_sync(FULL, r, pos / SL);
+}
+
 // Radix searches of a list job over the value keys that share `prefix` above
 // bit b0 (8 bits per pass, histogram `hist` of 256 bins in shared memory).
 // topk: the largest v with count(vkey >= v) >= k, i.e. the k-th largest key.
@@ -508,7 +560,10 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
   if (k > 0 && k < n && vmin != vmax) {
     const int b0 = 31 - __clz((unsigned)(vmin ^ vmax));
     const unsigned v = b0 >= 31 ? 0u : ((unsigned)vmax & ~((2u << b0) - 1u));
-    tk = radix_kth<CTA>(vk, n, v, b0, k, hist, R);
+    if (!CTA && n <= 64) tk = warp_kth_sorted<2>(vk, n, k);
+    else if (!CTA && n <= 128) tk = warp_kth_sorted<4>(vk, n, k);
+    else if (!CTA && n <= 256) tk = warp_kth_sorted<8>(vk, n, k);
+    else tk = radix_kth<CTA>(vk, n, v, b0, k, hist, R);
   }
 
   // ---- exact probabilities of the survivors (sampling.cpp:52-55) ----

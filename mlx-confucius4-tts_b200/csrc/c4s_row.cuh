@@ -512,8 +512,25 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
             }
           }
         };
+        // claim the ids first (independent atomics in flight together), then
+        // penalise the ones this thread claimed first
+        unsigned first = 0u;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) apply(hid[q]);
+        for (int q = 0; q < 16; ++q) {
+          const int t = hid[q];
+          if ((unsigned)t < (unsigned)V) {
+            const unsigned bit = 1u << (t & 31);
+            if (!(atomicOr(&S.bm[t >> 5], bit) & bit)) first |= 1u << q;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if (first & (1u << q)) {
+            const int t = hid[q];
+            const float sv = srow[t];
+            srow[t] = (sv < 0.0f) ? __fmul_rn(sv, pv) : div_rn(sv, pv, rpen);
+          }
+        }
         for (long long jj = h0 + tid + 16LL * RT; jj < h1; jj += RT) apply(a.hist[jj]);
         rsync();
       }
