@@ -457,7 +457,7 @@ __device__ __forceinline__ unsigned bisect_mass(const unsigned* __restrict__ vk,
                                                 unsigned prefix, int b0, double base, double Th, LRed& R) {
   using G = LG<CTA>;
   unsigned v = prefix;
-  if (CTA) {
+  if constexpr (CTA) {
     // two bits per step: three thresholds, one pair of CTA barriers
     for (int b = b0; b >= 0; b -= 2) {
       const int lo = b >= 1 ? b - 1 : 0;
@@ -476,19 +476,20 @@ __device__ __forceinline__ unsigned bisect_mass(const unsigned* __restrict__ vk,
       else if (base + g0 <= Th) v = c0;
     }
     return v;
-  }
-  for (int b = b0; b >= 0; --b) {
-    const unsigned c = v | (1u << b);
-    double g0 = 0.0, g1 = 0.0;
-    int e = G::rank();
-    for (; e + G::N < n; e += 2 * G::N) {
-      g0 += vk[e] < c ? pv[e] : 0.0;
-      g1 += vk[e + G::N] < c ? pv[e + G::N] : 0.0;
+  } else {
+    for (int b = b0; b >= 0; --b) {
+      const unsigned c = v | (1u << b);
+      double g0 = 0.0, g1 = 0.0;
+      int e = G::rank();
+      for (; e + G::N < n; e += 2 * G::N) {
+        g0 += vk[e] < c ? pv[e] : 0.0;
+        g1 += vk[e + G::N] < c ? pv[e + G::N] : 0.0;
+      }
+      if (e < n) g0 += vk[e] < c ? pv[e] : 0.0;
+      if (base + G::sum(g0 + g1, R) <= Th) v = c;
     }
-    if (e < n) g0 += vk[e] < c ? pv[e] : 0.0;
-    if (base + G::sum(g0 + g1, R) <= Th) v = c;
+    return v;
   }
-  return v;
 }
 
 // One list job. keys[0..n) (global): ckey(x, i) of the candidates' penalised,
@@ -836,8 +837,8 @@ constexpr int LW_CAP = 1024;                  // longest list one warp takes
 constexpr size_t LW_VK = 0, LW_PV = (size_t)LW_CAP * 4, LW_HIST = LW_PV + (size_t)LW_CAP * 8;
 constexpr size_t LW_BYTES = LW_HIST + 256 * 8;            // per warp
 constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)LCAP * 8;
-constexpr size_t LIST_SMEM = (size_t)LIST_WARPS * LW_BYTES;
-static_assert(LB_HIST + 256 * 8 <= LIST_SMEM, "a long list fits the warps' areas");
+constexpr size_t LIST_SMEM_W = (size_t)LIST_WARPS * LW_BYTES, LIST_SMEM_B = LB_HIST + 256 * 8;
+constexpr size_t LIST_SMEM = LIST_SMEM_W > LIST_SMEM_B ? LIST_SMEM_W : LIST_SMEM_B;   // warps' areas / one long list
 
 // A row without top-k whose top-p crossing fell inside the band of its
 // estimated tail, in the list kernel (whole CTA): the exact tail mass (sum of
@@ -1028,14 +1029,13 @@ __device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
 
 enum { ROW_DONE = 0, ROW_GENERAL = 1 };
 
-// Fixed-point octave mass of an estimate p in octave b (p <= 2^-b up to a
-// few ulps): p * 2^(b+20), truncated, from the float's bits (below 2^21, so
-// a bin's u32 sum over at most 2^10 elements cannot overflow). Truncation
-// loses less than 2^-(b+20) per element, i.e. below 2^-19 of any element in
-// octaves < NOCT.
+// Fixed-point octave mass of p in octave b (p <= 2^-b up to a few ulps):
+// p * 2^(b+22), truncated, from the float's bits (below 2^23, so a bin's u32
+// sum over at most 2^9 elements cannot overflow). Truncation loses less than
+// 2^-(b+22) per element, i.e. below 2^-21 of any element in octaves < NOCT.
 __device__ __forceinline__ unsigned oct_fix(float p, int b) {
   const unsigned u = __float_as_uint(p);
-  const int sh = 130 - (int)(u >> 23) - b;        // 23 - 20 - (exponent + b)
+  const int sh = 128 - (int)(u >> 23) - b;        // 23 - 22 - (exponent - 127 + b)
   const unsigned m = (u & 0x007fffffu) | 0x00800000u;
   return (u == 0u || sh > 31) ? 0u : (m >> max(sh, 0));
 }
