@@ -35,6 +35,8 @@ constexpr int K_CHUNK = 4096;             // rows per launch sequence (list stor
 constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
 constexpr int RQ_CAP = 16;                // list kernel: rows of one CTA waiting for an exact tail
+constexpr int LIST_MID = 128;             // lists longer than this are taken before the short ones
+constexpr int NCNT = 16;                  // slots of the per-launch counters (defer_cnt)
 
 enum { JOB_NONE = 0, JOB_TOPK = 1, JOB_K0 = 2, JOB_DEFER = 3 };
 enum { RES_DONE = 0, RES_DEFER = 1, RES_REFINE = 2 };
@@ -901,11 +903,10 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
   }
 }
 
-// Persistent: first the long lists (the row kernel queued them; one CTA
-// each, so the longest work starts at once), then the short lists, one warp
-// each, handed out row by row; between them each CTA refines the rows of its
-// own that need an exact tail. Counters: defer_cnt[4] long-list ticket,
-// defer_cnt[5] row ticket (the general kernel resets them).
+// Persistent: first the long lists (one CTA each, so the longest work starts
+// at once), then the mid-size and the short lists (one warp each), all from
+// the queues the row kernel fills; between them each CTA refines the rows of
+// its own that need an exact tail (the general kernel resets the queues).
 __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   static_assert(32 * LIST_WARPS == NT, "the list kernel's CTA barrier counts NT threads");
   extern __shared__ __align__(16) unsigned char lsm[];
@@ -940,19 +941,19 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
     }
   };
   cta_work();
-  // short lists: each warp takes rows one at a time
+  // the other lists, one warp each, mid-size before short (longest first)
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* wa = lsm + (size_t)w * LW_BYTES;
-  for (;;) {
-    int row = 0;
-    if (lane == 0) row = (int)atomicAdd(&a.defer_cnt[5], 1u);
-    row = __shfl_sync(FULL, row, 0);
-    if (row >= a.B) break;
-    RowJob& J = a.jobs[row];
-    const int kind = J.kind;
-    if ((kind == JOB_TOPK || kind == JOB_K0) && J.n <= LW_CAP) {
+  for (int q = 1; q <= 2; ++q) {
+    const unsigned nq = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3 + 2 * q]);
+    for (;;) {
+      unsigned t = 0u;
+      if (lane == 0) t = atomicAdd(&a.defer_cnt[4 + 2 * q], 1u);
+      t = __shfl_sync(FULL, t, 0);
+      if (t >= nq) break;
+      const int row = a.big_rows[(size_t)q * K_CHUNK + t];
       const size_t o = (size_t)row * LCAP;
-      list_job<false>(a, row, J, a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
+      list_job<false>(a, row, a.jobs[row], a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
                       reinterpret_cast<double*>(wa + LW_PV), reinterpret_cast<unsigned long long*>(wa + LW_HIST),
                       false, R, rq);
     }
@@ -1024,18 +1025,20 @@ __device__ __forceinline__ void fill_job(RowJob& J, const RowCtx& rc, int kind, 
 
 // A list longer than one list-kernel warp takes goes to the CTA-wide queue.
 __device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
-  if (n > LW_CAP) a.big_rows[atomicAdd(&a.defer_cnt[3], 1u)] = row;
+  const int q = n > LW_CAP ? 0 : (n > LIST_MID ? 1 : 2);
+  a.big_rows[(size_t)q * K_CHUNK + atomicAdd(&a.defer_cnt[3 + 2 * q], 1u)] = row;
 }
 
 enum { ROW_DONE = 0, ROW_GENERAL = 1 };
 
-// Fixed-point octave mass of p in octave b (p <= 2^-b up to a few ulps):
-// p * 2^(b+22), truncated, from the float's bits (below 2^23, so a bin's u32
-// sum over at most 2^9 elements cannot overflow). Truncation loses less than
-// 2^-(b+22) per element, i.e. below 2^-21 of any element in octaves < NOCT.
+// Fixed-point octave mass of an estimate p in octave b (p <= 2^-b up to a
+// few ulps): p * 2^(b+20), truncated, from the float's bits (below 2^21, so
+// a bin's u32 sum over at most 2^10 elements cannot overflow). Truncation
+// loses less than 2^-(b+20) per element, i.e. below 2^-19 of any element in
+// octaves < NOCT.
 __device__ __forceinline__ unsigned oct_fix(float p, int b) {
   const unsigned u = __float_as_uint(p);
-  const int sh = 128 - (int)(u >> 23) - b;        // 23 - 22 - (exponent - 127 + b)
+  const int sh = 130 - (int)(u >> 23) - b;        // 23 - 20 - (exponent + b)
   const unsigned m = (u & 0x007fffffu) | 0x00800000u;
   return (u == 0u || sh > 31) ? 0u : (m >> max(sh, 0));
 }
@@ -1098,9 +1101,8 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
       a.defer_cnt[0] = 0u;
       a.defer_cnt[1] = 0u;
       a.defer_cnt[2] = 0u;                          // the row kernel's row counter
-      a.defer_cnt[3] = 0u;                          // long lists queued for the list kernel
-      a.defer_cnt[4] = 0u;                          //   and the list kernel's ticket
-      a.defer_cnt[5] = 0u;                          //   and its row ticket
+#pragma unroll
+      for (int c = 3; c <= 8; ++c) a.defer_cnt[c] = 0u;   // the list kernel's queues
     }
   }
 }

@@ -44,7 +44,8 @@ struct Args {
   int* defer_rows;              // rows handed to the general path
   int* big_rows;                // rows whose lists the list kernel works with a whole CTA
   unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done, [2] row counter,
-                                // [3] long lists queued, [4] list-kernel ticket, [5] its row ticket
+                                // list queues: [3]/[4] long lists queued/taken, [5]/[6] mid-size,
+                                // [7]/[8] short (rows in big_rows + q * K_CHUNK, q = 0, 1, 2)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

@@ -19,7 +19,7 @@
 //   rows without top-k: an octave histogram of error-bounded estimates of
 //     exp(y - m_y) locates the top-p crossing; the octaves down to it (and a
 //     little deeper while the list stays short) form the list, the rest an
-//     estimated tail with a proven error bound (oct_err);
+//     estimated tail with a proven error bound (est_err);
 //   everything else (non-finite maxima, |m_y| >= 2^18, min_tokens_to_keep
 //   != 1, lists over LCAP, an undecidable crossing octave) goes to the
 //   general path (defer_kernel).
@@ -127,22 +127,13 @@ __device__ __forceinline__ int rblock_base(int cnt, RShared& S, int* total) {
   return base;
 }
 
-// Octave of an element without top-k: b(x) = min(trunc(-d log2 e), NOCT) for
-// d = fl(fl(x/T) - m_y), the reference's own exponent (sampling.cpp:16,52).
-// Every step is monotone in x, so the elements in octaves <= bl are exactly
-// those >= some x*, and the list and its tail are separated by one
-// comparison. An element in octave b < NOCT has |d| < (b+1) ln 2.
-__device__ __forceinline__ float oct_t(const RowCtx& rc, float x) { return __fsub_rn(yex(rc, x), rc.m_y); }
+// Octave of an element without top-k: b(x) = min(trunc(-t log2 e), NOCT) for
+// t = RN(x RN(1/T) - m_y), the one-FMA estimate of y - m_y. Every step is
+// monotone in x, so the elements in octaves <= bl are exactly those >= some
+// x*, and the list and its tail are separated by one comparison. An element
+// in octave b < NOCT has |t| < (b+1) ln 2, as oct_d() assumes.
+__device__ __forceinline__ float oct_t(const RowCtx& rc, float x) { return fmaf(x, rc.rT, -rc.m_y); }
 __device__ __forceinline__ int oct_of_t(float t) { return (int)fminf(t * -1.4426950408889634f, (float)NOCT); }
-
-// Error bound of a sum `mass` of octave-bin masses: per element, expf is
-// within 2 ulps (CUDA's documented bound; 4u relative, u = 2^-24) of e^d and
-// the 2^-(b+22) fixed point truncates less than 2^-21 = 8u of it (an element
-// of octave b is >= 2^-(b+1)); bins add exactly; the rest is the result
-// rounding. 16u with margin, plus 2^-126 for each result flushed to zero.
-__device__ __forceinline__ double oct_err(double mass, int nelem) {
-  return U24 * 16.0 * mass + (double)nelem * 1.1754943508222875e-38;
-}
 
 // The smallest x with oct(x) <= bl (it exists: oct(m_x) = 0), by bisection
 // over the float order between -inf (octave NOCT > bl) and m_x.
@@ -323,13 +314,10 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     const float4 v = rload(rb, g, rslot(g, q));
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float x = f4c(v, c);
-      if (x > -INFINITY) {
-        const float t = oct_t(rc, x);
-        const int b = oct_of_t(t);
-        const unsigned m = oct_fix(expf(t), b);
-        if (m) atomicAdd(&hrep[b], m);
-      }
+      const float t = oct_t(rc, f4c(v, c));
+      const int b = oct_of_t(t);
+      const unsigned m = oct_fix(__expf(fmaxf(t, -200.0f)), b);
+      if (m) atomicAdd(&hrep[b], m);
     }
   }
   rsync();
@@ -342,13 +330,14 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     for (int w = 0; w < RWARP; ++w)
 #pragma unroll
       for (int r = 0; r < HREP; ++r) qs += S.hw[w][r][lane];
-    o = ldexp((double)qs, -(lane + 22));
+    o = ldexp((double)qs, -(lane + 20));
   }
-  double suf = o;                                   // sums over octaves >= lane
+  const double wo = o * oct_d(lane <= NOCT ? lane : NOCT);
+  double suf = o, wsuf = wo;                        // sums over octaves >= lane
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    const double t1 = __shfl_down_sync(FULL, suf, off);
-    if (lane + off < 32) suf += t1;
+    const double t1 = __shfl_down_sync(FULL, suf, off), t2d = __shfl_down_sync(FULL, wsuf, off);
+    if (lane + off < 32) { suf += t1; wsuf += t2d; }
   }
   double pre = o * ldexp(1.0, lane + 1);            // count bound of octaves <= lane
 #pragma unroll
@@ -357,11 +346,11 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     if (lane >= off) pre += t;
   }
   const double Se = __shfl_sync(FULL, suf, 0);
-  const double below = __shfl_down_sync(FULL, suf, 1);
-  const double blw = lane < 31 ? below : 0.0;       // mass of the octaves > lane
+  const double below = __shfl_down_sync(FULL, suf, 1), wbelow = __shfl_down_sync(FULL, wsuf, 1);
+  const double blw = lane < 31 ? below : 0.0, wblw = lane < 31 ? wbelow : 0.0;   // octaves > lane
   const double Th = rc.thr * Se;
   const double rnd = 2.0 * ((4.0 * V + 16.0) * U53 * Se);
-  const double es = oct_err(Se, V);
+  const double es = est_err(Se, __shfl_sync(FULL, wsuf, 0), rc.m_y, 33, V);
   int bl = -1;
   {
     // crossing octave: suffix sum (from the deep end) first exceeds Th
@@ -369,7 +358,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
     const int bc = cr ? 31 - __clz(cr) : -1;
     if (bc < 0 || bc == NOCT) return ROW_GENERAL;
     // the list: octaves 0..bl, bl >= bc the first whose tail is clearly below Th
-    const bool okl = lane >= bc && lane < NOCT && blw + 2.0 * oct_err(blw, V) + rc.thr * es + rnd < Th;
+    const bool okl = lane >= bc && lane < NOCT && blw + 2.0 * est_err(blw, wblw, rc.m_y, 33, V) + rc.thr * es + rnd < Th;
     const unsigned lb = __ballot_sync(FULL, okl);
     bl = lb ? __ffs(lb) - 1 : -1;
     if (bl >= 0) {
@@ -413,7 +402,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
   for (int w = 1; w < RWARP; ++w) kx = kx > S.redu[w] ? kx : S.redu[w];
   const float xm = fkey_inv(kx);
   write_list(keys, base, rb, g, in_list);
-  const double tl = __shfl_sync(FULL, blw, bl), tl_err = oct_err(tl, V);
+  const double tl = __shfl_sync(FULL, blw, bl), tl_err = est_err(tl, __shfl_sync(FULL, wblw, bl), rc.m_y, 33, V);
   if (tid == 0) {
     RowJob& J = a.jobs[row];
     fill_job(J, rc, JOB_K0, ng, 0);
