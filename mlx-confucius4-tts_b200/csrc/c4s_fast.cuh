@@ -35,8 +35,9 @@ constexpr int K_CHUNK = 4096;             // rows per launch sequence (list stor
 constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
 constexpr int RQ_CAP = 16;                // list kernel: rows of one CTA waiting for an exact tail
-constexpr int LIST_MID = 128;             // lists longer than this are taken before the short ones
+constexpr int LIST_CLASSES = 6;           // list queues: long (CTA), then warp lists by size, longest first
 constexpr int NCNT = 16;                  // slots of the per-launch counters (defer_cnt)
+static_assert(3 + 2 * LIST_CLASSES <= NCNT, "the queue counters fit");
 
 enum { JOB_NONE = 0, JOB_TOPK = 1, JOB_K0 = 2, JOB_DEFER = 3 };
 enum { RES_DONE = 0, RES_DEFER = 1, RES_REFINE = 2 };
@@ -904,9 +905,10 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
 }
 
 // Persistent: first the long lists (one CTA each, so the longest work starts
-// at once), then the mid-size and the short lists (one warp each), all from
-// the queues the row kernel fills; between them each CTA refines the rows of
-// its own that need an exact tail (the general kernel resets the queues).
+// at once), then the other lists (one warp each) by size class, longest
+// first, all from the queues the row kernel fills; between them each CTA
+// refines the rows of its own that need an exact tail (the general kernel
+// resets the queues).
 __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   static_assert(32 * LIST_WARPS == NT, "the list kernel's CTA barrier counts NT threads");
   extern __shared__ __align__(16) unsigned char lsm[];
@@ -931,7 +933,10 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
         refine_in_list(a, r, bm, bvk, bpv, bh, R);
         continue;
       }
-      if (threadIdx.x == 0) next = (int)atomicAdd(&a.defer_cnt[4], 1u);
+      if (threadIdx.x == 0) {
+        const unsigned t = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[4]);
+        next = (int)(t < nbig ? atomicAdd(&a.defer_cnt[4], 1u) : t);
+      }
       csync();
       const int t = next;
       if (t >= (int)nbig) return false;
@@ -941,14 +946,21 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
     }
   };
   cta_work();
-  // the other lists, one warp each, mid-size before short (longest first)
+  // the other lists, one warp each, by size class, longest first
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* wa = lsm + (size_t)w * LW_BYTES;
-  for (int q = 1; q <= 2; ++q) {
+  for (int q = 1; q < LIST_CLASSES; ++q) {
     const unsigned nq = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3 + 2 * q]);
+    if (nq == 0u) continue;
+    volatile unsigned* tq = &a.defer_cnt[4 + 2 * q];
     for (;;) {
+      // a plain read first: thousands of warps finding a class empty would
+      // otherwise queue on one contended atomic
       unsigned t = 0u;
-      if (lane == 0) t = atomicAdd(&a.defer_cnt[4 + 2 * q], 1u);
+      if (lane == 0) {
+        t = *tq;
+        if (t < nq) t = atomicAdd(&a.defer_cnt[4 + 2 * q], 1u);
+      }
       t = __shfl_sync(FULL, t, 0);
       if (t >= nq) break;
       const int row = a.big_rows[(size_t)q * K_CHUNK + t];
@@ -1025,7 +1037,8 @@ __device__ __forceinline__ void fill_job(RowJob& J, const RowCtx& rc, int kind, 
 
 // A list longer than one list-kernel warp takes goes to the CTA-wide queue.
 __device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
-  const int q = n > LW_CAP ? 0 : (n > LIST_MID ? 1 : 2);
+  // classes: > LW_CAP, (512, 1024], (256, 512], (128, 256], (64, 128], <= 64
+  const int q = n > LW_CAP ? 0 : n > 512 ? 1 : n > 256 ? 2 : n > 128 ? 3 : n > 64 ? 4 : 5;
   a.big_rows[(size_t)q * K_CHUNK + atomicAdd(&a.defer_cnt[3 + 2 * q], 1u)] = row;
 }
 
@@ -1102,7 +1115,7 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
       a.defer_cnt[1] = 0u;
       a.defer_cnt[2] = 0u;                          // the row kernel's row counter
 #pragma unroll
-      for (int c = 3; c <= 8; ++c) a.defer_cnt[c] = 0u;   // the list kernel's queues
+      for (int c = 3; c < 3 + 2 * LIST_CLASSES; ++c) a.defer_cnt[c] = 0u;   // the list kernel's queues
     }
   }
 }

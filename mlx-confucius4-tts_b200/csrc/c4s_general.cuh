@@ -44,8 +44,8 @@ struct Args {
   int* defer_rows;              // rows handed to the general path
   int* big_rows;                // rows whose lists the list kernel works with a whole CTA
   unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done, [2] row counter,
-                                // list queues: [3]/[4] long lists queued/taken, [5]/[6] mid-size,
-                                // [7]/[8] short (rows in big_rows + q * K_CHUNK, q = 0, 1, 2)
+                                // list queues: [3 + 2q]/[4 + 2q] rows queued/taken in class q
+                                // (rows in big_rows + q * K_CHUNK; q = 0: long lists)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

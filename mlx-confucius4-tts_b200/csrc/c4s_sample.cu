@@ -186,7 +186,7 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     a.lkeys = ctx->d_lkeys;
     a.lsb = ctx->d_lsb;
     a.defer_rows = ctx->d_defer_rows;
-    a.big_rows = ctx->d_defer_rows + K_CHUNK;        // then the mid-size and the short lists
+    a.big_rows = ctx->d_defer_rows + K_CHUNK;        // LIST_CLASSES queues of K_CHUNK rows
     a.defer_cnt = ctx->d_defer_cnt;
     if (ctx->row_occ == 0) {
       int occ = 0;
@@ -318,7 +318,7 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_jobs, (size_t)c4s::K_CHUNK * sizeof(c4s::RowJob));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lkeys, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, 4 * (size_t)c4s::K_CHUNK * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (1 + c4s::LIST_CLASSES) * (size_t)c4s::K_CHUNK * sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, c4s::NCNT * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, c4s::NCNT * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));
