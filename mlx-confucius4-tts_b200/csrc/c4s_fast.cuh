@@ -333,8 +333,8 @@ __device__ void group_bitonic(unsigned long long* b, int np) {
 // Ascending bitonic sort of 32*SL keys held SL per lane (lane l: positions
 // SL*l .. SL*l+SL-1), in registers: within-lane stages by compare-exchange,
 // the others by shuffles. Whole warp calls.
-template <int SL>
-__device__ __forceinline__ void warp_sort_regs(unsigned (&v)[SL]) {
+template <int SL, typename T>
+__device__ __forceinline__ void warp_sort_regs(T (&v)[SL]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 2; k <= 32 * SL; k <<= 1) {
@@ -346,7 +346,7 @@ __device__ __forceinline__ void warp_sort_regs(unsigned (&v)[SL]) {
           const int p = j ^ jj;
           if (p > j) {
             const bool up = ((SL * lane + j) & k) == 0;
-            const unsigned lo = min(v[j], v[p]), hi = max(v[j], v[p]);
+            const T lo = v[j] < v[p] ? v[j] : v[p], hi = v[j] < v[p] ? v[p] : v[j];
             v[j] = up ? lo : hi;
             v[p] = up ? hi : lo;
           }
@@ -354,10 +354,10 @@ __device__ __forceinline__ void warp_sort_regs(unsigned (&v)[SL]) {
       } else {
 #pragma unroll
         for (int j = 0; j < SL; ++j) {
-          const unsigned o = __shfl_xor_sync(FULL, v[j], jj / SL);
+          const T o = __shfl_xor_sync(FULL, v[j], jj / SL);
           const int i = SL * lane + j;
           const bool keep_min = ((i & jj) == 0) == ((i & k) == 0);
-          v[j] = keep_min ? min(v[j], o) : max(v[j], o);
+          v[j] = keep_min ? (o < v[j] ? o : v[j]) : (o < v[j] ? v[j] : o);
         }
       }
     }
@@ -380,6 +380,62 @@ __device__ __forceinline__ unsigned warp_kth_sorted(const unsigned* vk, int n, i
 #pragma unroll
   for (int j = 0; j < SL; ++j) r = (pos % SL == j) ? v[j] : r;
   return __shfl_sync(FULL, r, pos / SL);
+}
+
+// Top-p crossing of at most 32*SL survivors (vk >= tk) by one warp: their
+// keys (value << 32 | position; positions are in index order, so this is the
+// canonical (value, index) order) are gathered into `buf`, sorted in
+// registers, and the first sorted position whose running mass from the low
+// end (starting at `tail`) exceeds Th is the crossing. Returns false if none;
+// else its list position and the running masses before and at it.
+template <int SL>
+__device__ __forceinline__ bool warp_sorted_crossing(const unsigned* vk, const double* pv, int n, unsigned tk, int ns,
+                                                     double tail, double Th, unsigned long long* buf, int* pos,
+                                                     double* before, double* cur) {
+  const int lane = threadIdx.x & 31;
+  int base = 0;
+  for (int e0 = 0; e0 < n; e0 += 32) {
+    const int e = e0 + lane;
+    const bool sv = e < n && vk[e] >= tk;
+    const unsigned bal = __ballot_sync(FULL, sv);
+    if (sv) buf[base + __popc(bal & ((1u << lane) - 1u))] = ((unsigned long long)vk[e] << 32) | (unsigned)e;
+    base += __popc(bal);
+  }
+  for (int i = ns + lane; i < 32 * SL; i += 32) buf[i] = KEY_MAX;
+  __syncwarp();
+  unsigned long long v[SL];
+#pragma unroll
+  for (int j = 0; j < SL; ++j) v[j] = buf[SL * lane + j];
+  __syncwarp();
+  warp_sort_regs<SL>(v);
+  double p[SL], s = 0.0;
+#pragma unroll
+  for (int j = 0; j < SL; ++j) {
+    p[j] = v[j] != KEY_MAX ? pv[(int)(v[j] & 0xffffffffull)] : 0.0;
+    s += p[j];
+  }
+  double incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(FULL, incl, o);
+    if (lane >= o) incl += y;
+  }
+  double run = tail + incl - s, bf = 0.0, cu = 0.0;
+  unsigned long long kx = 0ull;
+  bool hit = false;
+#pragma unroll
+  for (int j = 0; j < SL; ++j) {
+    const double nx = run + p[j];
+    if (!hit && nx > Th) { hit = true; bf = run; cu = nx; kx = v[j]; }
+    run = nx;
+  }
+  const unsigned cb = __ballot_sync(FULL, hit);
+  if (!cb) return false;
+  const int L = __ffs(cb) - 1;
+  *pos = (int)(__shfl_sync(FULL, kx, L) & 0xffffffffull);
+  *before = __shfl_sync(FULL, bf, L);
+  *cur = __shfl_sync(FULL, cu, L);
+  return true;
 }
 
 // Radix searches of a list job over the value keys that share `prefix` above
@@ -606,59 +662,16 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     for (int e = r0; e < n; e += GN)
       if (vk[e] >= tk && pv[e] > 0.0) mk0 = ykey(e) < mk0 ? ykey(e) : mk0;
     kst = G::qmin(mk0, R);
-  } else if (!CTA && ns <= 64) {
-    // few survivors: sort them in registers (two per lane) by (value,
-    // position) -- positions are in index order, so this is the canonical
-    // (value, index) order -- and find the crossing on a prefix scan
+  } else if (!CTA && ns <= 128) {
+    // few survivors: sort them in registers and find the crossing on a prefix scan
     const double Th = thr * St;
-    const int lane = r0;
-    int base = 0;
-    for (int e0 = 0; e0 < n; e0 += 32) {
-      const int e = e0 + lane;
-      const bool sv = e < n && vk[e] >= tk;
-      const unsigned bal = __ballot_sync(FULL, sv);
-      if (sv) hist[base + __popc(bal & ((1u << lane) - 1u))] = ((unsigned long long)vk[e] << 32) | (unsigned)e;
-      base += __popc(bal);
-    }
-    for (int i = ns + lane; i < 64; i += 32) hist[i] = KEY_MAX;
-    __syncwarp();
-    unsigned long long v0 = hist[2 * lane], v1 = hist[2 * lane + 1];
-    __syncwarp();
-#pragma unroll
-    for (int k2 = 2; k2 <= 64; k2 <<= 1) {
-#pragma unroll
-      for (int jj = k2 >> 1; jj > 0; jj >>= 1) {
-        if (jj == 1) {
-          const bool up = ((2 * lane) & k2) == 0;
-          const unsigned long long lo = v0 < v1 ? v0 : v1, hi = v0 < v1 ? v1 : v0;
-          v0 = up ? lo : hi;
-          v1 = up ? hi : lo;
-        } else {
-          const int lj = jj >> 1;
-          const unsigned long long o0 = __shfl_xor_sync(FULL, v0, lj), o1 = __shfl_xor_sync(FULL, v1, lj);
-          const int q0 = 2 * lane, q1 = 2 * lane + 1;
-          const bool m0 = ((q0 & jj) == 0) == ((q0 & k2) == 0);
-          const bool m1 = ((q1 & jj) == 0) == ((q1 & k2) == 0);
-          v0 = m0 ? (o0 < v0 ? o0 : v0) : (o0 > v0 ? o0 : v0);
-          v1 = m1 ? (o1 < v1 ? o1 : v1) : (o1 > v1 ? o1 : v1);
-        }
-      }
-    }
-    const double p0 = v0 != KEY_MAX ? pv[(int)(v0 & 0xffffffffull)] : 0.0;
-    const double p1 = v1 != KEY_MAX ? pv[(int)(v1 & 0xffffffffull)] : 0.0;
-    double tot;
-    const double pre = tail + G::exscan_d(p0 + p1, R, &tot);
-    const bool x0 = pre + p0 > Th, x1 = pre + p0 + p1 > Th;
-    const unsigned cb = __ballot_sync(FULL, x0 || x1);
-    if (cb) {
-      const int L = __ffs(cb) - 1;
-      const bool first = __shfl_sync(FULL, x0, L);
-      const double bl0 = __shfl_sync(FULL, pre, L), pl0 = __shfl_sync(FULL, p0, L), pl1 = __shfl_sync(FULL, p1, L);
-      const unsigned long long kj = first ? __shfl_sync(FULL, v0, L) : __shfl_sync(FULL, v1, L);
-      const double before = first ? bl0 : bl0 + pl0;
-      const double cur = first ? bl0 + pl0 : bl0 + pl0 + pl1;
+    int pos = 0;
+    double before = 0.0, cur = 0.0;
+    const bool hit = ns <= 64 ? warp_sorted_crossing<2>(vk, pv, n, tk, ns, tail, Th, hist, &pos, &before, &cur)
+                              : warp_sorted_crossing<4>(vk, pv, n, tk, ns, tail, Th, hist, &pos, &before, &cur);
+    if (hit) {
       const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
-      kst = ykey((int)(kj & 0xffffffffull));
+      kst = ykey(pos);
       exact_tp = !(before <= Th - bd && cur > Th + bd);
     } else {
       kst = KEY_MAX;                                  // no crossing: only the kept maximum
