@@ -171,134 +171,55 @@ __device__ __noinline__ void write_row_smem(const Args& a, const float* rb, cons
   }
 }
 
-// One staged, penalised row. Returns ROW_DONE or ROW_GENERAL.
-__device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& M, const float* rb, const RGeo& g,
-                                         RShared& S) {
-  const int V = a.V;
+// A top-k row, out of line like rows without top-k.
+__device__ __noinline__ int topk_body(const Args& a, int row, const RowCtx rc, const float* rb, const RGeo g,
+                                      RShared& S, unsigned long long* keys, int k, bool two, float tm, float t2) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const c4s_row_params P = M.P;
-  const int k = P.top_k;
-  const bool do_k = k > 0 && k < V;
-  const bool two = !P.greedy && do_k && k > RWARP * 32 / 2;   // the two largest per lane seed the list
-
-  // ---- row max, per-lane maxima (and second maxima), valid elements per lane ----
-  float tm = -INFINITY, t2 = -INFINITY;
+  // ---- top-k rows: candidates >= the maxima threshold form the list ----
+  // a warp whose kw-th largest lane maximum (of the two largest per lane
+  // when `two`) is finite has >= kw elements >= it, so >= k elements are >=
+  // tau, the smallest over the warps (-inf: not enough elements; general path)
+  if (k > RWARP * (two ? 64 : 32)) return ROW_GENERAL;
+  const int kw = (k + RWARP - 1) / RWARP;
+  const unsigned wthr = two ? warp_kth_largest64(fkey(tm), fkey(t2), kw) : warp_kth_largest32(fkey(tm), kw);
+  if (lane == 0) S.redu[warp] = wthr;
+  rsync();
+  unsigned tkey = S.redu[0];
+#pragma unroll
+  for (int w = 1; w < RWARP; ++w) tkey = S.redu[w] < tkey ? S.redu[w] : tkey;
+  const float tau = fkey_inv(tkey);
+  // fl(x/T) merges x only with values at most |x| 2^-23 below it: lowering tau
+  // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
+  const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;
+  if (!(tau_lo > -INFINITY)) return ROW_GENERAL;
+  int cnt = 0;
 #pragma unroll 4
   for (int q = 0; q < g.nq; ++q) {
     const float4 v = rload(rb, g, rslot(g, q));
-    if (two) {
-      t2 = fmaxf(t2, fminf(tm, v.x)); tm = fmaxf(tm, v.x);
-      t2 = fmaxf(t2, fminf(tm, v.y)); tm = fmaxf(tm, v.y);
-      t2 = fmaxf(t2, fminf(tm, v.z)); tm = fmaxf(tm, v.z);
-      t2 = fmaxf(t2, fminf(tm, v.w)); tm = fmaxf(tm, v.w);
-    } else {
-      tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-    }
+    cnt += (v.x >= tau_lo) + (v.y >= tau_lo) + (v.z >= tau_lo) + (v.w >= tau_lo);
   }
-  {
-    const unsigned km = __reduce_max_sync(FULL, fkey(tm));
-    if (lane == 0) S.redu[warp] = km;
+  int ng;
+  const int base = rblock_base(cnt, S, &ng);
+  if (ng > LCAP) return ROW_GENERAL;
+  write_list(keys, base, rb, g, [&](float x) { return x >= tau_lo; });
+  if (tid == 0) {
+    RowJob& J = a.jobs[row];
+    fill_job(J, rc, JOB_TOPK, ng, k);
+    queue_long_list(a, row, ng);
+    J.tail = 0.0;
+    J.tail_err = 0.0;
+    J.ykex = 0u;
   }
-  rsync();
-  unsigned kall = S.redu[0];
-#pragma unroll
-  for (int w = 1; w < RWARP; ++w) kall = kall > S.redu[w] ? kall : S.redu[w];
-  const float m_x = fkey_inv(kall);
-  rsync();
+  if (a.out_logits) write_row_smem(a, rb, g, rc, true);
+  return ROW_DONE;
+}
 
-  RowCtx rc;
-  rc.row = row; rc.V = V; rc.i0 = 0;
-  rc.T = P.temperature;
-  rc.do_t = !(rc.T == 1.0f || rc.T <= 0.0f);
-
-  // ---- greedy: first index of the max (sampling.cpp:73-76) ----
-  if (P.greedy) {
-    unsigned cand = 0xffffffffu;
-    if (m_x > -INFINITY && tm == m_x) {
-      for (int q = 0; q < g.nq; ++q) {
-        const int f = rslot(g, q);
-        const float4 v = rload(rb, g, f);
-        const int i0 = 4 * f - g.shift;
-        if (v.w == m_x) cand = min(cand, (unsigned)(i0 + 3));
-        if (v.z == m_x) cand = min(cand, (unsigned)(i0 + 2));
-        if (v.y == m_x) cand = min(cand, (unsigned)(i0 + 1));
-        if (v.x == m_x) cand = min(cand, (unsigned)i0);
-        if (cand != 0xffffffffu) break;              // later slots hold larger indices
-      }
-    }
-    cand = __reduce_min_sync(FULL, cand);
-    if (lane == 0) S.redu[warp] = cand;
-    rsync();
-    if (tid == 0) {
-      unsigned b = S.redu[0];
-      for (int w = 1; w < RWARP; ++w) b = S.redu[w] < b ? S.redu[w] : b;
-      a.out_ids[row] = b == 0xffffffffu ? 0 : (int)b;
-      a.jobs[row].kind = JOB_NONE;
-    }
-    if (a.out_logits) write_row_smem(a, rb, g, rc, false);
-    rsync();
-    return ROW_DONE;
-  }
-
-  // ---- sampled rows: preconditions ----
-  if (!(m_x > -INFINITY && m_x < INFINITY)) return ROW_GENERAL;
-  rc.m_x = m_x;
-  rc.m_y = rc.do_t ? __fdiv_rn(m_x, rc.T) : m_x;
-  rc.rT = rc.do_t ? __frcp_rn(rc.T) : 1.0f;
-  if (!(fabsf(rc.m_y) < 262144.0f)) return ROW_GENERAL;
-  if (P.min_tokens_to_keep != 1) return ROW_GENERAL;
-  if (a.debug & C4S_DEBUG_FORCE_EXACT) return ROW_GENERAL;
-  rc.thr = __dsub_rn(1.0, (double)P.top_p);
-  {
-    unsigned long long xs = M.rng;
-    xs ^= xs << 13; xs ^= xs >> 7; xs ^= xs << 17;
-    rc.xs = xs;
-    rc.u53 = xs >> 11;
-    rc.u = (double)rc.u53 * 1.1102230246251565e-16;   // (x>>11) / 2^53, exact
-  }
-  unsigned long long* keys = a.lkeys + (size_t)row * LCAP;
-
-  if (do_k) {
-    // ---- top-k rows: candidates >= the maxima threshold form the list ----
-    // a warp whose kw-th largest lane maximum (of the two largest per lane
-    // when `two`) is finite has >= kw elements >= it, so >= k elements are >=
-    // tau, the smallest over the warps (-inf: not enough elements; general path)
-    if (k > RWARP * (two ? 64 : 32)) return ROW_GENERAL;
-    const int kw = (k + RWARP - 1) / RWARP;
-    const unsigned wthr = two ? warp_kth_largest64(fkey(tm), fkey(t2), kw) : warp_kth_largest32(fkey(tm), kw);
-    if (lane == 0) S.redu[warp] = wthr;
-    rsync();
-    unsigned tkey = S.redu[0];
-#pragma unroll
-    for (int w = 1; w < RWARP; ++w) tkey = S.redu[w] < tkey ? S.redu[w] : tkey;
-    const float tau = fkey_inv(tkey);
-    // fl(x/T) merges x only with values at most |x| 2^-23 below it: lowering tau
-    // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
-    const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;
-    if (!(tau_lo > -INFINITY)) return ROW_GENERAL;
-    int cnt = 0;
-#pragma unroll 4
-    for (int q = 0; q < g.nq; ++q) {
-      const float4 v = rload(rb, g, rslot(g, q));
-      cnt += (v.x >= tau_lo) + (v.y >= tau_lo) + (v.z >= tau_lo) + (v.w >= tau_lo);
-    }
-    int ng;
-    const int base = rblock_base(cnt, S, &ng);
-    if (ng > LCAP) return ROW_GENERAL;
-    write_list(keys, base, rb, g, [&](float x) { return x >= tau_lo; });
-    if (tid == 0) {
-      RowJob& J = a.jobs[row];
-      fill_job(J, rc, JOB_TOPK, ng, k);
-      queue_long_list(a, row, ng);
-      J.tail = 0.0;
-      J.tail_err = 0.0;
-      J.ykex = 0u;
-    }
-    if (a.out_logits) write_row_smem(a, rb, g, rc, true);
-    return ROW_DONE;
-  }
-
-  // ---- rows without top-k (top-p over the whole row, sampling.cpp:42-71) ----
+// A row without top-k (top-p over the whole row, sampling.cpp:42-71), out of
+// line: the per-row paths stay small enough to share the instruction cache.
+__device__ __noinline__ int k0_body(const Args& a, int row, const RowCtx rc, const float* rb, const RGeo g,
+                                    RShared& S, unsigned long long* keys) {
+  const int V = a.V;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // top_p >= 1 and the forced binned paths: general path
   if (!(rc.thr > 0.0) || (a.debug & C4S_DEBUG_FORCE_BINS)) return ROW_GENERAL;
   // octave histogram of the estimates: per-warp fixed-point bins (exact adds)
@@ -413,6 +334,97 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
   }
   if (a.out_logits) write_row_smem(a, rb, g, rc, true);
   return ROW_DONE;
+}
+
+// One staged, penalised row. Returns ROW_DONE or ROW_GENERAL.
+__device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& M, const float* rb, const RGeo& g,
+                                         RShared& S) {
+  const int V = a.V;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const c4s_row_params P = M.P;
+  const int k = P.top_k;
+  const bool do_k = k > 0 && k < V;
+  const bool two = !P.greedy && do_k && k > RWARP * 32 / 2;   // the two largest per lane seed the list
+
+  // ---- row max, per-lane maxima (and second maxima), valid elements per lane ----
+  float tm = -INFINITY, t2 = -INFINITY;
+#pragma unroll 4
+  for (int q = 0; q < g.nq; ++q) {
+    const float4 v = rload(rb, g, rslot(g, q));
+    if (two) {
+      t2 = fmaxf(t2, fminf(tm, v.x)); tm = fmaxf(tm, v.x);
+      t2 = fmaxf(t2, fminf(tm, v.y)); tm = fmaxf(tm, v.y);
+      t2 = fmaxf(t2, fminf(tm, v.z)); tm = fmaxf(tm, v.z);
+      t2 = fmaxf(t2, fminf(tm, v.w)); tm = fmaxf(tm, v.w);
+    } else {
+      tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+  }
+  {
+    const unsigned km = __reduce_max_sync(FULL, fkey(tm));
+    if (lane == 0) S.redu[warp] = km;
+  }
+  rsync();
+  unsigned kall = S.redu[0];
+#pragma unroll
+  for (int w = 1; w < RWARP; ++w) kall = kall > S.redu[w] ? kall : S.redu[w];
+  const float m_x = fkey_inv(kall);
+  rsync();
+
+  RowCtx rc;
+  rc.row = row; rc.V = V; rc.i0 = 0;
+  rc.T = P.temperature;
+  rc.do_t = !(rc.T == 1.0f || rc.T <= 0.0f);
+
+  // ---- greedy: first index of the max (sampling.cpp:73-76) ----
+  if (P.greedy) {
+    unsigned cand = 0xffffffffu;
+    if (m_x > -INFINITY && tm == m_x) {
+      for (int q = 0; q < g.nq; ++q) {
+        const int f = rslot(g, q);
+        const float4 v = rload(rb, g, f);
+        const int i0 = 4 * f - g.shift;
+        if (v.w == m_x) cand = min(cand, (unsigned)(i0 + 3));
+        if (v.z == m_x) cand = min(cand, (unsigned)(i0 + 2));
+        if (v.y == m_x) cand = min(cand, (unsigned)(i0 + 1));
+        if (v.x == m_x) cand = min(cand, (unsigned)i0);
+        if (cand != 0xffffffffu) break;              // later slots hold larger indices
+      }
+    }
+    cand = __reduce_min_sync(FULL, cand);
+    if (lane == 0) S.redu[warp] = cand;
+    rsync();
+    if (tid == 0) {
+      unsigned b = S.redu[0];
+      for (int w = 1; w < RWARP; ++w) b = S.redu[w] < b ? S.redu[w] : b;
+      a.out_ids[row] = b == 0xffffffffu ? 0 : (int)b;
+      a.jobs[row].kind = JOB_NONE;
+    }
+    if (a.out_logits) write_row_smem(a, rb, g, rc, false);
+    rsync();
+    return ROW_DONE;
+  }
+
+  // ---- sampled rows: preconditions ----
+  if (!(m_x > -INFINITY && m_x < INFINITY)) return ROW_GENERAL;
+  rc.m_x = m_x;
+  rc.m_y = rc.do_t ? __fdiv_rn(m_x, rc.T) : m_x;
+  rc.rT = rc.do_t ? __frcp_rn(rc.T) : 1.0f;
+  if (!(fabsf(rc.m_y) < 262144.0f)) return ROW_GENERAL;
+  if (P.min_tokens_to_keep != 1) return ROW_GENERAL;
+  if (a.debug & C4S_DEBUG_FORCE_EXACT) return ROW_GENERAL;
+  rc.thr = __dsub_rn(1.0, (double)P.top_p);
+  {
+    unsigned long long xs = M.rng;
+    xs ^= xs << 13; xs ^= xs >> 7; xs ^= xs << 17;
+    rc.xs = xs;
+    rc.u53 = xs >> 11;
+    rc.u = (double)rc.u53 * 1.1102230246251565e-16;   // (x>>11) / 2^53, exact
+  }
+  unsigned long long* keys = a.lkeys + (size_t)row * LCAP;
+
+  if (do_k) return topk_body(a, row, rc, rb, g, S, keys, k, two, tm, t2);
+  return k0_body(a, row, rc, rb, g, S, keys);
 }
 
 // Persistent row kernel: rows handed out dynamically (the first G statically).
