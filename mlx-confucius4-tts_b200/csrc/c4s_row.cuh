@@ -192,16 +192,43 @@ __device__ __noinline__ int topk_body(const Args& a, int row, const RowCtx rc, c
   // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
   const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;
   if (!(tau_lo > -INFINITY)) return ROW_GENERAL;
-  int cnt = 0;
-#pragma unroll 4
+  // one pass: each warp stages its candidates' buffer positions, in index
+  // order, in its share of the (here unused) octave-bin area; once the warps'
+  // counts give their list offsets it copies them out (a warp with more
+  // candidates than fit writes its list with a second pass instead)
+  unsigned short* stage = reinterpret_cast<unsigned short*>(&S.hw[warp][0][0]);
+  constexpr int STAGE_CAP = HREP * 32 * 2;
+  int run = 0;
+#pragma unroll 2
   for (int q = 0; q < g.nq; ++q) {
-    const float4 v = rload(rb, g, rslot(g, q));
-    cnt += (v.x >= tau_lo) + (v.y >= tau_lo) + (v.z >= tau_lo) + (v.w >= tau_lo);
+    const int f = rslot(g, q);
+    const float4 v = rload(rb, g, f);
+    const int m = (v.x >= tau_lo ? 1 : 0) | (v.y >= tau_lo ? 2 : 0) | (v.z >= tau_lo ? 4 : 0) | (v.w >= tau_lo ? 8 : 0);
+    if (__any_sync(FULL, m)) {
+      int tot;
+      int pos = run + warp_prefix4(__popc(m), &tot);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (m & (1 << c)) {
+          if (pos < STAGE_CAP) stage[pos] = (unsigned short)(4 * f + c);
+          ++pos;
+        }
+      }
+      run += tot;
+    }
   }
   int ng;
-  const int base = rblock_base(cnt, S, &ng);
+  const int base = rblock_base(lane == 0 ? run : 0, S, &ng);
   if (ng > LCAP) return ROW_GENERAL;
-  write_list(keys, base, rb, g, [&](float x) { return x >= tau_lo; });
+  if (run <= STAGE_CAP) {
+    __syncwarp();
+    for (int i = lane; i < run; i += 32) {
+      const int bp = stage[i];
+      keys[base + i] = ckey(rb[bp], bp - g.shift);
+    }
+  } else {
+    write_list(keys, base, rb, g, [&](float x) { return x >= tau_lo; });
+  }
   if (tid == 0) {
     RowJob& J = a.jobs[row];
     fill_job(J, rc, JOB_TOPK, ng, k);
