@@ -326,16 +326,36 @@ __device__ __noinline__ int k0_body(const Args& a, int row, const RowCtx rc, con
   // the list: elements in octaves <= bl, i.e. >= x*, in index order
   const float xs = list_threshold(rc, bl);
   auto in_list = [&](float x) { return x >= xs; };
-  int cnt = 0;
-  float xmx = -INFINITY;                            // the largest element below the list
+  // one pass, as for top-k rows: positions staged per warp in the octave-bin
+  // area (every warp has read the bins once the barrier is passed), plus the
+  // largest element below the list
+  rsync();
+  unsigned short* stage = reinterpret_cast<unsigned short*>(&S.hw[warp][0][0]);
+  constexpr int STAGE_CAP = HREP * 32 * 2;
+  int run = 0;
+  float xmx = -INFINITY;
 #pragma unroll 2
   for (int q = 0; q < g.nq; ++q) {
-    const float4 v = rload(rb, g, rslot(g, q));
+    const int f = rslot(g, q);
+    const float4 v = rload(rb, g, f);
+    int m = 0;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const float x = f4c(v, c);
-      if (in_list(x)) ++cnt;
+      if (in_list(x)) m |= 1 << c;
       else xmx = fmaxf(xmx, x);
+    }
+    if (__any_sync(FULL, m)) {
+      int tot;
+      int pos = run + warp_prefix4(__popc(m), &tot);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (m & (1 << c)) {
+          if (pos < STAGE_CAP) stage[pos] = (unsigned short)(4 * f + c);
+          ++pos;
+        }
+      }
+      run += tot;
     }
   }
   {
@@ -343,13 +363,21 @@ __device__ __noinline__ int k0_body(const Args& a, int row, const RowCtx rc, con
     if (lane == 0) S.redu[warp] = km;
   }
   int ng;
-  const int base = rblock_base(cnt, S, &ng);        // its barriers also publish S.redu
+  const int base = rblock_base(lane == 0 ? run : 0, S, &ng);   // its barriers also publish S.redu
   if (ng > LCAP) return ROW_GENERAL;
   unsigned kx = S.redu[0];
 #pragma unroll
   for (int w = 1; w < RWARP; ++w) kx = kx > S.redu[w] ? kx : S.redu[w];
   const float xm = fkey_inv(kx);
-  write_list(keys, base, rb, g, in_list);
+  if (run <= STAGE_CAP) {
+    __syncwarp();
+    for (int i = lane; i < run; i += 32) {
+      const int bp = stage[i];
+      keys[base + i] = ckey(rb[bp], bp - g.shift);
+    }
+  } else {
+    write_list(keys, base, rb, g, in_list);
+  }
   const double tl = __shfl_sync(FULL, blw, bl), tl_err = est_err(tl, __shfl_sync(FULL, wblw, bl), rc.m_y, 33, V);
   if (tid == 0) {
     RowJob& J = a.jobs[row];
