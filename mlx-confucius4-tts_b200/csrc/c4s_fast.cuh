@@ -34,6 +34,7 @@ constexpr int LIST_DEEP = 1024;           // rows without top-k: lists go deeper
 constexpr int K_CHUNK = 4096;             // rows per launch sequence (list storage)
 constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
+constexpr int LW_CAP = 1024;              // list kernel: longest list one warp takes
 constexpr int RQ_CAP = 16;                // list kernel: rows of one CTA waiting for an exact tail
 constexpr int LIST_CLASSES = 6;           // list queues: long (CTA), then warp lists by size, longest first
 constexpr int NCNT = 16;                  // slots of the per-launch counters (defer_cnt)
@@ -685,7 +686,28 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     const unsigned smin32 = (unsigned)smin, vmax32 = (unsigned)vmax;
     const int b0 = (smin32 == vmax32) ? -1 : 31 - __clz(smin32 ^ vmax32);
     unsigned v = b0 < 0 ? smin32 : (b0 >= 31 ? 0u : (vmax32 & ~((2u << b0) - 1u)));
-    v = bisect_mass<CTA>(vk, pv, n, v, b0, tail, Th, R);
+    if (!CTA && ns < n && n <= LW_CAP / 2) {
+      // one warp: bisect over the survivors only, gathered into the unused
+      // upper half of the warp's staging area (top-k zeroes the others' mass)
+      unsigned* cvk = vk + LW_CAP / 2;
+      double* cpv = pv + LW_CAP / 2;
+      int cb = 0;
+      for (int e0 = 0; e0 < n; e0 += 32) {
+        const int e = e0 + r0;
+        const bool sv = e < n && vk[e] >= tk;
+        const unsigned bal = __ballot_sync(FULL, sv);
+        if (sv) {
+          const int o = cb + __popc(bal & ((1u << r0) - 1u));
+          cvk[o] = vk[e];
+          cpv[o] = pv[e];
+        }
+        cb += __popc(bal);
+      }
+      __syncwarp();
+      v = bisect_mass<CTA>(cvk, cpv, ns, v, b0, tail, Th, R);
+    } else {
+      v = bisect_mass<CTA>(vk, pv, n, v, b0, tail, Th, R);
+    }
     double Gs = 0.0, Mg = 0.0;
     int cg = 0;
     for (int e = r0; e < n; e += GN) {
@@ -849,7 +871,6 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
 // List kernel dynamic shared memory: per warp a list of up to LW_CAP entries
 // (staged value keys, probabilities) and a radix histogram; once the warps are
 // done, the same area holds one long list (up to LCAP) worked by the whole CTA.
-constexpr int LW_CAP = 1024;                  // longest list one warp takes
 constexpr size_t LW_VK = 0, LW_PV = (size_t)LW_CAP * 4, LW_HIST = LW_PV + (size_t)LW_CAP * 8;
 constexpr size_t LW_BYTES = LW_HIST + 256 * 8;            // per warp
 constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)LCAP * 8;
