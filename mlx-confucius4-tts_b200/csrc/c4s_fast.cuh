@@ -950,7 +950,11 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   __shared__ int next;
   __shared__ int rq[1 + RQ_CAP];
   __shared__ unsigned bm[(F_MAXV + 31) / 32 + 1];
-  if (threadIdx.x == 0) rq[0] = 0;
+  __shared__ Args sa;                               // for refine_in_list (no local copy)
+  if (threadIdx.x == 0) {
+    rq[0] = 0;
+    sa = a;
+  }
   const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
   unsigned* bvk = reinterpret_cast<unsigned*>(lsm + LB_VK);
   double* bpv = reinterpret_cast<double*>(lsm + LB_PV);
@@ -964,7 +968,7 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
         const int r = rq[nq];
         csync();
         if (threadIdx.x == 0) rq[0] = nq - 1;
-        refine_in_list(a, r, bm, bvk, bpv, bh, R);
+        refine_in_list(sa, r, bm, bvk, bpv, bh, R);
         continue;
       }
       if (threadIdx.x == 0) {
@@ -1126,6 +1130,7 @@ __device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf
 __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ Shared S;
+  __shared__ Args sa;                               // for general_row (no local copy)
   const Layout L = layout_for(a.V);
   float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
@@ -1133,13 +1138,16 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   unsigned long long* mass = reinterpret_cast<unsigned long long*>(dsm + L.mass);
   unsigned long long* lkey = reinterpret_cast<unsigned long long*>(dsm + L.key);
   double* pv = reinterpret_cast<double*>(dsm + L.pv);
-  if (threadIdx.x == 0) mbar_init(&S.bar, 1);
+  if (threadIdx.x == 0) {
+    mbar_init(&S.bar, 1);
+    sa = a;
+  }
   csync();
   unsigned phase = 0;
   const unsigned n = *reinterpret_cast<volatile unsigned*>(a.defer_cnt);
   for (unsigned t = blockIdx.x; t < n; t += gridDim.x) {
     const int row = a.defer_rows[t];
-    if (!general_row(a, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) break;
+    if (!general_row(sa, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) break;
   }
   csync();
   if (threadIdx.x == 0) {

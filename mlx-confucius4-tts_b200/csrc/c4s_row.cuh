@@ -156,7 +156,7 @@ __device__ __forceinline__ void defer_to_general(const Args& a, int row) {
 
 // The processed row (what the reference's vector holds before top-k/top-p
 // masking, which the mask kernel applies afterwards).
-__device__ __noinline__ void write_row_smem(const Args& a, const float* rb, const RGeo& g, const RowCtx& rc,
+__device__ __noinline__ void write_row_smem(const Args& a, const float* rb, const RGeo g, const RowCtx rc,
                                             bool temper) {
   float* o = a.out_logits + (long long)rc.row * a.out_ld;
   for (int q = 0; q < g.nq; ++q) {
@@ -392,8 +392,8 @@ __device__ __noinline__ int k0_body(const Args& a, int row, const RowCtx rc, con
 }
 
 // One staged, penalised row. Returns ROW_DONE or ROW_GENERAL.
-__device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& M, const float* rb, const RGeo& g,
-                                         RShared& S) {
+__device__ __forceinline__ int row_body(const Args& a, const Args& ao, int row, const MetaSlot& M, const float* rb,
+                                         const RGeo& g, RShared& S) {
   const int V = a.V;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const c4s_row_params P = M.P;
@@ -455,7 +455,7 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
       a.out_ids[row] = b == 0xffffffffu ? 0 : (int)b;
       a.jobs[row].kind = JOB_NONE;
     }
-    if (a.out_logits) write_row_smem(a, rb, g, rc, false);
+    if (a.out_logits) write_row_smem(ao, rb, g, rc, false);
     rsync();
     return ROW_DONE;
   }
@@ -478,20 +478,26 @@ __device__ __forceinline__ int row_body(const Args& a, int row, const MetaSlot& 
   }
   unsigned long long* keys = a.lkeys + (size_t)row * LCAP;
 
-  if (do_k) return topk_body(a, row, rc, rb, g, S, keys, k, two, tm, t2);
-  return k0_body(a, row, rc, rb, g, S, keys);
+  if (do_k) return topk_body(ao, row, rc, rb, g, S, keys, k, two, tm, t2);
+  return k0_body(ao, row, rc, rb, g, S, keys);
 }
 
 // Persistent row kernel: rows handed out dynamically (the first G statically).
 __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
   extern __shared__ __align__(128) float rb[];     // the staged row
   __shared__ RShared S;
+  // the out-of-line paths read the arguments from here: a reference to the
+  // kernel parameter would give every thread a copy in local memory
+  __shared__ Args sa;
   const int V = a.V;
   const int tid = threadIdx.x;
   const int G = gridDim.x;
   const int nbm = (V + 31) / 32;
 
-  if (tid == 0) mbar_init(&S.bar, 1);
+  if (tid == 0) {
+    mbar_init(&S.bar, 1);
+    sa = a;
+  }
   // every buffer position outside a row reads as -inf (see RGeo)
   for (int i = tid; i < 4 * R_SLOTS; i += RT) rb[i] = -INFINITY;
   int act_pend = 1;
@@ -602,7 +608,7 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
         rsync();
       }
       const RGeo g = rgeo(V, sg.shift);
-      if (row_body(a, row, cur, rb, g, S) == ROW_GENERAL) defer_to_general(a, row);
+      if (row_body(a, sa, row, cur, rb, g, S) == ROW_GENERAL) defer_to_general(a, row);
     } else if (tid == 0) {
       a.out_ids[row] = -1;
       a.jobs[row].kind = JOB_NONE;

@@ -49,6 +49,7 @@ namespace c4s {
 __global__ void __launch_bounds__(NT, 4) rows_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ Shared S;
+  __shared__ Args sa;                               // for general_row (no local copy)
   const Layout L = layout_for(a.V);
   float* rowbuf = reinterpret_cast<float*>(dsm + L.row);
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm + L.bitmap);
@@ -56,7 +57,10 @@ __global__ void __launch_bounds__(NT, 4) rows_kernel(Args a) {
   unsigned long long* mass = reinterpret_cast<unsigned long long*>(dsm + L.mass);
   unsigned long long* lkey = reinterpret_cast<unsigned long long*>(dsm + L.key);
   double* pv = reinterpret_cast<double*>(dsm + L.pv);
-  if (threadIdx.x == 0) mbar_init(&S.bar, 1);
+  if (threadIdx.x == 0) {
+    mbar_init(&S.bar, 1);
+    sa = a;
+  }
   csync();
   unsigned phase = 0;
   for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
@@ -64,7 +68,7 @@ __global__ void __launch_bounds__(NT, 4) rows_kernel(Args a) {
       if (threadIdx.x == 0) a.out_ids[row] = -1;
       continue;
     }
-    if (!general_row(a, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) return;
+    if (!general_row(sa, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) return;
   }
 }
 
