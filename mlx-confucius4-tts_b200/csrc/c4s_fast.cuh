@@ -869,10 +869,14 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
 }
 
 // List kernel dynamic shared memory: per warp a list of up to LW_CAP entries
-// (staged value keys, probabilities) and a radix histogram; once the warps are
-// done, the same area holds one long list (up to LCAP) worked by the whole CTA.
+// (staged value keys, probabilities) and 1 KB of scratch (a radix histogram of
+// 256 counts, or the 128 keys of the sorted top-p crossing); once the warps
+// are done, the same area holds one long list (up to LCAP) worked by the whole
+// CTA. Sized so that two CTAs (16 warps) fit on an SM.
 constexpr size_t LW_VK = 0, LW_PV = (size_t)LW_CAP * 4, LW_HIST = LW_PV + (size_t)LW_CAP * 8;
-constexpr size_t LW_BYTES = LW_HIST + 256 * 8;            // per warp
+constexpr size_t LW_BYTES = LW_HIST + 128 * 8;            // per warp
+static_assert(LW_BYTES - LW_HIST >= 256 * sizeof(unsigned), "radix histogram");
+static_assert(LW_BYTES - LW_HIST >= 32 * 4 * sizeof(unsigned long long), "sorted-crossing keys");
 constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)LCAP * 8;
 constexpr size_t LIST_SMEM_W = (size_t)LIST_WARPS * LW_BYTES, LIST_SMEM_B = LB_HIST + 256 * 8;
 constexpr size_t LIST_SMEM = LIST_SMEM_W > LIST_SMEM_B ? LIST_SMEM_W : LIST_SMEM_B;   // warps' areas / one long list
@@ -1099,6 +1103,16 @@ struct Staged {
   int hpos;                  // buffer position of this thread's plain-loaded element (-1: none)
   float hval;
 };
+// The 16-byte-aligned body of a row that stage_row copies, prefetched into L2
+// one row ahead so that its DRAM reads overlap the current row's work.
+__device__ __forceinline__ void prefetch_row(const float* g, int V) {
+  const unsigned long long ga = (unsigned long long)g;
+  int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);
+  if (head > V) head = V;
+  const int body = ((V - head) >> 2) << 2;
+  if (body > 0) bulk_prefetch_l2(g + head, (unsigned)body * 4u);
+}
+
 __device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf, unsigned long long* bar) {
   const unsigned long long ga = (unsigned long long)g;
   int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);

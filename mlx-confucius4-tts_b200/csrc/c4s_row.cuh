@@ -529,6 +529,7 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
     const int next = S.nrow[j & 1];
     issue_meta(next, nxt);
     cp_async_commit();
+    if (tid == 32 && next < a.B) prefetch_row(a.logits + (long long)next * a.ld, V);
     if (tid == 6 && next < a.B) nxt.active = act_pend;
     if (cur.active) {
       const c4s_row_params P = cur.P;

@@ -105,6 +105,7 @@ struct c4s_ctx {
   unsigned long long* d_counters = nullptr;
   c4s_row_params* d_default_params = nullptr;  // one zeroed struct (argmax reads no field)
   int row_occ = 0;                             // resident row-kernel CTAs per SM
+  int list_occ = 0;                            // resident list-kernel CTAs per SM
   c4s::RowJob* d_jobs = nullptr;               // fast path: per-row jobs of one chunk
   unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
   unsigned long long* d_lsb = nullptr;
@@ -197,6 +198,10 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, RT, R_SMEM) != cudaSuccess || occ < 1)
         return fail(ctx, C4S_ERR_CUDA, "row kernel occupancy");
       ctx->row_occ = occ;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, list_kernel, 32 * LIST_WARPS, LIST_SMEM) != cudaSuccess ||
+          occ < 1)
+        return fail(ctx, C4S_ERR_CUDA, "list kernel occupancy");
+      ctx->list_occ = occ;
     }
     const cudaStream_t st = (cudaStream_t)stream;
     const size_t gsm = layout_for(a.V).total;
@@ -215,7 +220,8 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       if (ev) cudaEventRecord(ev[0], st);
       row_kernel<<<g1, RT, R_SMEM, st>>>(ac);
       if (ev) cudaEventRecord(ev[1], st);
-      const int g2 = (int)std::min<long long>((ac.B + LIST_WARPS - 1) / LIST_WARPS, 2LL * ctx->num_sms);
+      const int g2 = (int)std::min<long long>((ac.B + LIST_WARPS - 1) / LIST_WARPS,
+                                                   (long long)ctx->list_occ * ctx->num_sms);
       list_kernel<<<g2, 32 * LIST_WARPS, LIST_SMEM, st>>>(ac);
       if (ev) cudaEventRecord(ev[2], st);
       const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
