@@ -54,7 +54,9 @@ struct __align__(16) RowJob {
   double tail, tail_err;     // JOB_K0: estimated mass below the list and its error bound
   unsigned long long u53, xs;
   unsigned long long kstar;  // result: keys below K* are removed by top-p
-  unsigned long long pad2;
+  unsigned vcross;           // JOB_K0 handed to a refinement: value key of the crossing group
+                             // the first pass found (0: none); the refinement's search starts there
+  unsigned pad2;
 };
 
 // Per-row metadata, fetched asynchronously one row ahead.
@@ -552,6 +554,54 @@ __device__ __forceinline__ unsigned bisect_mass(const unsigned* __restrict__ vk,
   }
 }
 
+// From a value key c of the list, steps to the neighbouring value group
+// (next survivor key below or above) until it reaches the group whose mass
+// range [base + G(v), base + G(v) + M(v)) holds Th, G(v) being the mass of
+// the survivors below v and M(v) that of the group v: the group bisect_mass
+// ends on. A refinement whose exact tail moved the crossing by little gets
+// there in a pass or two; false after 8 steps or past either end of the list
+// (the caller then bisects). Rounding differences against bisect_mass's sums
+// are harmless: the caller's band check accepts only a crossing that every
+// summation order agrees on.
+template <bool CTA>
+__device__ __forceinline__ bool step_to_crossing(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
+                                                 unsigned tk, double base, double Th, unsigned c, unsigned* out,
+                                                 LRed& R) {
+  using G = LG<CTA>;
+  for (int it = 0; it < 8; ++it) {
+    double gs = 0.0, mg = 0.0, z = 0.0;
+    unsigned long long below = 0ull, above = ~0ull;   // below: key + 1 (0: none)
+    for (int e = G::rank(); e < n; e += G::N) {
+      const unsigned x = vk[e];
+      if (x < tk) continue;                           // removed by top-k: no mass
+      if (x < c) {
+        gs += pv[e];
+        below = (unsigned long long)x + 1ull > below ? (unsigned long long)x + 1ull : below;
+      } else if (x == c) {
+        mg += pv[e];
+      } else {
+        above = (unsigned long long)x < above ? (unsigned long long)x : above;
+      }
+    }
+    G::sum3(gs, mg, z, R);
+    below = G::qmax(below, R);
+    above = G::qmin(above, R);
+    gs += base;
+    if (mg > 0.0 && gs <= Th && gs + mg > Th) {
+      *out = c;
+      return true;
+    }
+    if (gs > Th) {
+      if (below == 0ull) return false;
+      c = (unsigned)(below - 1ull);
+    } else {
+      if (above == ~0ull) return false;
+      c = (unsigned)above;
+    }
+  }
+  return false;
+}
+
 // One list job. keys[0..n) (global): ckey(x, i) of the candidates' penalised,
 // untempered values in index order (list position = index order). The job
 // stages the keys of their tempered values y = fl(x/T) into vk[] and their
@@ -614,7 +664,6 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
   G::sync();
   // no-top-k list: everything below it must be strictly smaller in value
   if (k0 && J.ykex >= vmin) { hand_back(RES_DEFER); return false; }
-  if (k0 && !refine && (a.debug & C4S_DEBUG_FORCE_REFINE)) { hand_back(RES_REFINE); return false; }
 
   // ---- top-k threshold: the k-th largest value key (sampling.cpp:30-40) ----
   unsigned tk = (unsigned)vmin;
@@ -656,6 +705,8 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
   const double St = tail + ps;
   unsigned long long kst = 0ull;
   bool exact_tp = false;
+  // the debug flag sends every first-pass no-top-k list to a refinement once its crossing is found
+  const bool force_ref = k0 && !refine && (a.debug & C4S_DEBUG_FORCE_REFINE) != 0;
   if (thr < 0.0) {
     kst = 0ull;                                       // p > 1: nothing removed
   } else if (thr == 0.0) {
@@ -678,7 +729,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
       kst = KEY_MAX;                                  // no crossing: only the kept maximum
       exact_tp = true;
     }
-    exact_tp = exact_tp || forced;
+    exact_tp = exact_tp || forced || force_ref;
   } else {
     const double Th = thr * St;
     // G(c) = tail + sum of p over value keys < c (removed candidates have p = 0);
@@ -686,7 +737,10 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     const unsigned smin32 = (unsigned)smin, vmax32 = (unsigned)vmax;
     const int b0 = (smin32 == vmax32) ? -1 : 31 - __clz(smin32 ^ vmax32);
     unsigned v = b0 < 0 ? smin32 : (b0 >= 31 ? 0u : (vmax32 & ~((2u << b0) - 1u)));
-    if (!CTA && ns < n && n <= LW_CAP / 2) {
+    // a refinement starts from the first pass's crossing and bisects only if that fails
+    const bool near = refine && J.vcross != 0u && step_to_crossing<CTA>(vk, pv, n, tk, tail, Th, J.vcross, &v, R);
+    if (near) {
+    } else if (!CTA && ns < n && n <= LW_CAP / 2) {
       // one warp: bisect over the survivors only, gathered into the unused
       // upper half of the warp's staging area (top-k zeroes the others' mass)
       unsigned* cvk = vk + LW_CAP / 2;
@@ -748,11 +802,14 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
       kst = KEY_MAX;                                  // no crossing: only the kept maximum
       exact_tp = true;
     }
-    exact_tp = exact_tp || forced;
+    exact_tp = exact_tp || forced || force_ref;
   }
   if (exact_tp) {
     if (k0) {                                         // the tail is exact only after a refine
-      if (!refine) hand_back(RES_REFINE);
+      if (!refine) {
+        if (r0 == 0) J.vcross = kst != KEY_MAX ? (unsigned)(kst >> 32) : 0u;
+        hand_back(RES_REFINE);
+      }
       return false;
     }
     // the reference's sequential sums over the survivors in ascending order
@@ -881,16 +938,66 @@ constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)
 constexpr size_t LIST_SMEM_W = (size_t)LIST_WARPS * LW_BYTES, LIST_SMEM_B = LB_HIST + 256 * 8;
 constexpr size_t LIST_SMEM = LIST_SMEM_W > LIST_SMEM_B ? LIST_SMEM_W : LIST_SMEM_B;   // warps' areas / one long list
 
+struct Staged {
+  int shift, body;           // body: bulk-copied elements (0: nothing in flight)
+  int hpos;                  // buffer position of this thread's plain-loaded element (-1: none)
+  float hval;
+};
+// The 16-byte-aligned body of a row that stage_row copies, prefetched into L2
+// one row ahead so that its DRAM reads overlap the current row's work.
+__device__ __forceinline__ void prefetch_row(const float* g, int V) {
+  const unsigned long long ga = (unsigned long long)g;
+  int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);
+  if (head > V) head = V;
+  const int body = ((V - head) >> 2) << 2;
+  if (body > 0) bulk_prefetch_l2(g + head, (unsigned)body * 4u);
+}
+
+__device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf, unsigned long long* bar) {
+  const unsigned long long ga = (unsigned long long)g;
+  int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);
+  if (head > V) head = V;
+  const int body = ((V - head) >> 2) << 2;
+  const int shift = (4 - head) & 3;
+  const int tid = threadIdx.x;
+  if (tid == 0 && body > 0) {
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, (unsigned)body * 4u);
+    bulk_g2s(rowbuf + shift + head, g + head, (unsigned)body * 4u, bar);
+  }
+  Staged st{shift, body, -1, 0.0f};
+  int i = -1;
+  if (tid < 4) i = tid < head ? tid : -1;
+  else if (tid < 8) i = head + body + (tid - 4) < V ? head + body + (tid - 4) : -1;
+  if (i >= 0) {
+    st.hpos = shift + i;
+    st.hval = __ldcs(g + i);
+  }
+  return st;
+}
+
 // A row without top-k whose top-p crossing fell inside the band of its
 // estimated tail, in the list kernel (whole CTA): the exact tail mass (sum of
 // exp((double)(y - m_y)) over every element below the list, each penalised
 // and tempered as the reference does, re-associated: its rounding is inside
 // the list's double-sum band) replaces the estimate and the list job runs
-// again. A row still undecided goes to the general kernel.
+// again, its top-p search starting from the first pass's crossing. A row
+// still undecided goes to the general kernel. The raw row is staged by one
+// bulk copy into the (still free) probability area, so the scan waits for one
+// DRAM round trip; `lbar` is the CTA's mbarrier and lst[0] its phase, lst[1]
+// set once a bounded wait has given up (later refinements then defer).
 __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm, unsigned* vk, double* pv,
-                                            unsigned long long* hist, LRed& R) {
+                                            unsigned long long* hist, LRed& R, unsigned long long* lbar,
+                                            unsigned* lst) {
   const int V = a.V, tid = threadIdx.x;
   RowJob& J = a.jobs[row];
+  if (lst[1]) {
+    if (tid == 0) defer_row(a, row);
+    return;
+  }
+  const float* g = a.logits + (long long)row * a.ld;
+  float* rowbuf = reinterpret_cast<float*>(pv);
+  const Staged sg = stage_row(g, V, rowbuf, lbar);
   const c4s_row_params P = a.params[(long long)row * a.params_stride];
   bool pen = a.hist_off && P.repetition_penalty != 1.0f;
   long long h0 = 0, h1 = 0;
@@ -906,27 +1013,34 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
       const int t = a.hist[j];
       if ((unsigned)t < (unsigned)V) atomicOr(&bm[t >> 5], 1u << (t & 31));
     }
+  if (tid == 0 && sg.body > 0) {
+    if (mbar_wait_bounded(lbar, lst[0])) {
+      lst[0] ^= 1u;
+    } else {
+      lst[1] = 1u;
+      atomicOr(a.errflags, C4S_DEVERR_TIMEOUT);
+      mbar_wait_bounded(lbar, lst[0]);             // let the copy drain (bounded)
+    }
+  }
+  if (sg.hpos >= 0) rowbuf[sg.hpos] = sg.hval;
   csync();
+  if (lst[1]) {
+    if (tid == 0) defer_row(a, row);
+    return;
+  }
   const float pp = P.repetition_penalty, rpen = __frcp_rn(pp);
   const float T = J.T;
   const bool do_t = T != 1.0f;
   const float rT = do_t ? __frcp_rn(T) : 1.0f;
   const unsigned ykex = J.ykex;
   const float m_y = J.m_y;
-  const float* g = a.logits + (long long)row * a.ld;
+  const float* srow = rowbuf + sg.shift;
   double t = 0.0;
-  for (int i0 = tid; i0 < V; i0 += 8 * NT) {
-    float xv[8];                                    // eight loads in flight per thread
-#pragma unroll
-    for (int q = 0; q < 8; ++q) xv[q] = i0 + q * NT < V ? __ldcs(g + i0 + q * NT) : -INFINITY;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int i = i0 + q * NT;
-      float x = xv[q];
-      if (i < V && pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
-      const float y = do_t ? div_rn(x, T, rT) : x;
-      if (x > -INFINITY && fkey(y) <= ykex) t += exp((double)__fsub_rn(y, m_y));
-    }
+  for (int i = tid; i < V; i += NT) {
+    float x = srow[i];
+    if (pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
+    const float y = do_t ? div_rn(x, T, rT) : x;
+    if (x > -INFINITY && fkey(y) <= ykex) t += exp((double)__fsub_rn(y, m_y));
   }
   const double tail = LG<true>::sum(t, R);
   if (tid == 0) {
@@ -934,7 +1048,7 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
     J.tail_err = 0.0;
     atomicAdd(&a.counters[C4S_CNT_EXACT_TAIL], 1ull);
   }
-  csync();
+  csync();                                          // the row buffer is free again
   const size_t o = (size_t)row * LCAP;
   if (!list_job<true>(a, row, J, a.lkeys + o, a.lsb + o, vk, pv, hist, true, R, nullptr) && tid == 0) {
     J.status = RES_DEFER;
@@ -955,9 +1069,14 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   __shared__ int rq[1 + RQ_CAP];
   __shared__ unsigned bm[(F_MAXV + 31) / 32 + 1];
   __shared__ Args sa;                               // for refine_in_list (no local copy)
+  __shared__ unsigned long long lbar;               // refinements' bulk row copies
+  __shared__ unsigned lst[2];                       // its phase; set after a wait gave up
   if (threadIdx.x == 0) {
     rq[0] = 0;
     sa = a;
+    mbar_init(&lbar, 1);
+    lst[0] = 0u;
+    lst[1] = 0u;
   }
   const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
   unsigned* bvk = reinterpret_cast<unsigned*>(lsm + LB_VK);
@@ -972,7 +1091,7 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
         const int r = rq[nq];
         csync();
         if (threadIdx.x == 0) rq[0] = nq - 1;
-        refine_in_list(sa, r, bm, bvk, bpv, bh, R);
+        refine_in_list(sa, r, bm, bvk, bpv, bh, R, &lbar, lst);
         continue;
       }
       if (threadIdx.x == 0) {
@@ -1075,6 +1194,7 @@ __device__ __forceinline__ void fill_job(RowJob& J, const RowCtx& rc, int kind, 
   J.u53 = rc.u53;
   J.xs = rc.xs;
   J.kstar = 0ull;
+  J.vcross = 0u;
 }
 
 // A list longer than one list-kernel warp takes goes to the CTA-wide queue.
@@ -1098,43 +1218,6 @@ __device__ __forceinline__ unsigned oct_fix(float p, int b) {
   return (u == 0u || sh > 31) ? 0u : (m >> max(sh, 0));
 }
 
-struct Staged {
-  int shift, body;           // body: bulk-copied elements (0: nothing in flight)
-  int hpos;                  // buffer position of this thread's plain-loaded element (-1: none)
-  float hval;
-};
-// The 16-byte-aligned body of a row that stage_row copies, prefetched into L2
-// one row ahead so that its DRAM reads overlap the current row's work.
-__device__ __forceinline__ void prefetch_row(const float* g, int V) {
-  const unsigned long long ga = (unsigned long long)g;
-  int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);
-  if (head > V) head = V;
-  const int body = ((V - head) >> 2) << 2;
-  if (body > 0) bulk_prefetch_l2(g + head, (unsigned)body * 4u);
-}
-
-__device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf, unsigned long long* bar) {
-  const unsigned long long ga = (unsigned long long)g;
-  int head = (int)(((16u - (unsigned)(ga & 15ull)) & 15u) >> 2);
-  if (head > V) head = V;
-  const int body = ((V - head) >> 2) << 2;
-  const int shift = (4 - head) & 3;
-  const int tid = threadIdx.x;
-  if (tid == 0 && body > 0) {
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(bar, (unsigned)body * 4u);
-    bulk_g2s(rowbuf + shift + head, g + head, (unsigned)body * 4u, bar);
-  }
-  Staged st{shift, body, -1, 0.0f};
-  int i = -1;
-  if (tid < 4) i = tid < head ? tid : -1;
-  else if (tid < 8) i = head + body + (tid - 4) < V ? head + body + (tid - 4) : -1;
-  if (i >= 0) {
-    st.hpos = shift + i;
-    st.hval = __ldcs(g + i);
-  }
-  return st;
-}
 
 
 // ---------------------------------------------------------------------------
