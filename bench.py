@@ -292,7 +292,8 @@ def run_ours(args):
     err, counters = ctx.status(reset=True)
 
     # ---- per-kernel device time: the same K steps again with CUDA events between
-    # the launches (row kernel -> list kernel -> general path, per 4096-row chunk) ----
+    # the launches (order pre-pass -> row kernel -> list kernel -> general path,
+    # per 4096-row chunk) ----
     ctx.kernel_timing(True)
     ctx.kernel_times(reset=True)
     for s in range(args.steps):

@@ -169,11 +169,14 @@ int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors,
 
 /* Measurement only; no counterpart in the reference. While enabled, every
  * c4s_sample call that takes the fast path records CUDA events on its stream
- * around its three kernels (row, list, general; per chunk of 4096 rows).
+ * around its kernels (per chunk of 4096 rows): the order pre-pass (rows by
+ * cost class; only when a chunk has more rows than the row kernel has CTAs
+ * and per-row parameters), the row, list and general kernels.
  * c4s_kernel_times waits for them and returns the summed device times in
- * milliseconds and the number of launches of each kernel in ms[3] /
- * launches[3]; reset forgets the recorded calls. Not for use while a stream
- * is being captured.                                                        */
+ * milliseconds and the number of launches of each kernel in ms[4] /
+ * launches[4], in that order; reset forgets the recorded calls. Not for use
+ * while a stream is being captured.                                         */
+#define C4S_NUM_KERNEL_TIMERS 4
 int c4s_kernel_timing(c4s_ctx* ctx, int32_t enable);
 int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset);
 

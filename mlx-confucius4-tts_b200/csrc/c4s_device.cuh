@@ -249,6 +249,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsig
   }
   return false;
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while the previous kernel of its stream finishes;
+// grid_dep_wait() returns once that kernel has completed and its writes are
+// visible (at once when there is none), grid_dep_launch() lets the next
+// kernel start launching.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -37,8 +37,10 @@ constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
 constexpr int LW_CAP = 1024;              // list kernel: longest list one warp takes
 constexpr int RQ_CAP = 16;                // list kernel: rows of one CTA waiting for an exact tail
 constexpr int LIST_CLASSES = 6;           // list queues: long (CTA), then warp lists by size, longest first
-constexpr int NCNT = 16;                  // slots of the per-launch counters (defer_cnt)
-static_assert(3 + 2 * LIST_CLASSES <= NCNT, "the queue counters fit");
+constexpr int ROW_CLASSES = 4;            // cost classes of the row kernel's order
+constexpr int ORD_CNT = 3 + 2 * LIST_CLASSES;   // first of their counters in defer_cnt
+constexpr int NCNT = 20;                  // slots of the per-launch counters (defer_cnt)
+static_assert(ORD_CNT + ROW_CLASSES <= NCNT, "the queue and order counters fit");
 
 enum { JOB_NONE = 0, JOB_TOPK = 1, JOB_K0 = 2, JOB_DEFER = 3 };
 enum { RES_DONE = 0, RES_DEFER = 1, RES_REFINE = 2 };
@@ -1078,6 +1080,8 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
     lst[0] = 0u;
     lst[1] = 0u;
   }
+  grid_dep_launch();
+  grid_dep_wait();                                 // the row kernel's jobs, lists and queues
   const unsigned nbig = *reinterpret_cast<volatile unsigned*>(&a.defer_cnt[3]);
   unsigned* bvk = reinterpret_cast<unsigned*>(lsm + LB_VK);
   double* bpv = reinterpret_cast<double*>(lsm + LB_PV);
@@ -1241,6 +1245,8 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
   }
   csync();
   unsigned phase = 0;
+  grid_dep_launch();
+  grid_dep_wait();                                 // the rows the row and list kernels handed back
   const unsigned n = *reinterpret_cast<volatile unsigned*>(a.defer_cnt);
   for (unsigned t = blockIdx.x; t < n; t += gridDim.x) {
     const int row = a.defer_rows[t];
@@ -1254,7 +1260,7 @@ __global__ void __launch_bounds__(NT, 4) defer_kernel(Args a) {
       a.defer_cnt[1] = 0u;
       a.defer_cnt[2] = 0u;                          // the row kernel's row counter
 #pragma unroll
-      for (int c = 3; c < 3 + 2 * LIST_CLASSES; ++c) a.defer_cnt[c] = 0u;   // the list kernel's queues
+      for (int c = 3; c < ORD_CNT + ROW_CLASSES; ++c) a.defer_cnt[c] = 0u;   // list queues, row order
     }
   }
 }

@@ -49,6 +49,7 @@ struct RShared {
   int redi[RWARP];
   float redf[RWARP];
   int abort_row;
+  int ocnt[ROW_CLASSES];                           // rows per cost class (with a.order)
 };
 
 // Slot geometry of one row: element i sits at buffer position shift + i;
@@ -482,6 +483,57 @@ __device__ __forceinline__ int row_body(const Args& a, const Args& ao, int row, 
   return k0_body(ao, row, rc, rb, g, S, keys);
 }
 
+// Rows by cost class for the row kernel, dearest first, so that its last
+// wave holds cheap rows and its CTAs finish together: sampled rows without
+// top-k (octave histogram), top-k above 64 (two maxima per lane), other top-k,
+// then greedy and inactive rows. One CTA of ORDER_NT threads for a chunk of
+// up to K_CHUNK rows: class slots from shared-memory counters (one atomic per
+// class and warp), the class sizes stored to defer_cnt[ORD_CNT + c].
+constexpr int ORDER_NT = 1024;
+__global__ void __launch_bounds__(ORDER_NT) order_kernel(Args a) {
+  __shared__ unsigned cnt[ROW_CLASSES];
+  const int lane = threadIdx.x & 31;
+  grid_dep_launch();
+  grid_dep_wait();                                 // the previous call resets the class counters
+  if (threadIdx.x < ROW_CLASSES) cnt[threadIdx.x] = 0u;
+  __syncthreads();
+  for (int r0 = 0; r0 < a.B; r0 += ORDER_NT) {
+    const int r = r0 + (int)threadIdx.x;
+    int c = -1;
+    if (r < a.B) {
+      const c4s_row_params P = a.params[(long long)r * a.params_stride];
+      const bool act = a.active == nullptr || a.active[r] != 0;
+      const int k = P.top_k;
+      c = (!act || P.greedy) ? 3 : (k <= 0 || k >= a.V) ? 0 : k > RWARP * 32 / 2 ? 1 : 2;
+    }
+#pragma unroll
+    for (int cc = 0; cc < ROW_CLASSES; ++cc) {
+      const unsigned m = __ballot_sync(FULL, c == cc);
+      if (m == 0u) continue;
+      const int leader = __ffs(m) - 1;
+      unsigned base = 0u;
+      if (lane == leader) base = atomicAdd(&cnt[cc], (unsigned)__popc(m));
+      base = __shfl_sync(FULL, base, leader);
+      const unsigned slot = base + (unsigned)__popc(m & ((1u << lane) - 1u));
+      if (c == cc && slot < (unsigned)K_CHUNK) a.order[(size_t)cc * K_CHUNK + slot] = r;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < ROW_CLASSES) a.defer_cnt[ORD_CNT + threadIdx.x] = cnt[threadIdx.x];
+}
+
+// The row of the row kernel's t-th ticket (B: none left).
+__device__ __forceinline__ int ticket_row(const Args& a, const RShared& S, int t) {
+  if (t >= a.B) return a.B;
+  if (a.order == nullptr) return t;
+#pragma unroll
+  for (int c = 0; c < ROW_CLASSES; ++c) {
+    if (t < S.ocnt[c]) return t < K_CHUNK ? a.order[(size_t)c * K_CHUNK + t] : a.B;
+    t -= S.ocnt[c];
+  }
+  return a.B;
+}
+
 // Persistent row kernel: rows handed out dynamically (the first G statically).
 __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
   extern __shared__ __align__(128) float rb[];     // the staged row
@@ -511,8 +563,14 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
     else if (tid == 6) act_pend = a.active ? (int)a.active[r] : 1;
   };
   unsigned* row_ctr = a.defer_cnt + 2;
-  const int r0 = blockIdx.x;
-  if (tid == 0) S.nrow[0] = G + (int)atomicAdd(row_ctr, 1u);
+  grid_dep_launch();
+  grid_dep_wait();                                 // counters, order and RNG states of earlier launches
+  if (a.order != nullptr) {
+    if (tid < ROW_CLASSES) S.ocnt[tid] = (int)a.defer_cnt[ORD_CNT + tid];
+    rsync();
+  }
+  const int r0 = ticket_row(a, S, blockIdx.x);
+  if (tid == 0) S.nrow[0] = ticket_row(a, S, G + (int)atomicAdd(row_ctr, 1u));
   issue_meta(r0, S.meta[0]);
   cp_async_commit();
   if (tid == 6 && r0 < a.B) S.meta[0].active = act_pend;
@@ -614,7 +672,7 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
       a.out_ids[row] = -1;
       a.jobs[row].kind = JOB_NONE;
     }
-    if (tid == 0) S.nrow[(j + 1) & 1] = next < a.B ? G + (int)atomicAdd(row_ctr, 1u) : a.B;   // the row after next
+    if (tid == 0) S.nrow[(j + 1) & 1] = next < a.B ? ticket_row(a, S, G + (int)atomicAdd(row_ctr, 1u)) : a.B;   // the row after next
     cp_async_wait<0>();
     rsync();                                       // next metadata visible; the row buffer is free
     sg = Staged{0, 0, -1, 0.0f};

@@ -110,10 +110,12 @@ struct c4s_ctx {
   unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
   unsigned long long* d_lsb = nullptr;
   int* d_defer_rows = nullptr;                 //   rows handed to the general path, then long lists
+  int* d_order = nullptr;                      //   the row kernel's rows by cost class
   unsigned* d_defer_cnt = nullptr;
   int debug = 0;
   bool timing = false;                         // c4s_kernel_timing: events between fast-path launches
-  std::vector<cudaEvent_t> tev;                //   4 per recorded chunk (before row, after row/list/defer)
+  std::vector<cudaEvent_t> tev;                //   5 per recorded chunk (before order, after order/row/list/defer)
+  std::vector<unsigned char> tev_order;        //   per recorded chunk: the order pre-pass ran
   size_t tev_used = 0;
   int cached_V = -1;
   int cached_occ = 0;
@@ -158,16 +160,37 @@ int occupancy(c4s_ctx* ctx, int V, size_t smem) {
 
 // Four timing events for the next recorded chunk (nullptr if they cannot be made).
 cudaEvent_t* timing_slot(c4s_ctx* ctx) {
-  if (ctx->tev_used + 4 > ctx->tev.size()) {
-    for (int i = 0; i < 4; ++i) {
+  if (ctx->tev_used + 5 > ctx->tev.size()) {
+    for (int i = 0; i < 5; ++i) {
       cudaEvent_t e;
       if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
       ctx->tev.push_back(e);
     }
   }
   cudaEvent_t* ev = ctx->tev.data() + ctx->tev_used;
-  ctx->tev_used += 4;
+  ctx->tev_used += 5;
+  ctx->tev_order.resize(ctx->tev_used / 5);
+  ctx->tev_order.back() = 0;
   return ev;
+}
+
+// The fast path's kernels are launched with programmatic stream serialisation:
+// each starts launching while its predecessor in the stream drains and waits
+// in grid_dep_wait() before it reads what earlier launches wrote, so the gaps
+// between the kernels of a step (and between steps) close.
+template <typename K>
+cudaError_t launch_pdl(K kern, int grid, int block, size_t smem, cudaStream_t st, const c4s::Args& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
@@ -218,15 +241,27 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       const int g1 = (int)std::min<long long>(ac.B, (long long)ctx->row_occ * ctx->num_sms);
       cudaEvent_t* ev = ctx->timing ? timing_slot(ctx) : nullptr;
       if (ev) cudaEventRecord(ev[0], st);
-      row_kernel<<<g1, RT, R_SMEM, st>>>(ac);
+      // more rows than CTAs, of varying kinds: the dearest rows go first
+      ac.order = nullptr;
+      if (ac.B > g1 && ac.params_stride != 0) {
+        ac.order = ctx->d_order;
+        e = launch_pdl(order_kernel, 1, ORDER_NT, 0, st, ac);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "order kernel launch");
+        if (ev) ctx->tev_order.back() = 1;
+      }
       if (ev) cudaEventRecord(ev[1], st);
+      e = launch_pdl(row_kernel, g1, RT, R_SMEM, st, ac);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "row kernel launch");
+      if (ev) cudaEventRecord(ev[2], st);
       const int g2 = (int)std::min<long long>((ac.B + LIST_WARPS - 1) / LIST_WARPS,
                                                    (long long)ctx->list_occ * ctx->num_sms);
-      list_kernel<<<g2, 32 * LIST_WARPS, LIST_SMEM, st>>>(ac);
-      if (ev) cudaEventRecord(ev[2], st);
-      const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
-      defer_kernel<<<g3, NT, gsm, st>>>(ac);
+      e = launch_pdl(list_kernel, g2, 32 * LIST_WARPS, LIST_SMEM, st, ac);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "list kernel launch");
       if (ev) cudaEventRecord(ev[3], st);
+      const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
+      e = launch_pdl(defer_kernel, g3, NT, gsm, st, ac);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "general kernel launch");
+      if (ev) cudaEventRecord(ev[4], st);
       if (a.out_logits) mask_kernel<<<ac.B, NT, 0, st>>>(ac);
       e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(ctx, e, "fast path launch");
@@ -255,6 +290,7 @@ void free_all(c4s_ctx* ctx) {
   cudaFree(ctx->d_lkeys);
   cudaFree(ctx->d_lsb);
   cudaFree(ctx->d_defer_rows);
+  cudaFree(ctx->d_order);
   cudaFree(ctx->d_defer_cnt);
 }
 
@@ -329,6 +365,7 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lkeys, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (1 + c4s::LIST_CLASSES) * (size_t)c4s::K_CHUNK * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_order, c4s::ROW_CLASSES * (size_t)c4s::K_CHUNK * sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, c4s::NCNT * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, c4s::NCNT * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));
@@ -373,18 +410,21 @@ int c4s_kernel_timing(c4s_ctx* ctx, int32_t enable) {
 int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset) {
   if (!ctx || !ms || !launches) return C4S_ERR_INVALID;
   DeviceGuard dg(ctx->device);
-  for (int k = 0; k < 3; ++k) { ms[k] = 0.0; launches[k] = 0; }
-  for (size_t c = 0; c + 4 <= ctx->tev_used; c += 4) {
-    for (int k = 0; k < 3; ++k) {
+  for (int k = 0; k < 4; ++k) { ms[k] = 0.0; launches[k] = 0; }
+  for (size_t c = 0; c + 5 <= ctx->tev_used; c += 5) {
+    for (int k = 0; k < 4; ++k) {
       if (cudaEventSynchronize(ctx->tev[c + k + 1]) != cudaSuccess) return fail(ctx, C4S_ERR_CUDA, "timing event");
       float t = 0.0f;
       if (cudaEventElapsedTime(&t, ctx->tev[c + k], ctx->tev[c + k + 1]) != cudaSuccess)
         return fail(ctx, C4S_ERR_CUDA, "timing event");
       ms[k] += t;
-      launches[k] += 1;
+      launches[k] += k > 0 ? 1 : ctx->tev_order[c / 5];
     }
   }
-  if (reset) ctx->tev_used = 0;
+  if (reset) {
+    ctx->tev_used = 0;
+    ctx->tev_order.clear();
+  }
   return C4S_OK;
 }
 

@@ -164,10 +164,11 @@ class SamplingContext:
 
     def kernel_times(self, reset: bool = True):
         """{kernel: (summed device ms, launches)} of the calls recorded so far."""
-        ms = (C.c_double * 3)()
-        n = (C.c_int64 * 3)()
+        ms = (C.c_double * 4)()
+        n = (C.c_int64 * 4)()
         self._check(self.lib.c4s_kernel_times(self._h, ms, n, int(reset)), "c4s_kernel_times")
-        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(("row_kernel", "list_kernel", "defer_kernel"))}
+        names = ("order_kernel", "row_kernel", "list_kernel", "defer_kernel")
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(names)}
 
     # -- batched entry points -----------------------------------------------------
     def seed_states(self, B: int, seed: int, row_offset: int = 0, out=None, stream=None):
