@@ -25,6 +25,7 @@
 #pragma once
 
 #include "c4s_general.cuh"
+#include "c4s_exp.cuh"
 
 namespace c4s {
 
@@ -978,11 +979,14 @@ __device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf
   return st;
 }
 
+__device__ const double EXP2_J64[64] = C4S_EXP2_J64_TABLE;   // exp_tail's table
+
 // A row without top-k whose top-p crossing fell inside the band of its
 // estimated tail, in the list kernel (whole CTA): the exact tail mass (sum of
 // exp((double)(y - m_y)) over every element below the list, each penalised
 // and tempered as the reference does, re-associated: its rounding is inside
-// the list's double-sum band) replaces the estimate and the list job runs
+// the list's double-sum band; each term by exp_tail, within 2^-51 of the
+// reference's, so tail_err = 2^-50 tail) replaces the estimate and the list job runs
 // again, its top-p search starting from the first pass's crossing. A row
 // still undecided goes to the general kernel. The raw row is staged by one
 // bulk copy into the (still free) probability area, so the scan waits for one
@@ -1008,13 +1012,29 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
     h1 = a.hist_off[row + 1];
     if (h0 < 0 || h1 < h0 || h1 > a.hist_total) pen = false;   // the row kernel flagged it
   }
+  // history ids eight per thread at a time, the first batch in flight while the bitmap clears
+  int hv[8];
+  long long j0 = h0 + tid;
+  auto load_ids = [&]() {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const long long j = j0 + (long long)q * NT;
+      hv[q] = (pen && j < h1) ? a.hist[j] : -1;
+    }
+  };
+  load_ids();
   for (int w = tid; w < (V + 31) / 32; w += NT) bm[w] = 0u;
   csync();
-  if (pen)
-    for (long long j = h0 + tid; j < h1; j += NT) {
-      const int t = a.hist[j];
-      if ((unsigned)t < (unsigned)V) atomicOr(&bm[t >> 5], 1u << (t & 31));
+  if (pen) {
+    for (;;) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if ((unsigned)hv[q] < (unsigned)V) atomicOr(&bm[hv[q] >> 5], 1u << (hv[q] & 31));
+      j0 += 8LL * NT;
+      if (j0 >= h1) break;
+      load_ids();
     }
+  }
   if (tid == 0 && sg.body > 0) {
     if (mbar_wait_bounded(lbar, lst[0])) {
       lst[0] ^= 1u;
@@ -1042,12 +1062,12 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
     float x = srow[i];
     if (pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
     const float y = do_t ? div_rn(x, T, rT) : x;
-    if (x > -INFINITY && fkey(y) <= ykex) t += exp((double)__fsub_rn(y, m_y));
+    if (x > -INFINITY && fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), EXP2_J64);
   }
   const double tail = LG<true>::sum(t, R);
   if (tid == 0) {
     J.tail = tail;
-    J.tail_err = 0.0;
+    J.tail_err = ldexp(tail, -50);
     atomicAdd(&a.counters[C4S_CNT_EXACT_TAIL], 1ull);
   }
   csync();                                          // the row buffer is free again
@@ -1209,20 +1229,6 @@ __device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
 }
 
 enum { ROW_DONE = 0, ROW_GENERAL = 1 };
-
-// Fixed-point octave mass of an estimate p in octave b (p <= 2^-b up to a
-// few ulps): p * 2^(b+20), truncated, from the float's bits (below 2^21, so
-// a bin's u32 sum over at most 2^10 elements cannot overflow). Truncation
-// loses less than 2^-(b+20) per element, i.e. below 2^-19 of any element in
-// octaves < NOCT.
-__device__ __forceinline__ unsigned oct_fix(float p, int b) {
-  const unsigned u = __float_as_uint(p);
-  const int sh = 130 - (int)(u >> 23) - b;        // 23 - 20 - (exponent + b)
-  const unsigned m = (u & 0x007fffffu) | 0x00800000u;
-  return (u == 0u || sh > 31) ? 0u : (m >> max(sh, 0));
-}
-
-
 
 // ---------------------------------------------------------------------------
 // The general path for the rows the row and list kernels handed back; the

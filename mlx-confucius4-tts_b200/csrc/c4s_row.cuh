@@ -44,7 +44,8 @@ struct RShared {
   MetaSlot meta[2];
   int nrow[2];
   unsigned bm[(F_MAXV + 31) / 32 + 4];             // penalty de-duplication bitmap
-  unsigned hw[RWARP][HREP][32];                    // octave bins, per warp and lane & 7
+  unsigned hw[RWARP][HREP][33];                    // octave bins, per warp and lane & 7; rows of 33 words
+                                                   // put the replicas of a bin in different banks
   unsigned redu[RWARP];
   int redi[RWARP];
   float redf[RWARP];
@@ -252,9 +253,8 @@ __device__ __noinline__ int k0_body(const Args& a, int row, const RowCtx rc, con
   if (!(rc.thr > 0.0) || (a.debug & C4S_DEBUG_FORCE_BINS)) return ROW_GENERAL;
   // octave histogram of the estimates: per-warp fixed-point bins (exact adds)
   {
-    unsigned* hz = &S.hw[warp][0][0];
 #pragma unroll
-    for (int r = 0; r < HREP; ++r) hz[32 * r + lane] = 0u;
+    for (int r = 0; r < HREP; ++r) S.hw[warp][r][lane] = 0u;
   }
   __syncwarp();
   unsigned* hrep = &S.hw[warp][lane & (HREP - 1)][0];   // fewer lanes per bin address
@@ -263,9 +263,16 @@ __device__ __noinline__ int k0_body(const Args& a, int row, const RowCtx rc, con
     const float4 v = rload(rb, g, rslot(g, q));
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float t = oct_t(rc, f4c(v, c));
-      const int b = oct_of_t(t);
-      const unsigned m = oct_fix(__expf(fmaxf(t, -200.0f)), b);
+      // octave b = oct_of_t(t) and the estimate's mass in units of 2^-(b+20),
+      // truncated: 2^(b - ns) 2^20 with ns = RN(-t log2 e); b - ns is exact
+      // (in (-1, 0] below NOCT), so the error is ex2.approx's own plus the
+      // rounding of ns, inside the 2 + 1.16 |t| ulp that the estimate's bound
+      // allows for an exponential of t, and truncation loses below 2^-19 of
+      // an element below NOCT. Below 2^21 per element, a replica's u32 bin
+      // (at most 2^10 elements) cannot overflow; padding (-inf) gives 0.
+      const float ns = oct_t(rc, f4c(v, c)) * -1.4426950408889634f;
+      const int b = (int)fminf(ns, (float)NOCT);
+      const unsigned m = (unsigned)(ex2_approx((float)b - ns) * 1048576.0f);
       if (m) atomicAdd(&hrep[b], m);
     }
   }
