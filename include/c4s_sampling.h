@@ -81,6 +81,10 @@ typedef struct c4s_row_params {
 /* Device-side error bits reported by c4s_get_status().                     */
 #define C4S_DEVERR_HIST_RANGE 1u /* a row's history offsets were out of range */
 #define C4S_DEVERR_TIMEOUT 2u    /* a bounded wait on a bulk copy gave up      */
+#define C4S_DEVERR_SHARD 4u      /* vocab-sharded merge: a row it cannot decide
+                                    exactly (top_k outside [1, 64], or more than
+                                    64 of a shard's values tied at the top_k
+                                    threshold); the row's id is -1            */
 
 /* Counter slots reported by c4s_get_status() (rows that took each path).    */
 #define C4S_CNT_TOPP_EXACT_FALLBACK 0 /* top-p guard band hit: exact re-sum   */
@@ -203,6 +207,61 @@ int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld,
                       int64_t hist_total, const c4s_row_params* d_params,
                       int32_t params_stride, uint64_t* d_rng,
                       const uint8_t* d_active, int32_t* d_out_ids, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Vocab-sharded sampling: the vocabulary of every row is split into
+ * contiguous shards (one per GPU), and no GPU holds a whole row. One step is
+ *
+ *   c4s_shard_candidates  on every shard: penalty (history ids inside the
+ *                         shard), temperature, the shard's 64 largest values;
+ *   all-gather            of the [B][64] candidate blocks of all shards
+ *                         (ncclAllGather, 512 B per row and shard);
+ *   c4s_merge_candidates  on every GPU: greedy argmax, or top_k, top_p and the
+ *                         xorshift64 draw over the gathered candidates.
+ *
+ * Every GPU gets the same ids and advances the same xorshift64 states. For
+ * sampled rows the result equals c4s_sample on the whole row (the reference's
+ * text2semantic.cpp:303-331) when 1 <= top_k <= 64; other sampled rows are
+ * refused per row (id -1, C4S_DEVERR_SHARD). The reference has no vocab
+ * sharding; these two calls together replace the same per-row body as
+ * c4s_sample (text2semantic.cpp:303-331).                                  */
+#define C4S_SHARD_CANDIDATES 64
+#define C4S_MAX_SHARDS 16
+#define C4S_CAND_TIES 0x80000000u /* set in the last candidate's index when the
+                                     shard has more values equal to its 64th */
+typedef struct c4s_candidate {
+  float value;    /* penalised (and, for sampled rows, tempered) logit        */
+  int32_t index;  /* global vocabulary index; bit 31 = C4S_CAND_TIES         */
+} c4s_candidate;
+
+/* Candidates of one shard for B rows.
+ *   d_logits      fp32 [B, ld]: this shard's V_shard columns of every row
+ *                 (ld >= V_shard; 4-byte aligned rows)
+ *   vocab_offset  global index of the shard's first column; the shard covers
+ *                 [vocab_offset, vocab_offset + V_shard) of [0, V)
+ *   d_hist..params_stride, d_active   as for c4s_sample (history ids are
+ *                 global; each shard penalises the ones it holds)
+ *   d_cand        c4s_candidate [B][C4S_SHARD_CANDIDATES], largest value
+ *                 first, ties by ascending index; inactive rows are skipped.
+ * 64 <= V_shard <= 32768.                                                   */
+int c4s_shard_candidates(c4s_ctx* ctx, const float* d_logits, int32_t B,
+                         int32_t V_shard, int64_t ld, int32_t vocab_offset,
+                         int32_t V, const int32_t* d_hist,
+                         const int64_t* d_hist_off, int64_t hist_total,
+                         const c4s_row_params* d_params, int32_t params_stride,
+                         const uint8_t* d_active, c4s_candidate* d_cand,
+                         void* stream);
+
+/* Token ids from the candidates of `num_shards` shards (1..C4S_MAX_SHARDS),
+ * shard s's block at d_cand + s * shard_stride (shard_stride >= B * 64, in
+ * candidates: the layout of an all-gather of the [B][64] blocks, shards in
+ * vocabulary order). d_rng, d_active and d_out_ids as for c4s_sample.        */
+int c4s_merge_candidates(c4s_ctx* ctx, const c4s_candidate* d_cand,
+                         int32_t num_shards, int64_t shard_stride, int32_t B,
+                         int32_t V, const c4s_row_params* d_params,
+                         int32_t params_stride, uint64_t* d_rng,
+                         const uint8_t* d_active, int32_t* d_out_ids,
+                         void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -42,6 +42,7 @@
 #include "c4s_general.cuh"
 #include "c4s_fast.cuh"
 #include "c4s_row.cuh"
+#include "c4s_shard.cuh"
 
 namespace c4s {
 
@@ -344,6 +345,9 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
     e = cudaFuncSetAttribute(c4s::defer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c4s::LIST_SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::shard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)c4s::shard_smem_bytes(c4s::MAX_VOCAB));
   // the row kernel keeps five rows in flight per SM only with the largest
   // shared-memory carveout
   if (e == cudaSuccess)
@@ -560,6 +564,74 @@ int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld, c
   const int grid = std::min(B, c4s::STATIC_CTAS);
   c4s::rows_kernel<<<grid, c4s::NT, c4s::layout_for(V).total, (cudaStream_t)stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? C4S_OK : C4S_ERR_CUDA;
+}
+
+int c4s_shard_candidates(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V_shard, int64_t ld,
+                         int32_t vocab_offset, int32_t V, const int32_t* d_hist, const int64_t* d_hist_off,
+                         int64_t hist_total, const c4s_row_params* d_params, int32_t params_stride,
+                         const uint8_t* d_active, c4s_candidate* d_cand, void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (B < 0) return fail(ctx, C4S_ERR_INVALID, "B < 0");
+  if (V_shard < c4s::SHARD_CAND) return fail(ctx, C4S_ERR_INVALID, "V_shard < 64");
+  if (V_shard > c4s::MAX_VOCAB) return fail(ctx, C4S_ERR_CAPACITY, "V_shard above 32768");
+  if (vocab_offset < 0 || (int64_t)vocab_offset + V_shard > V)
+    return fail(ctx, C4S_ERR_INVALID, "shard outside [0, V)");
+  if (ld < V_shard) return fail(ctx, C4S_ERR_INVALID, "ld < V_shard");
+  if (B == 0) return C4S_OK;
+  if (!d_logits || !d_params || !d_cand) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if (params_stride != 0 && params_stride != 1) return fail(ctx, C4S_ERR_INVALID, "params_stride not 0/1");
+  if (d_hist_off && (!d_hist && hist_total > 0)) return fail(ctx, C4S_ERR_INVALID, "history ids missing");
+  if (hist_total < 0) return fail(ctx, C4S_ERR_INVALID, "hist_total < 0");
+  if (((uintptr_t)d_logits & 3) || ((uintptr_t)d_cand & 7)) return fail(ctx, C4S_ERR_INVALID, "misaligned pointer");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  c4s::ShardArgs a{};
+  a.logits = d_logits;
+  a.B = B; a.Vs = V_shard; a.ld = ld; a.voff = vocab_offset; a.Vtot = V;
+  a.hist = d_hist; a.hist_off = reinterpret_cast<const long long*>(d_hist_off); a.hist_total = hist_total;
+  a.params = d_params; a.params_stride = params_stride;
+  a.active = d_active;
+  a.cand = d_cand;
+  a.errflags = ctx->d_err;
+  const size_t smem = c4s::shard_smem_bytes(V_shard);
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, c4s::shard_kernel, c4s::NT, smem);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "shard_kernel occupancy");
+  const int grid = (int)std::min<long long>((long long)B, (long long)std::max(occ, 1) * ctx->num_sms);
+  c4s::shard_kernel<<<grid, c4s::NT, smem, (cudaStream_t)stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "shard_kernel launch");
+  return C4S_OK;
+}
+
+int c4s_merge_candidates(c4s_ctx* ctx, const c4s_candidate* d_cand, int32_t num_shards, int64_t shard_stride,
+                         int32_t B, int32_t V, const c4s_row_params* d_params, int32_t params_stride,
+                         uint64_t* d_rng, const uint8_t* d_active, int32_t* d_out_ids, void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (B < 0) return fail(ctx, C4S_ERR_INVALID, "B < 0");
+  if (num_shards < 1 || num_shards > c4s::MAX_SHARDS) return fail(ctx, C4S_ERR_INVALID, "num_shards outside [1, 16]");
+  if (V < 1) return fail(ctx, C4S_ERR_INVALID, "V < 1");
+  if (B == 0) return C4S_OK;
+  if (num_shards > 1 && shard_stride < (int64_t)B * c4s::SHARD_CAND)
+    return fail(ctx, C4S_ERR_INVALID, "shard_stride < B * 64");
+  if (!d_cand || !d_params || !d_rng || !d_out_ids) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if (params_stride != 0 && params_stride != 1) return fail(ctx, C4S_ERR_INVALID, "params_stride not 0/1");
+  if ((uintptr_t)d_cand & 7) return fail(ctx, C4S_ERR_INVALID, "misaligned pointer");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  c4s::MergeArgs a{};
+  a.cand = d_cand;
+  a.G = num_shards; a.B = B; a.Vtot = V; a.shard_stride = shard_stride;
+  a.params = d_params; a.params_stride = params_stride;
+  a.rng = reinterpret_cast<unsigned long long*>(d_rng);
+  a.active = d_active;
+  a.out_ids = d_out_ids;
+  a.errflags = ctx->d_err;
+  const int grid = (int)std::min<long long>((long long)B, 8LL * ctx->num_sms);
+  c4s::merge_kernel<<<grid, c4s::NT, 0, (cudaStream_t)stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "merge_kernel launch");
+  return C4S_OK;
 }
 
 int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors, uint64_t* counters, int32_t reset, void* stream) {

@@ -39,6 +39,9 @@ DEBUG_FORCE_REFINE = 4
 COUNTER_NAMES = ("topp_exact_fallback", "draw_exact_fallback", "topk_radix",
                  "topp_binned", "draw_rowpass", "deferred", "exact_tail")
 MAX_VOCAB = 32768
+SHARD_CANDIDATES = 64   # candidates per row and vocab shard (C4S_SHARD_CANDIDATES)
+MAX_SHARDS = 16
+DEVERR_SHARD = 4
 
 _STATUS = {0: "ok", -1: "invalid argument", -2: "CUDA error", -3: "capacity exceeded",
            -4: "device-side error", -5: "device wait timed out", -6: "collective failed"}
@@ -81,6 +84,9 @@ def library() -> C.CDLL:
                 "c4s_get_status": ([vp, vp, vp, i32, vp], C.c_int),
                 "c4s_kernel_timing": ([vp, i32], C.c_int),
                 "c4s_kernel_times": ([vp, vp, vp, i32], C.c_int),
+                "c4s_shard_candidates": ([vp, vp, i32, i32, i64, i32, i32, vp, vp, i64, vp, i32, vp, vp,
+                                          vp], C.c_int),
+                "c4s_merge_candidates": ([vp, vp, i32, i64, i32, i32, vp, i32, vp, vp, vp, vp], C.c_int),
             }
             for name, (args, res) in sig.items():
                 f = getattr(L, name)
@@ -232,6 +238,39 @@ class SamplingContext:
                     stream=stream)
         out_ids.copy_(d["ids"], non_blocking=True)
         rng.copy_(d["rng"], non_blocking=True)
+        return out_ids
+
+    def shard_candidates(self, logits, V: int, vocab_offset: int, hist, hist_off, params,
+                         active=None, out=None, V_shard: int | None = None, params_stride: int = 1,
+                         stream=None):
+        """Candidates of one vocab shard: ``logits`` [B, ld] holds the shard's
+        columns [vocab_offset, vocab_offset + V_shard) of rows of width V.
+        Returns int64 [B, 64] raw c4s_candidate records (value, global index)."""
+        torch = _torch()
+        B, ld = logits.shape
+        V_shard = ld if V_shard is None else V_shard
+        if out is None:
+            out = torch.empty((B, SHARD_CANDIDATES), dtype=torch.int64, device=logits.device)
+        total = 0 if hist is None else hist.numel()
+        rc = self.lib.c4s_shard_candidates(
+            self._h, _dptr(logits), B, V_shard, logits.stride(0), vocab_offset, V, _dptr(hist),
+            _dptr(hist_off), total, _dptr(params), params_stride, _dptr(active), _dptr(out),
+            self._stream(stream))
+        self._check(rc, "c4s_shard_candidates")
+        return out
+
+    def merge_candidates(self, cand, V: int, params, rng, active=None, out_ids=None,
+                         params_stride: int = 1, stream=None):
+        """Token ids from gathered candidates ``cand`` int64 [G, B, 64] (shards
+        in vocabulary order); advances ``rng`` like ``sample``."""
+        torch = _torch()
+        G, B, _ = cand.shape
+        if out_ids is None:
+            out_ids = torch.empty(B, dtype=torch.int32, device=cand.device)
+        rc = self.lib.c4s_merge_candidates(
+            self._h, _dptr(cand), G, cand.stride(0), B, V, _dptr(params), params_stride, _dptr(rng),
+            _dptr(active), _dptr(out_ids), self._stream(stream))
+        self._check(rc, "c4s_merge_candidates")
         return out_ids
 
     def process(self, logits, hist, hist_off, params, stages: int, V: int | None = None,

@@ -1,0 +1,70 @@
+"""Vocab-sharded sampling: every row's vocabulary split across GPUs.
+
+No GPU holds a whole row, so one step is three parts (include/c4s_sampling.h):
+each rank computes the 64 largest penalised, tempered values of its shard
+(``SamplingContext.shard_candidates``), the ranks all-gather those [B, 64]
+blocks over NCCL, and every rank merges them into the same token ids with the
+same xorshift64 state updates (``SamplingContext.merge_candidates``). For
+rows with 1 <= top_k <= 64 the ids equal those of sampling the whole row
+(text2semantic.cpp:303-331 of the reference); other sampled rows come back
+as -1 with the C4S_DEVERR_SHARD error bit.
+"""
+from __future__ import annotations
+
+from .sampling import SHARD_CANDIDATES
+from .sharding import shard_rows
+
+
+def shard_vocab(V: int, rank: int, world: int) -> tuple[int, int]:
+    """(first column, width) of `rank`'s contiguous vocabulary shard."""
+    return shard_rows(V, rank, world)
+
+
+def sample_vocab_sharded(ctx, logits_shard, V: int, hist, hist_off, params, rng, group=None,
+                         active=None, out_ids=None, params_stride: int = 1, cand_out=None):
+    """One sampling step on this rank's shard of every row.
+
+    ``logits_shard`` [B, ld] holds the columns ``shard_vocab(V, rank, world)``
+    of each row (rank and world of ``group``, the default process group if
+    None). ``hist``/``hist_off`` carry global ids. Returns int32 ids [B],
+    identical on every rank; ``rng`` is advanced identically on every rank.
+    """
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    voff, width = shard_vocab(V, rank, world)
+    B = logits_shard.shape[0]
+    dev = logits_shard.device
+    local = torch.empty((B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
+    ctx.shard_candidates(logits_shard, V, voff, hist, hist_off, params, active=active,
+                         out=local, V_shard=width, params_stride=params_stride)
+    if world > 1:
+        if cand_out is None:
+            cand_out = torch.empty((world, B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(cand_out.view(world * B, SHARD_CANDIDATES), local, group=group)
+    else:
+        cand_out = local.unsqueeze(0)
+    return ctx.merge_candidates(cand_out, V, params, rng, active=active, out_ids=out_ids,
+                                params_stride=params_stride)
+
+
+def sample_vocab_split(ctx, logits, num_shards: int, hist, hist_off, params, rng, active=None,
+                       out_ids=None, params_stride: int = 1, cand_out=None, V: int | None = None):
+    """The same step with all shards on one GPU: ``logits`` [B, ld] holds whole
+    rows; shard s is the column block ``shard_vocab(V, s, num_shards)``, and
+    the candidate blocks land directly in the gathered layout [G, B, 64]."""
+    import torch
+
+    B, ld = logits.shape
+    V = ld if V is None else V
+    if cand_out is None:
+        cand_out = torch.empty((num_shards, B, SHARD_CANDIDATES), dtype=torch.int64,
+                               device=logits.device)
+    for s in range(num_shards):
+        voff, width = shard_vocab(V, s, num_shards)
+        ctx.shard_candidates(logits[:, voff:], V, voff, hist, hist_off, params, active=active,
+                             out=cand_out[s], V_shard=width, params_stride=params_stride)
+    return ctx.merge_candidates(cand_out, V, params, rng, active=active, out_ids=out_ids,
+                                params_stride=params_stride)

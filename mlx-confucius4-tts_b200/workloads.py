@@ -126,6 +126,22 @@ def config2(seed: int = 2, B: int = 4096, V: int = SEMANTIC_VOCAB,
     return Batch(logits, V, hist, off, params, seed_states(B, seed, row_offset))
 
 
+VOCAB_SHARDED_V = 65536       # config 4: 8 contiguous shards of 8192
+
+
+def config4(seed: int = 4, B: int = 512, V: int = VOCAB_SHARDED_V, top_k: int = 50,
+            top_p: float = 0.9) -> Batch:
+    """c4: vocab-sharded stress batch -- B=512 rows of V=65536 ~N(0, 3^2),
+    history 1024/row with ids uniform over the whole vocabulary, global
+    top_k 50 / top_p 0.9 with the reference's other defaults (T 0.8,
+    penalty 10), per-row states from seed `seed`."""
+    g = np.random.default_rng(5000 + seed)
+    logits = normal_logits(g, B, V)
+    hist, off = csr_history(g, np.full(B, 1024), hi=V)
+    return Batch(logits, V, hist, off, make_params(B, top_k=top_k, top_p=top_p),
+                 seed_states(B, seed))
+
+
 def append_history(hist: np.ndarray, off: np.ndarray, toks: np.ndarray,
                    active: np.ndarray | None = None):
     """Append one token per (active) row to a CSR history (text2semantic.cpp:334)."""
