@@ -35,6 +35,7 @@ constexpr int SHARD_CAND = C4S_SHARD_CANDIDATES;  // candidates per row and shar
 constexpr int SHARD_LIST = 1024;                   // fast-path list capacity
 constexpr int MAX_SHARDS = C4S_MAX_SHARDS;
 constexpr unsigned CAND_TIES = C4S_CAND_TIES;
+static_assert(SHARD_CAND * MAX_SHARDS % NT == 0, "merge ranks whole passes of the block");
 
 struct ShardArgs {
   const float* logits;   // this shard's columns: row r at logits + r * ld
@@ -69,8 +70,9 @@ __host__ __device__ inline size_t shard_smem_bytes(int Vs) {
 
 // Writes the row's 64 candidates from an ascending list of keys
 // (~fkey(value) << 32 | local index): largest value first, ties by index.
+// `temper`: srow holds untempered values; the emitted value is RN(x / T).
 __device__ __forceinline__ void shard_emit(const ShardArgs& a, int row, const float* srow,
-                                           const unsigned long long* list, bool ties) {
+                                           const unsigned long long* list, bool ties, bool temper, float T) {
   const int t = threadIdx.x;
   if (t < SHARD_CAND) {
     const unsigned long long k = list[t];
@@ -78,7 +80,7 @@ __device__ __forceinline__ void shard_emit(const ShardArgs& a, int row, const fl
     unsigned gi = (unsigned)(a.voff + li);
     if (t == SHARD_CAND - 1 && ties) gi |= CAND_TIES;
     c4s_candidate c;
-    c.value = srow[li];
+    c.value = temper ? __fdiv_rn(srow[li], T) : srow[li];
     c.index = (int)gi;
     a.cand[(long long)row * SHARD_CAND + t] = c;
   }
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
     } else {
       for (int i = tid; i < Vs; i += NT) srow[i] = __ldg(g + i);
     }
+    if (tid < ((4 - (Vs & 3)) & 3)) srow[Vs + tid] = -INFINITY;
     // 2. repetition penalty over the history ids inside this shard
     const bool pen = P.repetition_penalty != 1.0f && a.hist_off != nullptr;
     long long h0 = 0, h1 = 0;
@@ -138,22 +141,22 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
       }
       __syncthreads();
     }
-    // 3. temperature (sampled rows) and each thread's largest key
+    // 3. each thread's largest penalised value (16-byte passes over the row;
+    //    the buffer's padding to a multiple of 4 holds -inf)
     const bool temper = !P.greedy && !(P.temperature == 1.0f || P.temperature <= 0.0f);
     const float T = P.temperature;
-    const float rT = __frcp_rn(T);
-    unsigned tmax = 0u;
-    for (int i = tid; i < Vs; i += NT) {
-      float v = srow[i];
-      if (temper) {
-        v = div_rn(v, T, rT);
-        srow[i] = v;
-      }
-      tmax = max(tmax, fkey(v));
+    const int nv = (Vs + 3) >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(srow);
+    float tm = -INFINITY;
+    for (int i = tid; i < nv; i += NT) {
+      const float4 v = s4[i];
+      tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
     }
-    // 4. a lower bound on the 64th largest key: in every warp 8 lanes hold an
+    const unsigned tmax = fkey(tm);
+    // 4. a lower bound on the 64th largest value: in every warp 8 lanes hold an
     //    element at least as large as the warp's 8th-largest lane maximum, so
-    //    at least 64 elements are >= the least of the 8 warps' values.
+    //    at least 64 elements are >= the least of the 8 warps' values. Lanes
+    //    without elements hold -inf, which makes the bound -inf (every element).
     int rank = 0;
     for (int s = 0; s < 32; ++s) {
       const unsigned o = __shfl_sync(FULL, tmax, s);
@@ -166,30 +169,63 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
     unsigned tau0 = s_wk[0];
 #pragma unroll
     for (int w = 1; w < NWARP; ++w) tau0 = min(tau0, s_wk[w]);
-    // 5. every element >= the bound into the list (any order)
-    for (int i0 = 0; i0 < Vs; i0 += NT) {
-      const int i = i0 + tid;
-      const unsigned k = i < Vs ? fkey(srow[i]) : 0u;
-      const bool take = i < Vs && k >= tau0;
-      const unsigned m = __ballot_sync(FULL, take);
-      int base = 0;
-      if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
-      base = __shfl_sync(FULL, base, 0);
-      if (take) {
-        const int pos = base + __popc(m & ((1u << lane) - 1u));
-        if (pos < SHARD_LIST) list[pos] = ((unsigned long long)(~k) << 32) | (unsigned)i;
+    const float t0f = fkey_inv(tau0);
+    // 5. every element >= the bound into the list (any order), keyed by its
+    //    tempered value: ~fkey(value) << 32 | local index, ascending = largest
+    //    value first, ties by index. Temperature is monotone, so the list holds
+    //    the 64 largest tempered values unless an element below the bound
+    //    tempers to the list's 64th value (checked below).
+    for (int i = tid; i < nv; i += NT) {
+      const float4 v = s4[i];
+      if (fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)) >= t0f) {
+        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int idx = 4 * i + c;
+          if (idx < Vs && e[c] >= t0f) {
+            const float tv = temper ? __fdiv_rn(e[c], T) : e[c];
+            const int pos = atomicAdd(&s_cnt, 1);
+            if (pos < SHARD_LIST) list[pos] = ((unsigned long long)(~fkey(tv)) << 32) | (unsigned)idx;
+          }
+        }
       }
     }
     __syncthreads();
     const int n0 = s_cnt;
-    if (n0 >= SHARD_CAND && n0 <= SHARD_LIST) {
-      const int n2 = next_pow2(n0);
-      for (int i = n0 + tid; i < n2; i += NT) list[i] = KEY_MAX;
-      __syncthreads();
-      bitonic_sort_u64(list, n2);
+    bool fast = n0 >= SHARD_CAND && n0 <= SHARD_LIST;
+    if (fast) {
+      if (n0 <= NT) {
+        // rank sort (keys are distinct): the 65 smallest keys into list[0..64]
+        unsigned long long kt = 0ull;
+        int r = SHARD_LIST;
+        if (tid < n0) {
+          kt = list[tid];
+          r = 0;
+          for (int j = 0; j < n0; ++j) r += list[j] < kt;
+        }
+        __syncthreads();
+        if (r <= SHARD_CAND) list[r] = kt;
+        __syncthreads();
+      } else {
+        const int n2 = next_pow2(n0);
+        for (int i = n0 + tid; i < n2; i += NT) list[i] = KEY_MAX;
+        __syncthreads();
+        bitonic_sort_u64(list, n2);
+      }
+      if (temper) {
+        // every element below the bound tempers to at most RN(prev(bound) / T)
+        const float t64 = fkey_inv(~(unsigned)(list[SHARD_CAND - 1] >> 32));
+        fast = t64 > __fdiv_rn(nextafterf(t0f, -INFINITY), T);
+      }
+    }
+    if (fast) {
       const bool ties = n0 > SHARD_CAND && (list[SHARD_CAND] >> 32) == (list[SHARD_CAND - 1] >> 32);
-      shard_emit(a, row, srow, list, ties);
+      shard_emit(a, row, srow, list, ties, temper, T);
     } else {
+      if (temper) {
+        for (int i = tid; i < Vs; i += NT) srow[i] = __fdiv_rn(srow[i], T);
+        __syncthreads();
+      }
       // Rare (many equal values near the top): exact 64th largest key by a
       // byte-wise radix select, then the larger elements and the first
       // equal ones in index order.
@@ -261,46 +297,51 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         __syncthreads();
       }
       bitonic_sort_u64(list, SHARD_CAND);
-      shard_emit(a, row, srow, list, eq_before > want);
+      shard_emit(a, row, srow, list, eq_before > want, false, T);
     }
     __syncthreads();
   }
 }
 
 __global__ void __launch_bounds__(NT) merge_kernel(MergeArgs a) {
-  __shared__ unsigned long long key[SHARD_CAND * MAX_SHARDS];  // ascending (value, global index)
-  __shared__ double pr[SHARD_CAND * MAX_SHARDS];
-  __shared__ int ord[SHARD_CAND * MAX_SHARDS];
+  constexpr int NC = SHARD_CAND * MAX_SHARDS;
+  __shared__ unsigned long long dk[NC];  // (~fkey(value) << 32) | index: each shard's block ascending
+  __shared__ float val[NC];
+  __shared__ double pr[NC];
+  __shared__ int sv[NC];                 // survivors by descending (value), ascending index
+  __shared__ int ord[NC];                // survivors in ascending (value, index) order
   __shared__ unsigned s_tiekey[MAX_SHARDS];
   __shared__ unsigned long long s_red[NWARP];
-  __shared__ int s_first, s_keep, s_bad;
+  __shared__ unsigned s_tk;
+  __shared__ int s_m, s_keep, s_bad;
+  __shared__ double s_sum;
   const int tid = threadIdx.x;
-  const int n = a.G * SHARD_CAND;
-  const int n2 = next_pow2(n);
+  const int G = a.G;
+  const int n = G * SHARD_CAND;
   for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
     if (a.active && !a.active[row]) {
       if (tid == 0) a.out_ids[row] = -1;
       continue;
     }
     const c4s_row_params P = a.params[(long long)row * a.params_stride];
-    unsigned long long best = 0ull;
-    for (int j = tid; j < n2; j += NT) {
-      unsigned long long k = 0ull;  // padding sorts first
-      if (j < n) {
-        const int s = j / SHARD_CAND, q = j % SHARD_CAND;
-        const c4s_candidate c = a.cand[(long long)s * a.shard_stride + (long long)row * SHARD_CAND + q];
-        const unsigned gi = (unsigned)c.index & ~CAND_TIES;
-        k = ckey(c.value, (int)gi);
-        if (q == SHARD_CAND - 1) s_tiekey[s] = ((unsigned)c.index & CAND_TIES) ? fkey(c.value) : 0u;
-        // greedy: largest value, then smallest index
-        const unsigned long long gk = ((unsigned long long)fkey(c.value) << 32) | (0xffffffffu - gi);
-        best = gk > best ? gk : best;
-      }
-      key[j] = k;
+    unsigned long long best = KEY_MAX;
+    for (int j = tid; j < n; j += NT) {
+      const int s = j / SHARD_CAND, q = j % SHARD_CAND;
+      const c4s_candidate c = a.cand[(long long)s * a.shard_stride + (long long)row * SHARD_CAND + q];
+      const unsigned gi = (unsigned)c.index & ~CAND_TIES;
+      const unsigned long long d = ((unsigned long long)(~fkey(c.value)) << 32) | gi;
+      dk[j] = d;
+      val[j] = c.value;
+      if (q == SHARD_CAND - 1) s_tiekey[s] = ((unsigned)c.index & CAND_TIES) ? fkey(c.value) : 0u;
+      best = d < best ? d : best;
     }
-    if (P.greedy) {
-      best = block_reduce(best, MaxU64{}, s_red);
-      if (tid == 0) a.out_ids[row] = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+    if (tid == 0) {
+      s_m = 0;
+      s_bad = 0;
+    }
+    if (P.greedy) {  // largest value, then smallest index (sampling.cpp:73-76)
+      best = block_reduce(best, MinU64{}, s_red);
+      if (tid == 0) a.out_ids[row] = (int)(unsigned)(best & 0xffffffffull);
       __syncthreads();
       continue;
     }
@@ -314,15 +355,41 @@ __global__ void __launch_bounds__(NT) merge_kernel(MergeArgs a) {
       continue;
     }
     __syncthreads();
-    bitonic_sort_u64(key, n2);
-    // top_k: threshold = k-th largest; survivors = every candidate >= it
-    const unsigned tk = (unsigned)(key[n2 - k] >> 32);
-    if (tid == 0) s_bad = 0;
-    for (int j = n2 - n + tid; j <= n2 - k; j += NT) {
-      if ((unsigned)(key[j] >> 32) >= tk && (j == n2 - n || (unsigned)(key[j - 1] >> 32) < tk)) s_first = j;
+    // rank of every candidate in descending (value) / ascending index order:
+    // binary searches in the shards' sorted blocks
+    int myr[NC / NT];
+#pragma unroll
+    for (int t = 0; t < NC / NT; ++t) {
+      const int j = tid + t * NT;
+      myr[t] = -1;
+      if (j < n) {
+        const unsigned long long K = dk[j];
+        int r = 0;
+        for (int s = 0; s < G; ++s) {
+          const unsigned long long* blk = dk + s * SHARD_CAND;
+          int lo = 0, hi = SHARD_CAND;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (blk[mid] < K) lo = mid + 1;
+            else hi = mid;
+          }
+          r += lo;
+        }
+        myr[t] = r;
+        if (r == k - 1) s_tk = fkey(val[j]);  // top_k threshold: the k-th largest value
+      }
     }
     csync();
-    if (tid < a.G && s_tiekey[tid] != 0u && s_tiekey[tid] == tk) s_bad = 1;
+    const unsigned tk = s_tk;
+#pragma unroll
+    for (int t = 0; t < NC / NT; ++t) {
+      const int j = tid + t * NT;
+      if (j < n && fkey(val[j]) >= tk) {
+        sv[myr[t]] = j;
+        atomicAdd(&s_m, 1);
+      }
+    }
+    if (tid < G && s_tiekey[tid] != 0u && s_tiekey[tid] == tk) s_bad = 1;
     csync();
     if (s_bad) {
       if (tid == 0) {
@@ -332,59 +399,75 @@ __global__ void __launch_bounds__(NT) merge_kernel(MergeArgs a) {
       __syncthreads();
       continue;
     }
-    const int first = s_first;
-    // top_p over the survivors in ascending (value, index) order
-    const float maxv = fkey_inv((unsigned)(key[n2 - 1] >> 32));
-    for (int j = first + tid; j < n2; j += NT) pr[j] = prob(fkey_inv((unsigned)(key[j] >> 32)), maxv);
+    const int m = s_m;  // survivors of top_k: descending ranks [0, m)
+    // ascending (value, index) order: the reverse, with equal values kept in index order
+    const float maxv = val[sv[0]];
+    for (int r = tid; r < m; r += NT) {
+      const int j = sv[r];
+      const unsigned f = fkey(val[j]);
+      int r0 = r, r1 = r;
+      while (r0 > 0 && fkey(val[sv[r0 - 1]]) == f) --r0;
+      while (r1 < m - 1 && fkey(val[sv[r1 + 1]]) == f) ++r1;
+      const int pos = (m - 1 - r1) + (r - r0);
+      ord[pos] = j;
+      pr[pos] = prob(val[j], maxv);
+    }
     csync();
+    // top_p (sampling.cpp:54-68): the sum and the running sum in ascending order
     if (tid == 0) {
       double sum = 0.0;
-      for (int j = first; j < n2; ++j) sum += pr[j];
+      for (int r = 0; r < m; ++r) sum += pr[r];
+      s_sum = sum;
+    }
+    csync();
+    const double sum = s_sum;
+    for (int r = tid; r < m; r += NT) pr[r] = pr[r] / sum;
+    csync();
+    if (tid == 0) {
       const double thr = 1.0 - (double)P.top_p;
       double cum = 0.0;
       int nrem = 0;
-      for (int j = first; j < n2; ++j) {
-        cum += pr[j] / sum;
+      for (int r = 0; r < m; ++r) {
+        cum += pr[r];
         if (cum <= thr) ++nrem;
         else break;
       }
-      int keep = first + nrem;
       const int mk = P.min_tokens_to_keep;
-      if (mk > 0) keep = max(first, min(keep, n2 - mk));
-      s_keep = keep;
+      if (mk > 0) nrem = max(0, min(nrem, m - mk));
+      s_keep = nrem;
     }
     csync();
     const int keep = s_keep;
-    const int nk = n2 - keep;
-    // the draw, in index order over the kept candidates
-    const float mv = fmaxf(-1e30f, fkey_inv((unsigned)(key[n2 - 1] >> 32)));
-    for (int j = keep + tid; j < n2; j += NT) {
-      const unsigned gi = (unsigned)(key[j] & 0xffffffffull);
+    const int nk = m - keep;
+    // the draw (text2semantic.cpp:150-165), in index order over the kept candidates
+    const float mv = nk > 0 ? fmaxf(-1e30f, val[ord[m - 1]]) : -1e30f;
+    for (int p = keep + tid; p < m; p += NT) {
+      const int j = ord[p];
+      const unsigned gi = (unsigned)(dk[j] & 0xffffffffull);
       int r = 0;
-      for (int l = keep; l < n2; ++l) r += (unsigned)(key[l] & 0xffffffffull) < gi;
-      ord[r] = j;
-      pr[j] = prob(fkey_inv((unsigned)(key[j] >> 32)), mv);
+      for (int l = keep; l < m; ++l) r += (unsigned)(dk[ord[l]] & 0xffffffffull) < gi;
+      sv[r] = j;
+      pr[r] = prob(val[j], mv);
     }
     csync();
     if (tid == 0) {
-      double sum = 0.0;
-      for (int r = 0; r < nk; ++r) sum += pr[ord[r]];
+      double s2 = 0.0;
+      for (int r = 0; r < nk; ++r) s2 += pr[r];
       unsigned long long x = a.rng[row];
       x ^= x << 13;
       x ^= x >> 7;
       x ^= x << 17;
       a.rng[row] = x;
-      const double rr = (double)(x >> 11) / 9007199254740992.0 * sum;
+      const double rr = (double)(x >> 11) / 9007199254740992.0 * s2;
       int tok = a.Vtot - 1;
       if (nk == 0 || rr <= 0.0) {
         tok = 0;  // the reference's first index satisfies r <= acc
       } else {
         double acc = 0.0;
         for (int r = 0; r < nk; ++r) {
-          const int j = ord[r];
-          acc += pr[j];
+          acc += pr[r];
           if (rr <= acc) {
-            tok = (int)(unsigned)(key[j] & 0xffffffffull);
+            tok = (int)(unsigned)(dk[sv[r]] & 0xffffffffull);
             break;
           }
         }
