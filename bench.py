@@ -503,14 +503,15 @@ def run_vocab_sharded(args):
     # the shard kernel alone (the only kernel that reads the logits), same inputs
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     shard_ms = 0.0
-    nshard = G if world == 1 else 1
+    nshard = G if world == 1 else 1      # shards the one shard-kernel launch works
     for s in range(args.steps):
         p = pool[s % npool]
         ev[0].record(stream)
-        for g in range(nshard):
-            o, w = c4s.vocab_shard.shard_vocab(V, g, G) if world == 1 else (voff, width)
-            ctx.shard_candidates(p["logits"][:, o - (0 if world == 1 else voff):], V, o, p["hist"],
-                                 p["hist_off"], p["params"], out=cand[g if world == 1 else rank], V_shard=w)
+        if world == 1:
+            ctx.shard_candidates_split(p["logits"], G, p["hist"], p["hist_off"], p["params"], out=cand, V=V)
+        else:
+            ctx.shard_candidates(p["logits"], V, voff, p["hist"], p["hist_off"], p["params"], out=cand[rank],
+                                 V_shard=width)
         ev[1].record(stream)
         torch.cuda.synchronize()
         shard_ms += ev[0].elapsed_time(ev[1])
@@ -533,9 +534,9 @@ def run_vocab_sharded(args):
                        "l2": f"pool of {npool} batches rotated (inputs > 2x L2)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None, "kernel": "shard_kernel",
-                         "peak_kind": peak_kind, "alg_bytes_per_launch": alg / nshard},
+                         "peak_kind": peak_kind, "alg_bytes_per_launch": alg},
             "shard_kernel_ms_per_step": shard_ms,
-            "gpu_launches": (nshard + 1) * args.steps,
+            "gpu_launches": 2 * args.steps,
             "clocks": clocks, "device_errors": err,
         }
         print(json.dumps(line), flush=True)

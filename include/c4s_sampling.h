@@ -252,6 +252,23 @@ int c4s_shard_candidates(c4s_ctx* ctx, const float* d_logits, int32_t B,
                          const uint8_t* d_active, c4s_candidate* d_cand,
                          void* stream);
 
+/* Candidates of every shard of whole rows held by one GPU, in one launch:
+ * d_logits fp32 [B, ld] (ld >= V) holds whole rows; shard s is the column
+ * block starting at s*(V/G) + min(s, V%G), of width V/G (+1 for s < V%G),
+ * G = num_shards (1..C4S_MAX_SHARDS, every shard 64..32768 wide); shard s's
+ * [B][64] block is written at d_cand + s * shard_stride (>= B * 64), the
+ * layout c4s_merge_candidates reads. With c4s_merge_candidates this is the
+ * single-GPU form of the vocab-sharded step, and samples rows wider than
+ * c4s_sample's 32768 columns (for 1 <= top_k <= 64). Replaces the same
+ * per-row body of text2semantic.cpp:303-331 as c4s_sample.                 */
+int c4s_shard_candidates_split(c4s_ctx* ctx, const float* d_logits, int32_t B,
+                               int32_t V, int64_t ld, int32_t num_shards,
+                               const int32_t* d_hist, const int64_t* d_hist_off,
+                               int64_t hist_total, const c4s_row_params* d_params,
+                               int32_t params_stride, const uint8_t* d_active,
+                               c4s_candidate* d_cand, int64_t shard_stride,
+                               void* stream);
+
 /* Token ids from the candidates of `num_shards` shards (1..C4S_MAX_SHARDS),
  * shard s's block at d_cand + s * shard_stride (shard_stride >= B * 64, in
  * candidates: the layout of an all-gather of the [B][64] blocks, shards in

@@ -304,6 +304,22 @@ int check_common(c4s_ctx* ctx, int B, int V, long long ld) {
   return C4S_OK;
 }
 
+// Shard kernel launch: persistent CTAs over (row, shard) items.
+int launch_shard(c4s_ctx* ctx, c4s::ShardArgs& a, void* stream) {
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  const size_t smem = c4s::shard_smem_bytes(a.Vs);
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, c4s::shard_kernel, c4s::NT, smem);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "shard_kernel occupancy");
+  const long long items = (long long)a.B * a.G;
+  const int grid = (int)std::min<long long>(items, (long long)std::max(occ, 1) * ctx->num_sms);
+  c4s::shard_kernel<<<grid, c4s::NT, smem, (cudaStream_t)stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "shard_kernel launch");
+  return C4S_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -592,16 +608,42 @@ int c4s_shard_candidates(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t
   a.params = d_params; a.params_stride = params_stride;
   a.active = d_active;
   a.cand = d_cand;
+  a.G = 1;
+  a.cand_stride = 0;
   a.errflags = ctx->d_err;
-  const size_t smem = c4s::shard_smem_bytes(V_shard);
-  int occ = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, c4s::shard_kernel, c4s::NT, smem);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "shard_kernel occupancy");
-  const int grid = (int)std::min<long long>((long long)B, (long long)std::max(occ, 1) * ctx->num_sms);
-  c4s::shard_kernel<<<grid, c4s::NT, smem, (cudaStream_t)stream>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "shard_kernel launch");
-  return C4S_OK;
+  return launch_shard(ctx, a, stream);
+}
+
+int c4s_shard_candidates_split(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V, int64_t ld,
+                               int32_t num_shards, const int32_t* d_hist, const int64_t* d_hist_off,
+                               int64_t hist_total, const c4s_row_params* d_params, int32_t params_stride,
+                               const uint8_t* d_active, c4s_candidate* d_cand, int64_t shard_stride,
+                               void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (B < 0) return fail(ctx, C4S_ERR_INVALID, "B < 0");
+  if (num_shards < 1 || num_shards > c4s::MAX_SHARDS) return fail(ctx, C4S_ERR_INVALID, "num_shards outside [1, 16]");
+  if (V < 1 || V / num_shards < c4s::SHARD_CAND) return fail(ctx, C4S_ERR_INVALID, "a shard narrower than 64");
+  const int widest = V / num_shards + (V % num_shards ? 1 : 0);
+  if (widest > c4s::MAX_VOCAB) return fail(ctx, C4S_ERR_CAPACITY, "a shard wider than 32768");
+  if (ld < V) return fail(ctx, C4S_ERR_INVALID, "ld < V");
+  if (B == 0) return C4S_OK;
+  if (shard_stride < (int64_t)B * c4s::SHARD_CAND) return fail(ctx, C4S_ERR_INVALID, "shard_stride < B * 64");
+  if (!d_logits || !d_params || !d_cand) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if (params_stride != 0 && params_stride != 1) return fail(ctx, C4S_ERR_INVALID, "params_stride not 0/1");
+  if (d_hist_off && (!d_hist && hist_total > 0)) return fail(ctx, C4S_ERR_INVALID, "history ids missing");
+  if (hist_total < 0) return fail(ctx, C4S_ERR_INVALID, "hist_total < 0");
+  if (((uintptr_t)d_logits & 3) || ((uintptr_t)d_cand & 7)) return fail(ctx, C4S_ERR_INVALID, "misaligned pointer");
+  c4s::ShardArgs a{};
+  a.logits = d_logits;
+  a.B = B; a.Vs = widest; a.ld = ld; a.voff = 0; a.Vtot = V;
+  a.hist = d_hist; a.hist_off = reinterpret_cast<const long long*>(d_hist_off); a.hist_total = hist_total;
+  a.params = d_params; a.params_stride = params_stride;
+  a.active = d_active;
+  a.cand = d_cand;
+  a.G = num_shards;
+  a.cand_stride = shard_stride;
+  a.errflags = ctx->d_err;
+  return launch_shard(ctx, a, stream);
 }
 
 int c4s_merge_candidates(c4s_ctx* ctx, const c4s_candidate* d_cand, int32_t num_shards, int64_t shard_stride,

@@ -38,19 +38,30 @@ constexpr unsigned CAND_TIES = C4S_CAND_TIES;
 static_assert(SHARD_CAND * MAX_SHARDS % NT == 0, "merge ranks whole passes of the block");
 
 struct ShardArgs {
-  const float* logits;   // this shard's columns: row r at logits + r * ld
-  int B, Vs;             // rows, shard width
+  const float* logits;   // G == 1: this shard's columns, row r at logits + r * ld;
+                         // G > 1: whole rows, shard s at the columns shard_span(s)
+  int B, Vs;             // rows; shard width (G > 1: the widest shard)
   long long ld;
-  int voff, Vtot;        // global index of column 0, full vocabulary
+  int voff, Vtot;        // G == 1: global index of column 0; full vocabulary
+  int G;                 // shards worked by this launch (1, or all of a whole row)
+  long long cand_stride; // G > 1: candidates between the shards' blocks
   const int* hist;
   const long long* hist_off;
   long long hist_total;
   const c4s_row_params* params;
   int params_stride;
   const unsigned char* active;
-  c4s_candidate* cand;   // [B][SHARD_CAND]
+  c4s_candidate* cand;   // [B][SHARD_CAND] (G > 1: [G][cand_stride])
   unsigned* errflags;
 };
+
+// Columns [off, off + width) of shard s when V columns are split into G
+// contiguous shards whose widths differ by at most one.
+__host__ __device__ inline void shard_span(int V, int G, int s, int& off, int& width) {
+  const int base = V / G, extra = V % G;
+  off = s * base + (s < extra ? s : extra);
+  width = base + (s < extra ? 1 : 0);
+}
 
 struct MergeArgs {
   const c4s_candidate* cand;  // shard s, row r: cand + s * shard_stride + r * SHARD_CAND
@@ -71,18 +82,18 @@ __host__ __device__ inline size_t shard_smem_bytes(int Vs) {
 // Writes the row's 64 candidates from an ascending list of keys
 // (~fkey(value) << 32 | local index): largest value first, ties by index.
 // `temper`: srow holds untempered values; the emitted value is RN(x / T).
-__device__ __forceinline__ void shard_emit(const ShardArgs& a, int row, const float* srow,
+__device__ __forceinline__ void shard_emit(c4s_candidate* out, int voff, const float* srow,
                                            const unsigned long long* list, bool ties, bool temper, float T) {
   const int t = threadIdx.x;
   if (t < SHARD_CAND) {
     const unsigned long long k = list[t];
     const int li = (int)(unsigned)(k & 0xffffffffull);
-    unsigned gi = (unsigned)(a.voff + li);
+    unsigned gi = (unsigned)(voff + li);
     if (t == SHARD_CAND - 1 && ties) gi |= CAND_TIES;
     c4s_candidate c;
     c.value = temper ? __fdiv_rn(srow[li], T) : srow[li];
     c.index = (int)gi;
-    a.cand[(long long)row * SHARD_CAND + t] = c;
+    out[t] = c;
   }
 }
 
@@ -90,21 +101,38 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned long long* list = reinterpret_cast<unsigned long long*>(smem);
   float* srow = reinterpret_cast<float*>(smem + (size_t)SHARD_LIST * 8);
-  unsigned* bitmap = reinterpret_cast<unsigned*>(srow + align_up((size_t)a.Vs, 4));
+  unsigned* bitmap = reinterpret_cast<unsigned*>(srow + align_up((size_t)a.Vs, 4));  // a.Vs: widest shard
   __shared__ unsigned s_wk[NWARP];
   __shared__ unsigned s_hist[256];
   __shared__ int s_cnt, s_digit, s_want;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int Vs = a.Vs;
-  for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+  const long long items = (long long)a.B * a.G;
+  for (long long item = blockIdx.x; item < items; item += gridDim.x) {
+    const int row = (int)(item / a.G), sh = (int)(item % a.G);
     if (a.active && !a.active[row]) continue;
+    int voff = a.voff, Vs = a.Vs;
+    if (a.G > 1) shard_span(a.Vtot, a.G, sh, voff, Vs);
+    c4s_candidate* out = a.cand + (long long)sh * a.cand_stride + (long long)row * SHARD_CAND;
     const c4s_row_params P = a.params[(long long)row * a.params_stride];
-    const float* g = a.logits + (long long)row * a.ld;
+    const float* g = a.logits + (long long)row * a.ld + (a.G > 1 ? voff : 0);
     // 1. stage the shard's row (16-byte loads when the row is aligned)
     if ((((uintptr_t)g) & 15) == 0) {
       const float4* g4 = reinterpret_cast<const float4*>(g);
       float4* s4 = reinterpret_cast<float4*>(srow);
-      for (int i = tid; i < Vs / 4; i += NT) s4[i] = __ldg(g4 + i);
+      const int n4 = Vs >> 2;
+      for (int i0 = 0; i0 < n4; i0 += 8 * NT) {  // eight 16-byte loads in flight per thread
+        float4 r[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int i = i0 + q * NT + tid;
+          if (i < n4) r[q] = __ldg(g4 + i);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int i = i0 + q * NT + tid;
+          if (i < n4) s4[i] = r[q];
+        }
+      }
       for (int i = (Vs & ~3) + tid; i < Vs; i += NT) srow[i] = __ldg(g + i);
     } else {
       for (int i = tid; i < Vs; i += NT) srow[i] = __ldg(g + i);
@@ -129,7 +157,7 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
       const float rpv = __frcp_rn(pv);
       for (long long j = h0 + tid; j < h1; j += NT) {
         const int t = a.hist[j];
-        const unsigned u = (unsigned)t - (unsigned)a.voff;
+        const unsigned u = (unsigned)t - (unsigned)voff;
         if (t >= 0 && u < (unsigned)Vs) {
           const unsigned bit = 1u << (u & 31);
           const unsigned old = atomicOr(&bitmap[u >> 5], bit);
@@ -220,7 +248,7 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
     }
     if (fast) {
       const bool ties = n0 > SHARD_CAND && (list[SHARD_CAND] >> 32) == (list[SHARD_CAND - 1] >> 32);
-      shard_emit(a, row, srow, list, ties, temper, T);
+      shard_emit(out, voff, srow, list, ties, temper, T);
     } else {
       if (temper) {
         for (int i = tid; i < Vs; i += NT) srow[i] = __fdiv_rn(srow[i], T);
@@ -297,7 +325,7 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         __syncthreads();
       }
       bitonic_sort_u64(list, SHARD_CAND);
-      shard_emit(a, row, srow, list, eq_before > want, false, T);
+      shard_emit(out, voff, srow, list, eq_before > want, false, T);
     }
     __syncthreads();
   }

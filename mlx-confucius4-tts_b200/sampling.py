@@ -86,6 +86,8 @@ def library() -> C.CDLL:
                 "c4s_kernel_times": ([vp, vp, vp, i32], C.c_int),
                 "c4s_shard_candidates": ([vp, vp, i32, i32, i64, i32, i32, vp, vp, i64, vp, i32, vp, vp,
                                           vp], C.c_int),
+                "c4s_shard_candidates_split": ([vp, vp, i32, i32, i64, i32, vp, vp, i64, vp, i32, vp, vp,
+                                                i64, vp], C.c_int),
                 "c4s_merge_candidates": ([vp, vp, i32, i64, i32, i32, vp, i32, vp, vp, vp, vp], C.c_int),
             }
             for name, (args, res) in sig.items():
@@ -257,6 +259,23 @@ class SamplingContext:
             _dptr(hist_off), total, _dptr(params), params_stride, _dptr(active), _dptr(out),
             self._stream(stream))
         self._check(rc, "c4s_shard_candidates")
+        return out
+
+    def shard_candidates_split(self, logits, num_shards: int, hist, hist_off, params, active=None,
+                               out=None, V: int | None = None, params_stride: int = 1, stream=None):
+        """Candidates of all ``num_shards`` shards of whole rows ``logits``
+        [B, ld] in one launch, into ``out`` int64 [G, B, 64] (the gathered layout)."""
+        torch = _torch()
+        B, ld = logits.shape
+        V = ld if V is None else V
+        if out is None:
+            out = torch.empty((num_shards, B, SHARD_CANDIDATES), dtype=torch.int64, device=logits.device)
+        total = 0 if hist is None else hist.numel()
+        rc = self.lib.c4s_shard_candidates_split(
+            self._h, _dptr(logits), B, V, logits.stride(0), num_shards, _dptr(hist), _dptr(hist_off),
+            total, _dptr(params), params_stride, _dptr(active), _dptr(out), out.stride(0),
+            self._stream(stream))
+        self._check(rc, "c4s_shard_candidates_split")
         return out
 
     def merge_candidates(self, cand, V: int, params, rng, active=None, out_ids=None,

@@ -54,7 +54,9 @@ def sample_vocab_split(ctx, logits, num_shards: int, hist, hist_off, params, rng
                        out_ids=None, params_stride: int = 1, cand_out=None, V: int | None = None):
     """The same step with all shards on one GPU: ``logits`` [B, ld] holds whole
     rows; shard s is the column block ``shard_vocab(V, s, num_shards)``, and
-    the candidate blocks land directly in the gathered layout [G, B, 64]."""
+    one launch writes the candidate blocks straight into the gathered layout
+    [G, B, 64]. Also the way to sample rows wider than ``SamplingContext.sample``
+    takes (32768) on one GPU, for 1 <= top_k <= 64."""
     import torch
 
     B, ld = logits.shape
@@ -62,9 +64,7 @@ def sample_vocab_split(ctx, logits, num_shards: int, hist, hist_off, params, rng
     if cand_out is None:
         cand_out = torch.empty((num_shards, B, SHARD_CANDIDATES), dtype=torch.int64,
                                device=logits.device)
-    for s in range(num_shards):
-        voff, width = shard_vocab(V, s, num_shards)
-        ctx.shard_candidates(logits[:, voff:], V, voff, hist, hist_off, params, active=active,
-                             out=cand_out[s], V_shard=width, params_stride=params_stride)
+    ctx.shard_candidates_split(logits, num_shards, hist, hist_off, params, active=active,
+                               out=cand_out, V=V, params_stride=params_stride)
     return ctx.merge_candidates(cand_out, V, params, rng, active=active, out_ids=out_ids,
                                 params_stride=params_stride)

@@ -404,3 +404,23 @@ def test_nccl_two_ranks_match_whole_rows(oracle):
             assert err == 0
             assert np.array_equal(ids[step], oid)
             assert np.array_equal(st[step], ro)
+
+
+@pytest.mark.gpu
+def test_split_launch_matches_per_shard_calls(sctx):
+    """The one-launch form (all shards of whole rows) writes the same
+    candidate blocks as one c4s_shard_candidates call per shard."""
+    import torch
+    c4s = load_c4s()
+    b = c4s.workloads.config4(seed=5, B=96, V=20011)
+    b.params["greedy"][::9] = 1
+    d = to_dev(b, torch)
+    G = 6
+    split = sctx.shard_candidates_split(d["logits"], G, d["hist"], d["hist_off"], d["params"], V=b.V)
+    per = torch.empty_like(split)
+    for s in range(G):
+        voff, width = c4s.vocab_shard.shard_vocab(b.V, s, G)
+        sctx.shard_candidates(d["logits"][:, voff:], b.V, voff, d["hist"], d["hist_off"], d["params"],
+                              out=per[s], V_shard=width)
+    torch.cuda.synchronize()
+    assert torch.equal(split, per)
