@@ -229,7 +229,13 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         if (tid < n0) {
           kt = list[tid];
           r = 0;
-          for (int j = 0; j < n0; ++j) r += list[j] < kt;
+          const ulonglong2* l2 = reinterpret_cast<const ulonglong2*>(list);  // two keys per load
+#pragma unroll 4
+          for (int j = 0; j < (n0 >> 1); ++j) {
+            const ulonglong2 kk = l2[j];
+            r += (kk.x < kt) + (kk.y < kt);
+          }
+          if (n0 & 1) r += list[n0 - 1] < kt;
         }
         __syncthreads();
         if (r <= SHARD_CAND) list[r] = kt;
