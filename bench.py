@@ -485,7 +485,15 @@ def run_vocab_sharded(args):
     for s in range(max(3, args.warmup)):
         step(s)
     torch.cuda.synchronize()
+    # clocks under sustained load: ~2 s of back-to-back steps, then the timed region
     clk = ClockSampler(phys_index(local))
+    t_end = time.time() + 2.0
+    s = 0
+    while time.time() < t_end:
+        for _ in range(50):
+            step(s)
+            s += 1
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -520,6 +528,14 @@ def run_vocab_sharded(args):
     alg = B * width * 4 + nshard * (4 * H + B * (8 + 24)) + nshard * B * 64 * 8
     achieved = alg / (shard_ms / 1e3) / 1e9
     hbm_peak, peak_kind = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the reference's CPU path on whole 65536-wide rows of the same workload
+        v, kind, threads, nrows = cpu_reference_rows_per_s(c4s, args.cpu_seconds,
+                                                           batch=wl.config4(seed=4, B=B, V=V))
+        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{nrows} whole rows of the config-4 batch (V=65536, wrapping), "
+                         f"OpenMP over rows, {threads} host threads, ~{args.cpu_seconds:.0f} s"}
     if rank == 0:
         line = {
             "metric": "sampled tokens/s (B=512, V=65536, vocab-sharded, config 4)",
@@ -536,6 +552,7 @@ def run_vocab_sharded(args):
                          "frac": achieved / hbm_peak, "traffic": None, "kernel": "shard_kernel",
                          "peak_kind": peak_kind, "alg_bytes_per_launch": alg},
             "shard_kernel_ms_per_step": shard_ms,
+            "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks, "device_errors": err,
         }
