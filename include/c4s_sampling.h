@@ -76,7 +76,13 @@ typedef struct c4s_row_params {
  * can check them on ordinary inputs.                                        */
 #define C4S_DEBUG_FORCE_EXACT 1 /* exact sequential sums; radix-select top-k   */
 #define C4S_DEBUG_FORCE_BINS 2  /* binned top-p and row-pass draw paths        */
-#define C4S_DEBUG_FORCE_REFINE 4 /* no-top-k list rows: exact tail in the general kernel */
+#define C4S_DEBUG_FORCE_REFINE 4 /* no-top-k list rows: exact tail before their list job decides */
+#define C4S_DEBUG_SPLIT_PATH 8   /* batches of up to 256 rows: sample through the split kernels
+                                    (row, list, general) instead of the fused kernel */
+#define C4S_DEBUG_FUSED_PATH 32  /* larger batches: sample through the fused kernel instead of the
+                                    split kernels */
+#define C4S_DEBUG_FAIL_AFTER_ROW 16 /* split path: fail the list-kernel launch on the host (no kernel
+                                    runs or faults), to test recovery of the next call */
 
 /* Device-side error bits reported by c4s_get_status().                     */
 #define C4S_DEVERR_HIST_RANGE 1u /* a row's history offsets were out of range */
@@ -124,7 +130,7 @@ int c4s_set_debug(c4s_ctx* ctx, int32_t flags);
 int c4s_seed_states(uint64_t* d_state, int32_t B, uint64_t seed,
                     int64_t row_offset, void* stream);
 
-/* One fused sampling step over B rows: for each active row b,
+/* One sampling step over B rows: for each active row b,
  *   repetition penalty over hist[hist_off[b] .. hist_off[b+1]),
  *   then greedy ? argmax : temperature, top_k, top_p, xorshift64 draw.
  * Replaces the per-row body of text2semantic.cpp:303-331 (and :142-165).
@@ -173,14 +179,15 @@ int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors,
 
 /* Measurement only; no counterpart in the reference. While enabled, every
  * c4s_sample call that takes the fast path records CUDA events on its stream
- * around its kernels (per chunk of 4096 rows): the order pre-pass (rows by
- * cost class; only when a chunk has more rows than the row kernel has CTAs
- * and per-row parameters), the row, list and general kernels.
+ * around its kernels: the fused kernel (one launch per call), or, on the
+ * split path (C4S_DEBUG_SPLIT_PATH), per chunk of 4096 rows the order
+ * pre-pass (rows by cost class; only when a chunk has more rows than the row
+ * kernel has CTAs and per-row parameters), the row, list and general kernels.
  * c4s_kernel_times waits for them and returns the summed device times in
- * milliseconds and the number of launches of each kernel in ms[4] /
- * launches[4], in that order; reset forgets the recorded calls. Not for use
- * while a stream is being captured.                                         */
-#define C4S_NUM_KERNEL_TIMERS 4
+ * milliseconds and the number of launches of each kernel in ms[5] /
+ * launches[5], in the order order, row, list, general, fused; reset forgets
+ * the recorded calls. Not for use while a stream is being captured.         */
+#define C4S_NUM_KERNEL_TIMERS 5
 int c4s_kernel_timing(c4s_ctx* ctx, int32_t enable);
 int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset);
 
@@ -200,13 +207,21 @@ int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset)
  *     different streams or threads) race and must be serialised by the caller.
  *   - The device error flags and path counters that the kernel writes are
  *     cleared (stream-ordered) at the start of every call; they are not
- *     reported: validate history offsets before calling.                    */
+ *     reported: validate history offsets before calling. A row whose bulk
+ *     copy was not seen to complete within the kernel's bounded wait (about
+ *     2 s) gets id -1, as do the later rows of its CTA.                     */
 #define C4S_STATIC_MAX_VOCAB 16384
 int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld,
                       const int32_t* d_hist, const int64_t* d_hist_off,
                       int64_t hist_total, const c4s_row_params* d_params,
                       int32_t params_stride, uint64_t* d_rng,
                       const uint8_t* d_active, int32_t* d_out_ids, void* stream);
+
+/* Test hook, no counterpart in the reference: d_out[i] = x[i] / d computed by
+ * the kernels' inline division (a Markstein-corrected reciprocal product with
+ * a proof check, else the IEEE division), so that tests can compare it bit
+ * for bit with IEEE round-to-nearest division (sampling.cpp:16, :26).      */
+int c4s_test_div_rn(const float* d_x, float d, float* d_out, int64_t n, void* stream);
 
 /* ------------------------------------------------------------------------
  * Vocab-sharded sampling: the vocabulary of every row is split into

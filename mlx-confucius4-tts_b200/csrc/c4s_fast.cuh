@@ -605,8 +605,10 @@ __device__ __forceinline__ bool step_to_crossing(const unsigned* __restrict__ vk
   return false;
 }
 
-// One list job. keys[0..n) (global): ckey(x, i) of the candidates' penalised,
-// untempered values in index order (list position = index order). The job
+// One list job. keys: the candidates' penalised, untempered value keys
+// (keys.val(e)) and indices (keys.idx(e)) in index order (list position =
+// index order), from a global ckey list (GlobalKeys) or from the staged row
+// (the fused kernel). The job
 // stages the keys of their tempered values y = fl(x/T) into vk[] and their
 // probabilities into pv[] (zero for candidates that top-k removes), both in
 // shared memory, so that its passes stay on chip; ykey(e) = ckey(y, i);
@@ -614,10 +616,18 @@ __device__ __forceinline__ bool step_to_crossing(const unsigned* __restrict__ vk
 // false) or by the whole CTA (long lists). With `refine` (the general kernel,
 // after replacing an estimated tail by the exact one) a row that cannot be
 // decided is not handed back: the caller finishes it on the general path.
+// With INL (the fused kernel) an undecided row is not queued either: J.status
+// says whether it needs an exact tail (RES_REFINE) or the general path.
 // Returns whether the row is finished.
-template <bool CTA>
-__device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
-                                         const unsigned long long* __restrict__ keys, unsigned long long* sb,
+// Candidate keys of a list in global memory: ckey(x, i) per position.
+struct GlobalKeys {
+  const unsigned long long* __restrict__ k;
+  __device__ __forceinline__ unsigned val(int e) const { return (unsigned)(__ldcg(k + e) >> 32); }
+  __device__ __forceinline__ unsigned idx(int e) const { return (unsigned)(k[e] & 0xffffffffull); }
+};
+
+template <bool CTA, bool INL = false, typename KS = GlobalKeys>
+__device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, const KS keys, unsigned long long* sb,
                                          unsigned* __restrict__ vk, double* __restrict__ pv,
                                          unsigned long long* __restrict__ hist, bool refine, LRed& R, int* rq) {
   using G = LG<CTA>;
@@ -630,6 +640,10 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
   // rq: the list kernel CTA's queue of rows that need an exact tail
   // (rq[0] = count, capacity RQ_CAP); elsewhere they go to the general kernel
   auto hand_back = [&](int st) {
+    if (INL) {                                      // the caller reads J.status and finishes the row
+      if (r0 == 0 && !refine) J.status = st;
+      return;
+    }
     if (r0 == 0 && !refine) {
       J.status = st;
       const int slot = (st == RES_REFINE && rq != nullptr) ? atomicAdd(&rq[0], 1) : RQ_CAP;
@@ -637,7 +651,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
       else defer_row(a, row);
     }
   };
-  auto ykey = [&](int e) { return ((unsigned long long)vk[e] << 32) | (keys[e] & 0xffffffffull); };
+  auto ykey = [&](int e) { return ((unsigned long long)vk[e] << 32) | keys.idx(e); };
   // stage the tempered value keys (sampling.cpp:16): eight loads in flight per member
   const float T = J.T;
   const bool do_t = T != 1.0f;
@@ -648,7 +662,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int e = e0 + q * GN;
-      v[q] = e < n ? (unsigned)(__ldcg(keys + e) >> 32) : 0u;
+      v[q] = e < n ? keys.val(e) : 0u;
     }
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -717,13 +731,17 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     for (int e = r0; e < n; e += GN)
       if (vk[e] >= tk && pv[e] > 0.0) mk0 = ykey(e) < mk0 ? ykey(e) : mk0;
     kst = G::qmin(mk0, R);
-  } else if (!CTA && ns <= 128) {
-    // few survivors: sort them in registers and find the crossing on a prefix scan
+  } else if (!CTA && (ns <= 128 || (ns <= 256 && (INL || n <= LW_CAP / 2)))) {
+    // few survivors: sort them in registers and find the crossing on a prefix
+    // scan; 256 keys need 2 KB: the fused kernel's histogram area, or the list
+    // kernel's unused upper half of the probability area
     const double Th = thr * St;
     int pos = 0;
     double before = 0.0, cur = 0.0;
-    const bool hit = ns <= 64 ? warp_sorted_crossing<2>(vk, pv, n, tk, ns, tail, Th, hist, &pos, &before, &cur)
-                              : warp_sorted_crossing<4>(vk, pv, n, tk, ns, tail, Th, hist, &pos, &before, &cur);
+    unsigned long long* cbuf = (INL || ns <= 128) ? hist : reinterpret_cast<unsigned long long*>(pv + LW_CAP / 2);
+    const bool hit = ns <= 64    ? warp_sorted_crossing<2>(vk, pv, n, tk, ns, tail, Th, cbuf, &pos, &before, &cur)
+                     : ns <= 128 ? warp_sorted_crossing<4>(vk, pv, n, tk, ns, tail, Th, cbuf, &pos, &before, &cur)
+                                 : warp_sorted_crossing<8>(vk, pv, n, tk, ns, tail, Th, cbuf, &pos, &before, &cur);
     if (hit) {
       const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
       kst = ykey(pos);
@@ -896,7 +914,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
     }
     const double bd2 = 2.0 * ((4.0 * nk + 16.0) * U53 * s2);
     if (!forced && found >= 0 && prev < r - bd2 && cur > r + bd2) {
-      tok = ckey_idx(keys[found]);
+      tok = (int)keys.idx(found);
     } else {
       // the reference's sequential sums in index order
       int t = V - 1;
@@ -909,7 +927,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J,
         for (int e = 0; e < n; ++e) {
           if (kept(e)) {
             acc = __dadd_rn(acc, pv[e]);
-            if (rr <= acc) { t = ckey_idx(keys[e]); break; }
+            if (rr <= acc) { t = (int)keys.idx(e); break; }
           }
         }
         atomicAdd(&a.counters[C4S_CNT_DRAW_EXACT_FALLBACK], 1ull);
@@ -1072,7 +1090,7 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
   }
   csync();                                          // the row buffer is free again
   const size_t o = (size_t)row * LCAP;
-  if (!list_job<true>(a, row, J, a.lkeys + o, a.lsb + o, vk, pv, hist, true, R, nullptr) && tid == 0) {
+  if (!list_job<true>(a, row, J, GlobalKeys{a.lkeys + o}, a.lsb + o, vk, pv, hist, true, R, nullptr) && tid == 0) {
     J.status = RES_DEFER;
     defer_row(a, row);
   }
@@ -1127,7 +1145,7 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
       if (t >= (int)nbig) return false;
       const int r = a.big_rows[t];
       const size_t o = (size_t)r * LCAP;
-      list_job<true>(a, r, a.jobs[r], a.lkeys + o, a.lsb + o, bvk, bpv, bh, false, R, rq);
+      list_job<true>(a, r, a.jobs[r], GlobalKeys{a.lkeys + o}, a.lsb + o, bvk, bpv, bh, false, R, rq);
     }
   };
   cta_work();
@@ -1150,7 +1168,7 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
       if (t >= nq) break;
       const int row = a.big_rows[(size_t)q * K_CHUNK + t];
       const size_t o = (size_t)row * LCAP;
-      list_job<false>(a, row, a.jobs[row], a.lkeys + o, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
+      list_job<false>(a, row, a.jobs[row], GlobalKeys{a.lkeys + o}, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
                       reinterpret_cast<double*>(wa + LW_PV), reinterpret_cast<unsigned long long*>(wa + LW_HIST),
                       false, R, rq);
     }
@@ -1202,6 +1220,82 @@ __device__ __forceinline__ unsigned warp_kth_largest32(unsigned key, int kw) {
     }
   }
   return __shfl_sync(FULL, key, 32 - kw);
+}
+
+// A tight lower bound tau on the k-th largest element of a row: at least k
+// elements are >= tau, and few more. U holds each thread's largest element
+// (and its second largest with `two`). The k-th largest value of U is
+// located in a 256-bin histogram of the key distances d = fkey(m_x) -
+// fkey(v) (bin 0: d = 0; then eight bins per octave of d), and tau is the
+// smallest value of that bin's key range, so every U value in the bins up to
+// it -- at least k of them -- is >= tau. Returns -inf if U holds fewer than k
+// finite values. `bins` is 256 words of shared memory, res one word; every
+// thread of the group (NTH threads, barrier `sync`) calls.
+__device__ __forceinline__ int ubin(unsigned d) {
+  if (d == 0u) return 0;
+  const int e = 31 - __clz(d);
+  const unsigned sub = e >= 3 ? (d >> (e - 3)) & 7u : (d << (3 - e)) & 7u;
+  return min(255, 1 + 8 * e + (int)sub);
+}
+template <int NTH, typename Sync>
+__device__ __forceinline__ float u_threshold(float tm, float t2, bool two, float m_x, int k, unsigned* bins,
+                                             unsigned* res, Sync sync) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 256; i += NTH) bins[i] = 0u;
+  sync();
+  const unsigned km = fkey(m_x);
+  if (tm > -INFINITY) atomicAdd(&bins[ubin(km - fkey(tm))], 1u);
+  if (two && t2 > -INFINITY) atomicAdd(&bins[ubin(km - fkey(t2))], 1u);
+  sync();
+  if (tid < 32) {
+    unsigned c[8], sl = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { c[j] = bins[8 * tid + j]; sl += c[j]; }
+    unsigned incl = sl;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(FULL, incl, o);
+      if (tid >= o) incl += y;
+    }
+    const unsigned hit = __ballot_sync(FULL, incl >= (unsigned)k);
+    unsigned tkey = fkey(-INFINITY);
+    if (hit) {
+      const int L = __ffs(hit) - 1;
+      int bs = 0;
+      if (tid == L) {
+        unsigned run = incl - sl;
+        bs = 8 * L + 7;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          run += c[j];
+          if (run >= (unsigned)k) { bs = 8 * L + j; break; }
+        }
+      }
+      bs = __shfl_sync(FULL, bs, L);
+      // the largest distance in bin bs (ubin is monotone in d); the last bin
+      // is open: every finite value
+      unsigned dmax;
+      if (bs == 0) {
+        dmax = 0u;
+      } else if (bs == 255) {
+        dmax = km - fkey(-3.4028234663852886e38f);
+      } else {
+        const int e = (bs - 1) >> 3, sub = (bs - 1) & 7;
+        if (e >= 3) {
+          dmax = (1u << e) + ((unsigned)(sub + 1) << (e - 3)) - 1u;
+        } else {
+          dmax = 1u;
+          for (unsigned d = 1u; d < 8u; ++d)
+            if (ubin(d) <= bs) dmax = d;
+        }
+      }
+      const unsigned lim = km - fkey(-3.4028234663852886e38f);   // tau stays finite
+      tkey = km - (dmax < lim ? dmax : lim);
+    }
+    if (tid == 0) *res = tkey;
+  }
+  sync();
+  return fkey_inv(*res);
 }
 
 // Header fields common to both list job kinds (thread 0).

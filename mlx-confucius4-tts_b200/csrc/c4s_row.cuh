@@ -181,15 +181,8 @@ __device__ __noinline__ int topk_body(const Args& a, int row, const RowCtx rc, c
   // a warp whose kw-th largest lane maximum (of the two largest per lane
   // when `two`) is finite has >= kw elements >= it, so >= k elements are >=
   // tau, the smallest over the warps (-inf: not enough elements; general path)
-  if (k > RWARP * (two ? 64 : 32)) return ROW_GENERAL;
-  const int kw = (k + RWARP - 1) / RWARP;
-  const unsigned wthr = two ? warp_kth_largest64(fkey(tm), fkey(t2), kw) : warp_kth_largest32(fkey(tm), kw);
-  if (lane == 0) S.redu[warp] = wthr;
-  rsync();
-  unsigned tkey = S.redu[0];
-#pragma unroll
-  for (int w = 1; w < RWARP; ++w) tkey = S.redu[w] < tkey ? S.redu[w] : tkey;
-  const float tau = fkey_inv(tkey);
+  if (k > RT * (two ? 2 : 1)) return ROW_GENERAL;
+  const float tau = u_threshold<RT>(tm, t2, two, rc.m_x, k, &S.hw[0][0][0], &S.redu[0], [] { rsync(); });
   // fl(x/T) merges x only with values at most |x| 2^-23 below it: lowering tau
   // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
   const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;

@@ -43,6 +43,7 @@
 #include "c4s_fast.cuh"
 #include "c4s_row.cuh"
 #include "c4s_shard.cuh"
+#include "c4s_fused.cuh"
 
 namespace c4s {
 
@@ -69,8 +70,20 @@ __global__ void __launch_bounds__(NT, 4) rows_kernel(Args a) {
       if (threadIdx.x == 0) a.out_ids[row] = -1;
       continue;
     }
-    if (!general_row(sa, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) return;
+    if (!general_row(sa, row, rowbuf, bitmap, cnt, mass, lkey, pv, S, phase)) {
+      // a bounded wait gave up (C4S_DEVERR_TIMEOUT): this CTA's remaining
+      // rows are marked as not sampled instead of keeping stale ids
+      if (a.mode != MODE_PROCESS && threadIdx.x == 0)
+        for (int r = row; r < a.B; r += gridDim.x) a.out_ids[r] = -1;
+      return;
+    }
   }
+}
+
+// div_rn over n dividends and one divisor (test hook of the exact division).
+__global__ void div_test_kernel(const float* x, float d, float* out, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = div_rn(x[i], d, __frcp_rn(d));
 }
 
 // Scratch of c4s_sample_static(), at file scope so that the entry point
@@ -107,6 +120,9 @@ struct c4s_ctx {
   c4s_row_params* d_default_params = nullptr;  // one zeroed struct (argmax reads no field)
   int row_occ = 0;                             // resident row-kernel CTAs per SM
   int list_occ = 0;                            // resident list-kernel CTAs per SM
+  int fused_occ = 0;                           // resident fused-kernel CTAs per SM
+  bool split_dirty = false;                    // a split-path launch sequence stopped early: its
+                                               // queue counters may be stale until cleared
   c4s::RowJob* d_jobs = nullptr;               // fast path: per-row jobs of one chunk
   unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
   unsigned long long* d_lsb = nullptr;
@@ -115,8 +131,9 @@ struct c4s_ctx {
   unsigned* d_defer_cnt = nullptr;
   int debug = 0;
   bool timing = false;                         // c4s_kernel_timing: events between fast-path launches
-  std::vector<cudaEvent_t> tev;                //   5 per recorded chunk (before order, after order/row/list/defer)
-  std::vector<unsigned char> tev_order;        //   per recorded chunk: the order pre-pass ran
+  std::vector<cudaEvent_t> tev;                //   TEV per recorded chunk: before the first kernel, then after
+                                               //   the order, row, list, general and fused kernels
+  std::vector<unsigned char> tev_mask;         //   per recorded chunk: bit k = kernel k ran
   size_t tev_used = 0;
   int cached_V = -1;
   int cached_occ = 0;
@@ -159,19 +176,22 @@ int occupancy(c4s_ctx* ctx, int V, size_t smem) {
   return occ;
 }
 
-// Four timing events for the next recorded chunk (nullptr if they cannot be made).
+// Timing events of the next recorded chunk (nullptr if they cannot be made):
+// ev[0] before its first kernel, ev[k + 1] after kernel k (order, row, list,
+// general, fused), recorded at once for kernels that do not run.
+constexpr int TEV = 1 + C4S_NUM_KERNEL_TIMERS;
 cudaEvent_t* timing_slot(c4s_ctx* ctx) {
-  if (ctx->tev_used + 5 > ctx->tev.size()) {
-    for (int i = 0; i < 5; ++i) {
+  if (ctx->tev_used + TEV > ctx->tev.size()) {
+    for (int i = 0; i < TEV; ++i) {
       cudaEvent_t e;
       if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
       ctx->tev.push_back(e);
     }
   }
   cudaEvent_t* ev = ctx->tev.data() + ctx->tev_used;
-  ctx->tev_used += 5;
-  ctx->tev_order.resize(ctx->tev_used / 5);
-  ctx->tev_order.back() = 0;
+  ctx->tev_used += TEV;
+  ctx->tev_mask.resize(ctx->tev_used / TEV);
+  ctx->tev_mask.back() = 0;
   return ev;
 }
 
@@ -208,9 +228,39 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
   while ((1 << lg) < a.V) ++lg;
   a.qscale = std::ldexp(1.0, 62 - std::max(lg, 1));
   cudaError_t e;
+  const cudaStream_t st0 = (cudaStream_t)stream;
+  const bool fused = a.B <= FUSED_MAX_ROWS ? !(ctx->debug & C4S_DEBUG_SPLIT_PATH) : (ctx->debug & C4S_DEBUG_FUSED_PATH) != 0;
+  if (a.mode == MODE_SAMPLE && a.V <= F_MAXV && fused) {
+    // fused path (small batches, or C4S_DEBUG_FUSED_PATH): one launch, every
+    // row finished in its CTA
+    a.defer_cnt = ctx->d_defer_cnt + FUSED_CNT;
+    const size_t smem = fused_smem_bytes(a.V);
+    if (ctx->fused_occ == 0) {
+      int occ = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fused_kernel, NT, fused_smem_bytes(F_MAXV)) !=
+              cudaSuccess || occ < 1)
+        return fail(ctx, C4S_ERR_CUDA, "fused kernel occupancy");
+      ctx->fused_occ = occ;
+    }
+    // every CTA uses two scratch slabs (blockIdx.x and grid + blockIdx.x)
+    const int grid = (int)std::min<long long>(std::min<long long>(a.B, (long long)ctx->fused_occ * ctx->num_sms),
+                                              (long long)ctx->scratch_ctas / 2);
+    cudaEvent_t* ev = ctx->timing ? timing_slot(ctx) : nullptr;
+    if (ev)
+      for (int k = 0; k < TEV - 1; ++k) cudaEventRecord(ev[k], st0);
+    e = launch_pdl(fused_kernel, grid, NT, smem, st0, a);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "fused kernel launch");
+    if (ev) {
+      cudaEventRecord(ev[TEV - 1], st0);
+      ctx->tev_mask.back() = 1u << 4;
+    }
+    return C4S_OK;
+  }
   if (a.mode == MODE_SAMPLE && a.V <= F_MAXV) {
-    // fast path, per chunk of K_CHUNK rows: row kernel -> list kernel -> general
-    // path for handed-back rows (-> masking of processed logits)
+    // split path (large batches, or C4S_DEBUG_SPLIT_PATH), per chunk of K_CHUNK
+    // rows: row kernel -> list kernel -> general path for handed-back rows (->
+    // masking of processed logits). Many list jobs run concurrently, one per
+    // warp, which hides their latency at large batch sizes.
     a.jobs = ctx->d_jobs;
     a.lkeys = ctx->d_lkeys;
     a.lsb = ctx->d_lsb;
@@ -229,6 +279,12 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     }
     const cudaStream_t st = (cudaStream_t)stream;
     const size_t gsm = layout_for(a.V).total;
+    if (ctx->split_dirty) {
+      // an earlier sequence stopped after its row kernel: clear its queue counters
+      e = cudaMemsetAsync(ctx->d_defer_cnt, 0, FUSED_CNT * sizeof(unsigned), st);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "clear queue counters");
+      ctx->split_dirty = false;
+    }
     for (int c0 = 0; c0 < a.B; c0 += K_CHUNK) {
       Args ac = a;
       ac.B = std::min(K_CHUNK, a.B - c0);
@@ -248,21 +304,30 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
         ac.order = ctx->d_order;
         e = launch_pdl(order_kernel, 1, ORDER_NT, 0, st, ac);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "order kernel launch");
-        if (ev) ctx->tev_order.back() = 1;
+        if (ev) ctx->tev_mask.back() |= 1u;
       }
       if (ev) cudaEventRecord(ev[1], st);
       e = launch_pdl(row_kernel, g1, RT, R_SMEM, st, ac);
       if (e != cudaSuccess) return cuda_fail(ctx, e, "row kernel launch");
+      // from here on the row kernel has taken queue tickets: a sequence that
+      // stops before the general kernel (which clears them) leaves them stale
+      ctx->split_dirty = true;
       if (ev) cudaEventRecord(ev[2], st);
       const int g2 = (int)std::min<long long>((ac.B + LIST_WARPS - 1) / LIST_WARPS,
                                                    (long long)ctx->list_occ * ctx->num_sms);
-      e = launch_pdl(list_kernel, g2, 32 * LIST_WARPS, LIST_SMEM, st, ac);
+      e = (ctx->debug & C4S_DEBUG_FAIL_AFTER_ROW) ? cudaErrorInvalidConfiguration
+                                                  : launch_pdl(list_kernel, g2, 32 * LIST_WARPS, LIST_SMEM, st, ac);
       if (e != cudaSuccess) return cuda_fail(ctx, e, "list kernel launch");
       if (ev) cudaEventRecord(ev[3], st);
       const int g3 = std::min(std::min(ac.B, ctx->num_sms), ctx->scratch_ctas);
       e = launch_pdl(defer_kernel, g3, NT, gsm, st, ac);
       if (e != cudaSuccess) return cuda_fail(ctx, e, "general kernel launch");
-      if (ev) cudaEventRecord(ev[4], st);
+      ctx->split_dirty = false;
+      if (ev) {
+        cudaEventRecord(ev[4], st);
+        cudaEventRecord(ev[5], st);
+        ctx->tev_mask.back() |= 2u | 4u | 8u;
+      }
       if (a.out_logits) mask_kernel<<<ac.B, NT, 0, st>>>(ac);
       e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(ctx, e, "fast path launch");
@@ -353,8 +418,9 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   if (prop.major != 10) { delete ctx; return C4S_ERR_CUDA; }  // built for sm_100a only
   ctx->num_sms = prop.multiProcessorCount;
-  // The attribute is per kernel (not per context): always allow the largest
-  // row any context may launch, so contexts of different sizes coexist.
+  // The attribute belongs to the kernel on the current device and is set on
+  // every create for the largest row any context may launch, so contexts of
+  // different sizes (and on different devices) coexist.
   const size_t smem_max = c4s::layout_for(c4s::MAX_VOCAB).total;
   e = cudaFuncSetAttribute(c4s::rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
   if (e == cudaSuccess)
@@ -364,6 +430,12 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::shard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c4s::shard_smem_bytes(c4s::MAX_VOCAB));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)c4s::fused_smem_bytes(c4s::F_MAXV));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::fused_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
   // the row kernel keeps five rows in flight per SM only with the largest
   // shared-memory carveout
   if (e == cudaSuccess)
@@ -375,9 +447,11 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e != cudaSuccess) { delete ctx; return C4S_ERR_CUDA; }
   int p2 = 1;
   while (p2 < max_vocab) p2 <<= 1;
-  ctx->scratch_stride = p2;
+  // one slab holds a sort of a whole row (general path, exact fallbacks) or
+  // the fused kernel's long candidate list
+  ctx->scratch_stride = std::max(p2, c4s::F_MIN_SCRATCH_STRIDE);
   ctx->scratch_ctas = ctx->num_sms * 8;
-  e = cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * p2 * sizeof(unsigned long long));
+  e = cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_counters, C4S_NUM_COUNTERS * sizeof(unsigned long long));
   const size_t nl = (size_t)c4s::K_CHUNK * c4s::LCAP;
@@ -386,8 +460,8 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (1 + c4s::LIST_CLASSES) * (size_t)c4s::K_CHUNK * sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_order, c4s::ROW_CLASSES * (size_t)c4s::K_CHUNK * sizeof(int));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, c4s::NCNT * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, c4s::NCNT * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, (c4s::FUSED_CNT + 2) * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, (c4s::FUSED_CNT + 2) * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_default_params, 0, sizeof(c4s_row_params));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(unsigned));
@@ -416,7 +490,9 @@ const char* c4s_last_error(const c4s_ctx* ctx) { return ctx ? ctx->last_error.c_
 
 int c4s_set_debug(c4s_ctx* ctx, int32_t flags) {
   if (!ctx) return C4S_ERR_INVALID;
-  if (flags & ~(C4S_DEBUG_FORCE_EXACT | C4S_DEBUG_FORCE_BINS | C4S_DEBUG_FORCE_REFINE)) return fail(ctx, C4S_ERR_INVALID, "unknown debug flag");
+  if (flags & ~(C4S_DEBUG_FORCE_EXACT | C4S_DEBUG_FORCE_BINS | C4S_DEBUG_FORCE_REFINE | C4S_DEBUG_SPLIT_PATH |
+                C4S_DEBUG_FAIL_AFTER_ROW | C4S_DEBUG_FUSED_PATH))
+    return fail(ctx, C4S_ERR_INVALID, "unknown debug flag");
   ctx->debug = flags;
   return C4S_OK;
 }
@@ -430,20 +506,22 @@ int c4s_kernel_timing(c4s_ctx* ctx, int32_t enable) {
 int c4s_kernel_times(c4s_ctx* ctx, double* ms, int64_t* launches, int32_t reset) {
   if (!ctx || !ms || !launches) return C4S_ERR_INVALID;
   DeviceGuard dg(ctx->device);
-  for (int k = 0; k < 4; ++k) { ms[k] = 0.0; launches[k] = 0; }
-  for (size_t c = 0; c + 5 <= ctx->tev_used; c += 5) {
-    for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < C4S_NUM_KERNEL_TIMERS; ++k) { ms[k] = 0.0; launches[k] = 0; }
+  for (size_t c = 0; c + TEV <= ctx->tev_used; c += TEV) {
+    const unsigned mask = ctx->tev_mask[c / TEV];
+    for (int k = 0; k < C4S_NUM_KERNEL_TIMERS; ++k) {
       if (cudaEventSynchronize(ctx->tev[c + k + 1]) != cudaSuccess) return fail(ctx, C4S_ERR_CUDA, "timing event");
+      if (!(mask & (1u << k))) continue;
       float t = 0.0f;
       if (cudaEventElapsedTime(&t, ctx->tev[c + k], ctx->tev[c + k + 1]) != cudaSuccess)
         return fail(ctx, C4S_ERR_CUDA, "timing event");
       ms[k] += t;
-      launches[k] += k > 0 ? 1 : ctx->tev_order[c / 5];
+      launches[k] += 1;
     }
   }
   if (reset) {
     ctx->tev_used = 0;
-    ctx->tev_order.clear();
+    ctx->tev_mask.clear();
   }
   return C4S_OK;
 }
@@ -582,6 +660,29 @@ int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld, c
   return cudaGetLastError() == cudaSuccess ? C4S_OK : C4S_ERR_CUDA;
 }
 
+#ifdef C4S_TRACE
+// Measurement builds only: copy out the fused kernel's phase trace and clear it.
+int c4s_trace_read(long long* out, int* info) {
+  constexpr size_t nt = (size_t)c4s::TR_CTAS * c4s::TR_ROWS * c4s::TR_PH, ni = (size_t)c4s::TR_CTAS * c4s::TR_ROWS;
+  if (cudaMemcpyFromSymbol(out, c4s::g_trace, nt * sizeof(long long)) != cudaSuccess) return C4S_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(info, c4s::g_trace_info, ni * sizeof(int)) != cudaSuccess) return C4S_ERR_CUDA;
+  static long long zl[nt];
+  static int zi[ni];
+  if (cudaMemcpyToSymbol(c4s::g_trace, zl, sizeof(zl)) != cudaSuccess) return C4S_ERR_CUDA;
+  if (cudaMemcpyToSymbol(c4s::g_trace_info, zi, sizeof(zi)) != cudaSuccess) return C4S_ERR_CUDA;
+  return C4S_OK;
+}
+#endif
+
+int c4s_test_div_rn(const float* d_x, float d, float* d_out, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!d_x || !d_out))) return C4S_ERR_INVALID;
+  if (n == 0) return C4S_OK;
+  const long long blocks = (n + 255) / 256;
+  if (blocks > 0x7fffffffLL) return C4S_ERR_INVALID;
+  c4s::div_test_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(d_x, d, d_out, n);
+  return cudaGetLastError() == cudaSuccess ? C4S_OK : C4S_ERR_CUDA;
+}
+
 int c4s_shard_candidates(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V_shard, int64_t ld,
                          int32_t vocab_offset, int32_t V, const int32_t* d_hist, const int64_t* d_hist_off,
                          int64_t hist_total, const c4s_row_params* d_params, int32_t params_stride,
@@ -695,7 +796,10 @@ int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors, uint64_t* counters, int32
     cudaDeviceSynchronize();
   }
   if (err & C4S_DEVERR_TIMEOUT) return fail(ctx, C4S_ERR_TIMEOUT, "a bulk-copy wait timed out");
-  if (err) return fail(ctx, C4S_ERR_DEVICE, "history offsets out of range");
+  if (err & C4S_DEVERR_HIST_RANGE) return fail(ctx, C4S_ERR_DEVICE, "history offsets out of range");
+  if (err & C4S_DEVERR_SHARD)
+    return fail(ctx, C4S_ERR_DEVICE, "vocab-sharded merge refused rows it cannot decide exactly (id -1)");
+  if (err) return fail(ctx, C4S_ERR_DEVICE, "unknown device error flag");
   return C4S_OK;
 }
 

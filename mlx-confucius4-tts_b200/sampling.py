@@ -36,6 +36,9 @@ STAGE_ALL = 15
 DEBUG_FORCE_EXACT = 1
 DEBUG_FORCE_BINS = 2
 DEBUG_FORCE_REFINE = 4
+DEBUG_SPLIT_PATH = 8
+DEBUG_FAIL_AFTER_ROW = 16
+DEBUG_FUSED_PATH = 32
 COUNTER_NAMES = ("topp_exact_fallback", "draw_exact_fallback", "topk_radix",
                  "topp_binned", "draw_rowpass", "deferred", "exact_tail")
 MAX_VOCAB = 32768
@@ -89,6 +92,7 @@ def library() -> C.CDLL:
                 "c4s_shard_candidates_split": ([vp, vp, i32, i32, i64, i32, vp, vp, i64, vp, i32, vp, vp,
                                                 i64, vp], C.c_int),
                 "c4s_merge_candidates": ([vp, vp, i32, i64, i32, i32, vp, i32, vp, vp, vp, vp], C.c_int),
+                "c4s_test_div_rn": ([vp, C.c_float, vp, i64, vp], C.c_int),
             }
             for name, (args, res) in sig.items():
                 f = getattr(L, name)
@@ -172,10 +176,10 @@ class SamplingContext:
 
     def kernel_times(self, reset: bool = True):
         """{kernel: (summed device ms, launches)} of the calls recorded so far."""
-        ms = (C.c_double * 4)()
-        n = (C.c_int64 * 4)()
+        ms = (C.c_double * 5)()
+        n = (C.c_int64 * 5)()
         self._check(self.lib.c4s_kernel_times(self._h, ms, n, int(reset)), "c4s_kernel_times")
-        names = ("order_kernel", "row_kernel", "list_kernel", "defer_kernel")
+        names = ("order_kernel", "row_kernel", "list_kernel", "defer_kernel", "fused_kernel")
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(names)}
 
     # -- batched entry points -----------------------------------------------------

@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures under tests/golden/.
 
-Needs the reference tree (default /root/reference, or $C4S_REFERENCE) and is
-run by hand, never by the tests. It writes two kinds of fixtures:
+Needs the reference tree ($C4S_REFERENCE, else BASELINE.json's
+reference_path) and is run by hand, never by the tests. It writes two kinds of fixtures:
 
   hf/sampling/*.npy   The reference's own HuggingFace goldens: this script
                       imports the reference's tools/dump_golden.py and calls
@@ -24,7 +24,20 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("C4S_REFERENCE", "/root/reference")
+
+
+def _reference_tree():
+    path = os.environ.get("C4S_REFERENCE")
+    if not path:
+        import json
+        with open(os.path.join(REPO, "BASELINE.json")) as f:
+            path = json.load(f).get("reference_path")
+    if not path or not os.path.isdir(path):
+        sys.exit("make_golden.py needs the reference tree: set C4S_REFERENCE")
+    return path
+
+
+REF = _reference_tree()
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 import oracle as orc  # noqa: E402
 

@@ -178,10 +178,98 @@ def test_config2_full_batch(ctx, oracle, wl):
     assert np.array_equal(rg2, ro2)
 
 
-@pytest.mark.parametrize("flags", [1, 2, 3, 4])
+def test_fused_path_config2(c4s, oracle, wl):
+    """The fused kernel (the small-batch path) forced on the full config-2
+    batch: ids, states and processed logits bit-exact."""
+    ctx = c4s.SamplingContext(max_vocab=8194, device=0)
+    ctx.set_debug(c4s.sampling.DEBUG_FUSED_PATH)
+    b = wl.config2(seed=2)
+    ig, rg, lg = gpu_sample(ctx, b, torch, want_logits=True)
+    io, ro, lo = oracle_sample(oracle, b, want_logits=True)
+    assert np.array_equal(ig, io), np.nonzero(ig != io)[0][:10]
+    assert np.array_equal(rg, ro)
+    assert np.array_equal(bits(lg), bits(lo))
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_batch_of_three_chunks(c4s, oracle, wl, fused):
+    """B = 8192 + 37 rows with ragged histories: three 4096-row chunks on the
+    split path (each chunk offsets logits, history offsets, states and ids),
+    one launch on the fused path; ids, states and processed logits bit-exact."""
+    ctx = c4s.SamplingContext(max_vocab=8194, device=0)
+    if fused:
+        ctx.set_debug(c4s.sampling.DEBUG_FUSED_PATH)
+    b = wl.config2(seed=31, B=8192 + 37)
+    ig, rg, lg = gpu_sample(ctx, b, torch, want_logits=True)
+    io, ro, lo = oracle_sample(oracle, b, want_logits=True)
+    assert np.array_equal(ig, io), np.nonzero(ig != io)[0][:10]
+    assert np.array_equal(rg, ro)
+    assert np.array_equal(bits(lg), bits(lo))
+
+
+def test_split_path_recovers_after_failed_launch(c4s, oracle, wl):
+    """A split-path call whose list-kernel launch fails on the host (no kernel
+    faults: the launch is refused before it is made) returns an error; its
+    row kernel has already taken queue tickets, and the next call must still
+    sample every row bit-exactly."""
+    ctx = c4s.SamplingContext(max_vocab=8194, device=0)
+    ctx.set_debug(c4s.sampling.DEBUG_SPLIT_PATH | c4s.sampling.DEBUG_FAIL_AFTER_ROW)
+    b = wl.config2(seed=33, B=1000)
+    with pytest.raises(c4s.C4SError):
+        gpu_sample(ctx, b, torch)
+    torch.cuda.synchronize()
+    ctx.set_debug(c4s.sampling.DEBUG_SPLIT_PATH)
+    ig, rg, _ = gpu_sample(ctx, b, torch)
+    io, ro, _ = oracle_sample(oracle, b)
+    assert np.array_equal(ig, io)
+    assert np.array_equal(rg, ro)
+
+
+def _div_sweep(c4s, xbits, divisors):
+    lib = c4s.library()
+    x = torch.from_numpy(xbits.view(np.float32)).cuda()
+    out = torch.empty_like(x)
+    xh = xbits.view(np.float32)
+    for d in divisors:
+        rc = lib.c4s_test_div_rn(x.data_ptr(), float(np.float32(d)), out.data_ptr(), x.numel(), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        want = (xh / np.float32(d)).astype(np.float32)          # IEEE round-to-nearest
+        got = out.cpu().numpy()
+        bad = np.nonzero(got.view(np.uint32) != want.view(np.uint32))[0]
+        assert bad.size == 0, (d, xh[bad[:5]], got[bad[:5]], want[bad[:5]])
+
+
+def test_div_rn_every_mantissa(c4s):
+    """The inline exact division against IEEE division, bit for bit: every
+    mantissa of x in the binades [1, 2) and [-2^-3, -2^-2), for temperatures,
+    penalties, powers of two and divisors next to 1 (sampling.cpp:16, :26)."""
+    m = np.arange(1 << 23, dtype=np.uint32)
+    divisors = [0.5, 0.8, 1.2, 0.5000001, 0.99999994, 1.0000001, 3.0, 10.0, 2.0, 0.25, 1.7, 9.99]
+    _div_sweep(c4s, m | np.uint32(127 << 23), divisors)                     # [1, 2)
+    _div_sweep(c4s, m | np.uint32((1 << 31) | (124 << 23)), divisors)       # [-2^-3, -2^-2)
+
+
+def test_div_rn_extreme_operands(c4s):
+    """Quotients near the proof check's limits: tiny and huge dividends,
+    subnormals, zeros of both signs, infinities."""
+    g = np.random.default_rng(17)
+    xs = [g.integers(0, 1 << 32, 1 << 20, dtype=np.uint64).astype(np.uint32)]   # every float class
+    for e in (1, 2, 25, 26, 27, 100, 101, 126, 127, 226, 227, 228, 253, 254):
+        xs.append(g.integers(0, 1 << 23, 4096).astype(np.uint32) | np.uint32(e << 23))
+    xs.append(np.arange(1 << 16, dtype=np.uint32))                             # subnormals
+    xs.append(np.array([0, 1 << 31, 0x7f800000, 0xff800000, 0x7f7fffff, 0x00800000], np.uint32))
+    xb = np.concatenate(xs)
+    xb = xb[~np.isnan(xb.view(np.float32))]
+    _div_sweep(c4s, xb, [0.5, 0.8, 1.2, 10.0, 1e-30, 1e30, 3.0e-39, 1.0e38, 2.0 ** -100, 2.0 ** 100,
+                         7.0, 0.1])
+
+
+@pytest.mark.parametrize("flags", [1, 2, 3, 4, 1 | 32, 2 | 32, 4 | 32])
 def test_forced_slow_paths(c4s, oracle, wl, flags):
     """The exact fallbacks, the binned paths and the exact-tail refinement of
-    rows without top-k, forced on ordinary rows."""
+    rows without top-k, forced on ordinary rows (split kernels at B = 384,
+    and with flag 32 the fused kernel)."""
     ctx = c4s.SamplingContext(max_vocab=8194, device=0)
     ctx.set_debug(flags)
     b = wl.config2(seed=7, B=384)

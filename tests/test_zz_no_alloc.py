@@ -54,6 +54,24 @@ def test_static_entry_matches_context_entry(c4s):
 
 
 @pytest.mark.gpu
+def test_static_entry_matches_oracle(c4s, oracle):
+    """Independently of the context path: the static entry point against the
+    CPU oracle on two steps in a row (ids and states bit-exact)."""
+    wl = c4s.workloads
+    dev = torch.device("cuda", 0)
+    f = _bind(c4s.library())
+    rng_s = torch.from_numpy(wl.config2(seed=41, B=300).rng.view(np.int64).copy()).to(dev)
+    ro = wl.config2(seed=41, B=300).rng.copy()
+    for step in range(2):
+        b = wl.config2(seed=41 + step, B=300)
+        ids_s = _static_step(f, b, rng_s, dev)
+        io, _ = oracle.sample_batch(np.ascontiguousarray(b.logits), b.V, b.hist, b.hist_off, b.params, ro,
+                                    nthreads=8)
+        assert np.array_equal(ids_s, io), step
+        assert np.array_equal(rng_s.cpu().numpy().view(np.uint64), ro), step
+
+
+@pytest.mark.gpu
 def test_static_entry_rejects_oversized_rows(c4s):
     f = _bind(c4s.library())
     # V above the static scratch's capacity is refused before any launch
