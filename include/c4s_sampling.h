@@ -217,6 +217,39 @@ int c4s_sample_static(const float* d_logits, int32_t B, int32_t V, int64_t ld,
                       int32_t params_stride, uint64_t* d_rng,
                       const uint8_t* d_active, int32_t* d_out_ids, void* stream);
 
+/* ------------------------------------------------------------------------
+ * LM head of the T2S decoder on tcgen05 tensor cores. The reference computes
+ * per step (text2semantic.cpp:118-121, batched :283-286)
+ *     logits = linear(layer_norm(h, final_norm.weight, final_norm.bias),
+ *                     semantic_head.weight, semantic_head.bias)
+ * (nn.cpp:73-83: biased variance, (x - mean) / sqrt(var + eps); nn.cpp:11-16:
+ * y W^T + b with W = (out, in)) and copies the logits to the host.
+ *   d_hidden  bf16 [B, ld_hidden]          d_gamma, d_beta  fp32 [d] or NULL (1, 0)
+ *   d_weight  bf16 [N, ld_weight] (out x in, as the checkpoint stores it)
+ *   d_bias    fp32 [N] or NULL             d_logits  fp32 [B, ld_logits] (output)
+ *   d_norm    bf16 [B, d]: caller-owned workspace for the normalised states,
+ *             the GEMM's A operand; NULL skips the LayerNorm (logits =
+ *             hidden W^T + b, nn.cpp:11-16 alone).
+ * The GEMM accumulates in fp32 (bf16 products are exact in fp32). d is a
+ * multiple of 64 (of 128 with the LayerNorm), at most 8192; weight rows (and
+ * hidden rows without the LayerNorm) 16-byte aligned. bf16 values are passed
+ * as uint16_t bit patterns.                                                  */
+int c4s_head_logits(c4s_ctx* ctx, const uint16_t* d_hidden, int32_t B, int32_t d, int64_t ld_hidden,
+                    const float* d_gamma, const float* d_beta, float eps, const uint16_t* d_weight, int32_t N,
+                    int64_t ld_weight, const float* d_bias, uint16_t* d_norm, float* d_logits, int64_t ld_logits,
+                    void* stream);
+
+/* c4s_head_logits, then c4s_sample on the logits (same semantics and
+ * arguments; N is the vocabulary): one decode step's head and sampling with
+ * no host round trip. Replaces text2semantic.cpp:134-165 (single stream) and
+ * :296-331 (batched) after the GPT-2 forward pass.                         */
+int c4s_head_sample(c4s_ctx* ctx, const uint16_t* d_hidden, int32_t B, int32_t d, int64_t ld_hidden,
+                    const float* d_gamma, const float* d_beta, float eps, const uint16_t* d_weight, int32_t N,
+                    int64_t ld_weight, const float* d_bias, uint16_t* d_norm, float* d_logits, int64_t ld_logits,
+                    const int32_t* d_hist, const int64_t* d_hist_off, int64_t hist_total,
+                    const c4s_row_params* d_params, int32_t params_stride, uint64_t* d_rng,
+                    const uint8_t* d_active, int32_t* d_out_ids, void* stream);
+
 /* Test hook, no counterpart in the reference: d_out[i] = x[i] / d computed by
  * the kernels' inline division (a Markstein-corrected reciprocal product with
  * a proof check, else the IEEE division), so that tests can compare it bit

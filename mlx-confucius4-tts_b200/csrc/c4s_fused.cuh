@@ -146,7 +146,9 @@ struct RowKeys {
   __device__ __forceinline__ unsigned idx(int e) const { return li[e]; }
 };
 
-// Block sum of per-thread counts: every thread gets its warp's base and the total.
+// Block sum of per-thread counts: every thread gets its warp's base and the
+// total. S.redi is next written only behind later CTA barriers (the fill of
+// the row's job record is followed by one), so no barrier closes this.
 __device__ __forceinline__ int fblock_base(int cnt, FShared& S, int* total) {
   const int w = threadIdx.x >> 5;
   const int ws = __reduce_add_sync(FULL, cnt);
@@ -158,7 +160,6 @@ __device__ __forceinline__ int fblock_base(int cnt, FShared& S, int* total) {
     if (k < w) base += S.redi[k];
     t += S.redi[k];
   }
-  csync();
   *total = t;
   return base;
 }
@@ -424,12 +425,167 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
   csync();
 }
 
+// The list job of a list of at most 64 entries, by one warp with the list in
+// registers (lane l holds list positions 2l and 2l+1; positions are in index
+// order): tempered value keys; one ascending register sort of (value key,
+// position) gives the k-th largest value (top-k, sampling.cpp:30-40) and the
+// canonical top-p order (sampling.cpp:42-71); exact double probabilities of
+// the survivors; the top-p crossing on a prefix scan from the tail mass; the
+// draw (text2semantic.cpp:150-165) on a prefix scan in index order. Every
+// decision is the one list_job takes; when one of them falls inside its
+// rounding band (or the debug flags force the slow paths) it returns false
+// without writing anything, and the caller runs list_job instead.
+__device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, const float* srow,
+                                         const unsigned short* li) {
+  const int lane = threadIdx.x & 31;
+  const int n = J.n, k = J.k;
+  const bool k0 = J.kind == JOB_K0;
+  if (n > 64 || (a.debug & (C4S_DEBUG_FORCE_BINS | C4S_DEBUG_FORCE_REFINE))) return false;
+  const float T = J.T;
+  const bool do_t = T != 1.0f;
+  const float rT = do_t ? __frcp_rn(T) : 1.0f;
+  const float m_y = J.m_y;
+  unsigned vkey[2], idx[2];
+  unsigned lmin = ~0u, lmax = 0u;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int p = 2 * lane + j;
+    vkey[j] = 0u;
+    idx[j] = 0u;
+    if (p < n) {
+      idx[j] = li[p];
+      const float x = srow[idx[j]];
+      vkey[j] = fkey(do_t ? div_rn(x, T, rT) : x);
+      lmin = min(lmin, vkey[j]);
+      lmax = max(lmax, vkey[j]);
+    }
+  }
+  const unsigned vmin = __reduce_min_sync(FULL, lmin), vmax = __reduce_max_sync(FULL, lmax);
+  if (k0 && J.ykex >= vmin) return false;         // list_job hands such a row to the general path
+  // ascending (value key, position); padding (key 0) sorts first
+  unsigned long long sk[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) sk[j] = 2 * lane + j < n ? ((unsigned long long)vkey[j] << 32) | (unsigned)(2 * lane + j) : 0ull;
+  warp_sort_regs<2>(sk);
+  auto at = [&](int pos) {                          // sorted key at position pos (uniform)
+    return __shfl_sync(FULL, (pos & 1) ? sk[1] : sk[0], pos >> 1);
+  };
+  unsigned tk = vmin;
+  if (k > 0 && k < n && vmin != vmax) tk = (unsigned)(at(64 - k) >> 32);
+  // exact probabilities of the survivors, in sorted order
+  double pr[2];
+  int nl = 0;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const unsigned v = (unsigned)(sk[j] >> 32);
+    const bool sv = sk[j] != 0ull && v >= tk;
+    pr[j] = sv ? exp((double)__fsub_rn(fkey_inv(v), m_y)) : 0.0;
+    nl += sv ? 1 : 0;
+  }
+  const double ps = warp_sum_d(pr[0] + pr[1]);
+  const int ns = __reduce_add_sync(FULL, nl);
+  const unsigned long long s63 = at(63);             // the largest survivor: (vmax, last position)
+  const unsigned long long kmax = (s63 & 0xffffffff00000000ull) | li[(int)(s63 & 0xffffffffull)];
+  const double thr = J.thr, St = J.tail + ps;
+  unsigned long long kst;
+  if (thr < 0.0) {
+    kst = 0ull;                                     // p > 1: nothing removed
+  } else if (thr == 0.0) {
+    unsigned long long mk0 = KEY_MAX;               // p == 1: only zero probabilities go
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (pr[j] > 0.0) {
+        const unsigned long long y = (sk[j] & 0xffffffff00000000ull) | li[(int)(sk[j] & 0xffffffffull)];
+        mk0 = y < mk0 ? y : mk0;
+      }
+    kst = warp_min_u64(mk0);
+  } else {
+    // the first sorted position whose running mass from the tail exceeds Th
+    const double Th = thr * St;
+    const double ls = pr[0] + pr[1];
+    double incl = ls;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += y;
+    }
+    double run = J.tail + incl - ls, bf = 0.0, cu = 0.0;
+    int hj = -1;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const double nx = run + pr[j];
+      if (hj < 0 && pr[j] > 0.0 && nx > Th) { hj = j; bf = run; cu = nx; }
+      run = nx;
+    }
+    const unsigned cb = __ballot_sync(FULL, hj >= 0);
+    if (!cb) return false;                          // no crossing: list_job's exact path
+    const int L = __ffs(cb) - 1;
+    const int jL = __shfl_sync(FULL, hj, L);
+    const double before = __shfl_sync(FULL, bf, L), cur = __shfl_sync(FULL, cu, L);
+    const unsigned long long ck = at(2 * L + jL);
+    const double bd = 2.0 * ((4.0 * (k0 ? a.V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
+    if (!(before <= Th - bd && cur > Th + bd)) return false;
+    kst = (ck & 0xffffffff00000000ull) | li[(int)(ck & 0xffffffffull)];
+  }
+  kst = kst < kmax ? kst : kmax;                    // min_tokens_to_keep = 1
+  // the draw, in index order (list positions)
+  int tok = 0;
+  if (J.u53 != 0ull) {
+    double q[2];
+    int kl = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const unsigned long long yk = ((unsigned long long)vkey[j] << 32) | idx[j];
+      const bool kept = 2 * lane + j < n && vkey[j] >= tk && yk >= kst;
+      q[j] = kept ? exp((double)__fsub_rn(fkey_inv(vkey[j]), m_y)) : 0.0;
+      kl += kept ? 1 : 0;
+    }
+    const double ls = q[0] + q[1];
+    double incl = ls;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const double s2 = __shfl_sync(FULL, incl, 31);
+    const int nk = __reduce_add_sync(FULL, kl);
+    const double r = J.u * s2;
+    double acc = incl - ls, pv0 = 0.0, cv0 = 0.0;
+    int fj = -1;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const double nx = acc + q[j];
+      if (fj < 0 && q[j] > 0.0 && nx >= r) { fj = j; pv0 = acc; cv0 = nx; }
+      acc = nx;
+    }
+    const unsigned fb = __ballot_sync(FULL, fj >= 0);
+    if (!fb) return false;
+    const int L = __ffs(fb) - 1;
+    const int jL = __shfl_sync(FULL, fj, L);
+    const double prev = __shfl_sync(FULL, pv0, L), cur = __shfl_sync(FULL, cv0, L);
+    const double bd2 = 2.0 * ((4.0 * nk + 16.0) * U53 * s2);
+    if (!(prev < r - bd2 && cur > r + bd2)) return false;
+    tok = (int)__shfl_sync(FULL, jL ? idx[1] : idx[0], L);
+  }
+  if (lane == 0) {
+    a.out_ids[row] = tok;
+    a.rng[row] = J.xs;
+    J.kstar = kst;
+    J.thresh_key = k > 0 ? tk : 0u;
+    J.status = RES_DONE;
+  }
+  __syncwarp();
+  return true;
+}
+
 // The list job on a short list, by warp 0 (the other warps wait at the barrier).
 __device__ __noinline__ void f_list_warp(const Args& a, int row, const float* srow, FShared& S, FList L,
                                          unsigned long long* sb, bool refine) {
   if ((threadIdx.x >> 5) == 0) {
-    const bool ok = list_job<false, true, RowKeys>(a, row, S.J, RowKeys{srow, L.li}, sb, L.vk, L.pv, L.hist,
-                                                   refine, S.R, nullptr);
+    bool ok = !refine && f_short_job(a, row, S.J, srow, L.li);
+    if (!ok)
+      ok = list_job<false, true, RowKeys>(a, row, S.J, RowKeys{srow, L.li}, sb, L.vk, L.pv, L.hist, refine, S.R,
+                                          nullptr);
     if (threadIdx.x == 0) S.lres = ok ? 1 : 0;
   }
   csync();
@@ -515,7 +671,6 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
 #pragma unroll
   for (int w = 1; w < NWARP; ++w) kall = kall > S.redu[w] ? kall : S.redu[w];
   const float m_x = fkey_inv(kall);
-  csync();
   C4S_TR(S.tslot, 3);
 
   RowCtx rc;
@@ -525,6 +680,7 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
 
   // ---- greedy: first index of the max (sampling.cpp:73-76) ----
   if (P.greedy) {
+    csync();                                       // every warp has read S.redu
     unsigned cand = 0xffffffffu;
     if (m_x > -INFINITY && tm == m_x) {
       for (int q = 0; q < g.nq; ++q) {
@@ -634,7 +790,8 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
     sa = a;
   }
   auto fill_ninf = [&]() {
-    for (int i = tid; i < 4 * F_SLOTS; i += NT) rb[i] = -INFINITY;
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    for (int i = tid; i < F_SLOTS; i += NT) reinterpret_cast<float4*>(rb)[i] = ninf;
   };
   fill_ninf();
   int act_pend = 1;
@@ -647,18 +804,23 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
     else if (tid == 5) cp_async8(&ms.rng, a.rng + r);
     else if (tid == 6) act_pend = a.active ? (int)a.active[r] : 1;
   };
-  grid_dep_wait();                                 // RNG states and counters of the previous step
+  // one CTA takes the rows in order; several take tickets (the first row statically)
+  const bool tickets = G > 1;
+  csync();                                         // the buffer is filled before the first copy lands
+  // the previous kernel of the stream may write the logits (a head GEMM), the
+  // RNG states and the counters: wait for it, then issue the first row's copy
+  // at once, in parallel with its metadata
+  grid_dep_wait();
   grid_dep_launch();
   const int r0 = blockIdx.x;
-  if (tid == 0) S.nrow[0] = G + (int)atomicAdd(&ctr[0], 1u);
+  Staged sg = stage_row(a.logits + (long long)r0 * a.ld, V, rb, &S.bar);
+  if (tid == 0) S.nrow[0] = tickets ? G + (int)atomicAdd(&ctr[0], 1u) : r0 + 1;
   issue_meta(r0, S.meta[0]);
   cp_async_commit();
   if (tid == 6 && r0 < a.B) S.meta[0].active = act_pend;
   cp_async_wait<0>();
   csync();
   unsigned phase = 0, gphase = 0;
-  Staged sg{0, 0, -1, 0.0f};
-  if (r0 < a.B && S.meta[0].active) sg = stage_row(a.logits + (long long)r0 * a.ld, V, rb, &S.bar);
 
   int j = 0;
   int lost0 = a.B, lost1 = a.B;                    // rows this CTA holds when a bounded wait gave up
@@ -672,6 +834,22 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
     cp_async_commit();
     if (tid == 32 && next < a.B) prefetch_row(a.logits + (long long)next * a.ld, V);
     if (tid == 6 && next < a.B) nxt.active = act_pend;
+    if (!cur.active && sg.body > 0) {
+      // an inactive first row was staged before its metadata arrived: let the
+      // copy complete (bounded) so that the barrier's phase stays in step
+      if (tid == 0) {
+        S.abort_row = mbar_wait_bounded(&S.bar, phase) ? 0 : 1;
+        if (S.abort_row) atomicOr(a.errflags, C4S_DEVERR_TIMEOUT);
+      }
+      phase ^= 1u;
+      csync();
+      if (S.abort_row) {
+        if (tid == 0) mbar_wait_bounded(&S.bar, phase ^ 1u);
+        lost0 = row;
+        lost1 = next;
+        break;
+      }
+    }
     if (cur.active) {
       const c4s_row_params P = cur.P;
       const bool pen = a.hist_off && P.repetition_penalty != 1.0f;
@@ -773,7 +951,8 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
     } else if (tid == 0) {
       a.out_ids[row] = -1;
     }
-    if (tid == 0) S.nrow[(j + 1) & 1] = next < a.B ? G + (int)atomicAdd(&ctr[0], 1u) : a.B;   // the row after next
+    if (tid == 0)                                   // the row after next
+      S.nrow[(j + 1) & 1] = next >= a.B ? a.B : tickets ? G + (int)atomicAdd(&ctr[0], 1u) : next + 1;
     cp_async_wait<0>();
     csync();                                       // next metadata visible; the row buffer is free
     sg = Staged{0, 0, -1, 0.0f};
@@ -790,7 +969,7 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
     if (lost1 < a.B) a.out_ids[lost1] = -1;
   }
   // the last CTA clears the ticket counters for the next launch
-  if (tid == 0) {
+  if (tid == 0 && tickets) {
     __threadfence();
     if (atomicAdd(&ctr[1], 1u) == (unsigned)G - 1u) {
       ctr[0] = 0u;

@@ -44,6 +44,7 @@
 #include "c4s_row.cuh"
 #include "c4s_shard.cuh"
 #include "c4s_fused.cuh"
+#include "c4s_head.cuh"
 
 namespace c4s {
 
@@ -385,6 +386,91 @@ int launch_shard(c4s_ctx* ctx, c4s::ShardArgs& a, void* stream) {
   return C4S_OK;
 }
 
+// cuTensorMapEncodeTiled from the driver, through the runtime (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map of `outer` rows of `inner` elements (row pitch
+// row_bytes), read in 64 x 128 boxes with the 128-byte swizzle the UMMA
+// descriptors expect; rows past the end read as zeros.
+bool encode_bf16_rows(CUtensorMap* m, const void* base, unsigned long long inner, unsigned long long outer,
+                      unsigned long long row_bytes) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)c4s::HG_BK, (cuuint32_t)c4s::HG_BM};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_head(c4s_ctx* ctx, const uint16_t* d_hidden, int B, int d, long long ld_hidden, const float* d_gamma,
+                const float* d_beta, float eps, const uint16_t* d_weight, int N, long long ld_weight,
+                const float* d_bias, uint16_t* d_norm, float* d_logits, long long ld_logits, void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (B < 1 || N < 1) return fail(ctx, C4S_ERR_INVALID, "B and N must be >= 1");
+  if (d < c4s::HG_BK || d % c4s::HG_BK || d > c4s::HN_MAXD) return fail(ctx, C4S_ERR_INVALID, "d must be a multiple of 64 in [64, 8192]");
+  if (d_norm && d % 128) return fail(ctx, C4S_ERR_INVALID, "the LayerNorm needs d a multiple of 128");
+  if (ld_hidden < d || ld_weight < d || ld_logits < N) return fail(ctx, C4S_ERR_INVALID, "row stride below the row length");
+  if (!d_hidden || !d_weight || !d_logits) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if (((uintptr_t)d_weight & 15) || ((ld_weight * 2) & 15) || ((uintptr_t)d_norm & 15) || ((uintptr_t)d_logits & 3))
+    return fail(ctx, C4S_ERR_INVALID, "misaligned pointer or stride (TMA needs 16-byte rows)");
+  if (d_norm ? (((uintptr_t)d_hidden & 7) || (ld_hidden & 3)) : (((uintptr_t)d_hidden & 15) || ((ld_hidden * 2) & 15)))
+    return fail(ctx, C4S_ERR_INVALID, "misaligned hidden states");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  const cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e;
+  const uint16_t* A = d_hidden;
+  long long lda = ld_hidden;
+  if (d_norm) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((B + c4s::HN_WARPS - 1) / c4s::HN_WARPS));
+    cfg.blockDim = dim3(32 * c4s::HN_WARPS);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, c4s::ln_kernel, (const unsigned short*)d_hidden, ld_hidden, B, d, d_gamma, d_beta,
+                           eps, (unsigned short*)d_norm);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "layer-norm kernel launch");
+    A = d_norm;
+    lda = d;
+  }
+  CUtensorMap ta, tb;
+  if (!encode_bf16_rows(&ta, A, (unsigned long long)d, (unsigned long long)B, (unsigned long long)lda * 2) ||
+      !encode_bf16_rows(&tb, d_weight, (unsigned long long)d, (unsigned long long)N, (unsigned long long)ld_weight * 2))
+    return fail(ctx, C4S_ERR_CUDA, "tensor map encoding failed");
+  c4s::HeadGemmArgs g{d_logits, ld_logits, d_bias, B, N, d, ctx->d_err};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + c4s::HG_BN - 1) / c4s::HG_BN), (unsigned)((B + c4s::HG_BM - 1) / c4s::HG_BM));
+  cfg.blockDim = dim3(c4s::HG_THREADS);
+  cfg.dynamicSmemBytes = c4s::HG_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, c4s::head_gemm_kernel, ta, tb, g);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "head GEMM launch");
+  return C4S_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -433,6 +519,8 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c4s::fused_smem_bytes(c4s::F_MAXV));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::head_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c4s::HG_SMEM);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::fused_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              (int)cudaSharedmemCarveoutMaxShared);
@@ -775,6 +863,29 @@ int c4s_merge_candidates(c4s_ctx* ctx, const c4s_candidate* d_cand, int32_t num_
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(ctx, e, "merge_kernel launch");
   return C4S_OK;
+}
+
+int c4s_head_logits(c4s_ctx* ctx, const uint16_t* d_hidden, int32_t B, int32_t d, int64_t ld_hidden,
+                    const float* d_gamma, const float* d_beta, float eps, const uint16_t* d_weight, int32_t N,
+                    int64_t ld_weight, const float* d_bias, uint16_t* d_norm, float* d_logits, int64_t ld_logits,
+                    void* stream) {
+  return launch_head(ctx, d_hidden, B, d, ld_hidden, d_gamma, d_beta, eps, d_weight, N, ld_weight, d_bias, d_norm,
+                     d_logits, ld_logits, stream);
+}
+
+int c4s_head_sample(c4s_ctx* ctx, const uint16_t* d_hidden, int32_t B, int32_t d, int64_t ld_hidden,
+                    const float* d_gamma, const float* d_beta, float eps, const uint16_t* d_weight, int32_t N,
+                    int64_t ld_weight, const float* d_bias, uint16_t* d_norm, float* d_logits, int64_t ld_logits,
+                    const int32_t* d_hist, const int64_t* d_hist_off, int64_t hist_total,
+                    const c4s_row_params* d_params, int32_t params_stride, uint64_t* d_rng, const uint8_t* d_active,
+                    int32_t* d_out_ids, void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (N > ctx->max_vocab) return fail(ctx, C4S_ERR_CAPACITY, "N above the context's max_vocab");
+  const int rc = launch_head(ctx, d_hidden, B, d, ld_hidden, d_gamma, d_beta, eps, d_weight, N, ld_weight, d_bias,
+                             d_norm, d_logits, ld_logits, stream);
+  if (rc) return rc;
+  return c4s_sample(ctx, d_logits, B, N, ld_logits, d_hist, d_hist_off, hist_total, d_params, params_stride, d_rng,
+                    d_active, d_out_ids, nullptr, 0, stream);
 }
 
 int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors, uint64_t* counters, int32_t reset, void* stream) {

@@ -93,6 +93,10 @@ def library() -> C.CDLL:
                                                 i64, vp], C.c_int),
                 "c4s_merge_candidates": ([vp, vp, i32, i64, i32, i32, vp, i32, vp, vp, vp, vp], C.c_int),
                 "c4s_test_div_rn": ([vp, C.c_float, vp, i64, vp], C.c_int),
+                "c4s_head_logits": ([vp, vp, i32, i32, i64, vp, vp, C.c_float, vp, i32, i64, vp, vp, vp, i64, vp],
+                                    C.c_int),
+                "c4s_head_sample": ([vp, vp, i32, i32, i64, vp, vp, C.c_float, vp, i32, i64, vp, vp, vp, i64,
+                                     vp, vp, i64, vp, i32, vp, vp, vp, vp], C.c_int),
             }
             for name, (args, res) in sig.items():
                 f = getattr(L, name)
@@ -212,6 +216,51 @@ class SamplingContext:
             _dptr(out_logits), 0 if out_logits is None else out_logits.stride(0), self._stream(stream))
         self._check(rc, "c4s_sample")
         return out_ids
+
+    def head_logits(self, hidden, weight, bias=None, gamma=None, beta=None, eps: float = 1e-5,
+                    layer_norm: bool = True, norm_out=None, logits_out=None, stream=None):
+        """LM head (text2semantic.cpp:118-121): logits = LayerNorm(hidden) W^T + b
+        on the tensor cores. hidden int16/uint16 CUDA tensor of bf16 bits [B, d]
+        (or torch.bfloat16), weight bf16 [N, d]; returns fp32 logits [B, N].
+        layer_norm=False skips the LayerNorm (a plain linear, nn.cpp:11-16)."""
+        torch = _torch()
+        B, d = hidden.shape
+        N = weight.shape[0]
+        dev = hidden.device
+        if logits_out is None:
+            logits_out = torch.empty((B, N), dtype=torch.float32, device=dev)
+        if layer_norm and norm_out is None:
+            norm_out = torch.empty((B, d), dtype=torch.int16, device=dev)
+        rc = self.lib.c4s_head_logits(self._h, _dptr(hidden), B, d, hidden.stride(0), _dptr(gamma), _dptr(beta),
+                                      eps, _dptr(weight), N, weight.stride(0), _dptr(bias),
+                                      _dptr(norm_out) if layer_norm else None, _dptr(logits_out),
+                                      logits_out.stride(0), self._stream(stream))
+        self._check(rc, "c4s_head_logits")
+        return logits_out, (norm_out if layer_norm else None)
+
+    def head_sample(self, hidden, weight, bias, gamma, beta, hist, hist_off, params, rng, active=None,
+                    out_ids=None, eps: float = 1e-5, norm_out=None, logits_out=None, params_stride: int = 1,
+                    stream=None):
+        """One decode step's head and sampling (c4s_head_sample); returns
+        (ids, logits, normalised states)."""
+        torch = _torch()
+        B, d = hidden.shape
+        N = weight.shape[0]
+        dev = hidden.device
+        if logits_out is None:
+            logits_out = torch.empty((B, N), dtype=torch.float32, device=dev)
+        if norm_out is None:
+            norm_out = torch.empty((B, d), dtype=torch.int16, device=dev)
+        if out_ids is None:
+            out_ids = torch.empty(B, dtype=torch.int32, device=dev)
+        total = 0 if hist is None else hist.numel()
+        rc = self.lib.c4s_head_sample(self._h, _dptr(hidden), B, d, hidden.stride(0), _dptr(gamma), _dptr(beta),
+                                      eps, _dptr(weight), N, weight.stride(0), _dptr(bias), _dptr(norm_out),
+                                      _dptr(logits_out), logits_out.stride(0), _dptr(hist), _dptr(hist_off), total,
+                                      _dptr(params), params_stride, _dptr(rng), _dptr(active), _dptr(out_ids),
+                                      self._stream(stream))
+        self._check(rc, "c4s_head_sample")
+        return out_ids, logits_out, norm_out
 
     def sample_from_host(self, logits, hist, hist_off, params, rng, out_ids, V: int | None = None,
                          stream=None):

@@ -142,6 +142,64 @@ def config4(seed: int = 4, B: int = 512, V: int = VOCAB_SHARDED_V, top_k: int = 
                  seed_states(B, seed))
 
 
+HEAD_DIM = 1280              # GPT-2 hidden size of the T2S model (config 3)
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bf16 bit patterns (uint16), round to nearest even."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+def bf16_float(b: np.ndarray) -> np.ndarray:
+    """bf16 bit patterns (uint16) -> float32 (exact)."""
+    return (np.ascontiguousarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+@dataclasses.dataclass
+class HeadBatch:
+    """Config 3 inputs: decoder hidden states and the LM head, bf16 as uint16."""
+    hidden: np.ndarray      # uint16 (bf16) [B, d]
+    gamma: np.ndarray       # float32 [d]   final_norm.weight
+    beta: np.ndarray        # float32 [d]   final_norm.bias
+    weight: np.ndarray      # uint16 (bf16) [N, d]  semantic_head.weight (out x in)
+    bias: np.ndarray        # float32 [N]   semantic_head.bias
+    hist: np.ndarray
+    hist_off: np.ndarray
+    params: np.ndarray
+    rng: np.ndarray
+
+    @property
+    def B(self) -> int:
+        return self.hidden.shape[0]
+
+    @property
+    def N(self) -> int:
+        return self.weight.shape[0]
+
+
+def config3(seed: int = 3, B: int = 256, d: int = HEAD_DIM, N: int = SEMANTIC_VOCAB,
+            hist_len: int = 512) -> HeadBatch:
+    """c3: fused LM head + sampling -- hidden states bf16 ~N(0, 1) [B, d], head
+    weight bf16 ~N(0, 0.02^2) [N, d], LayerNorm affine and head bias near
+    their initial values (gamma 1 + N(0, 0.05^2), beta and bias N(0, 0.02^2)),
+    history 512 per row, config-0 sampling parameters, states from `seed`."""
+    g = np.random.default_rng(4000 + seed)
+    hidden = bf16_bits(g.normal(0.0, 1.0, size=(B, d)).astype(np.float32))
+    weight = bf16_bits(g.normal(0.0, 0.02, size=(N, d)).astype(np.float32))
+    gamma = (1.0 + g.normal(0.0, 0.05, size=d)).astype(np.float32)
+    beta = g.normal(0.0, 0.02, size=d).astype(np.float32)
+    bias = g.normal(0.0, 0.02, size=N).astype(np.float32)
+    hist, off = csr_history(g, np.full(B, hist_len), hi=min(N, 8192))
+    return HeadBatch(hidden, gamma, beta, weight, bias, hist, off, make_params(B), seed_states(B, seed))
+
+
+def head_flops(B: int, d: int, N: int) -> int:
+    """Multiply-adds of the head GEMM counted as 2 flops."""
+    return 2 * B * d * N
+
+
 def append_history(hist: np.ndarray, off: np.ndarray, toks: np.ndarray,
                    active: np.ndarray | None = None):
     """Append one token per (active) row to a CSR history (text2semantic.cpp:334)."""
