@@ -50,8 +50,9 @@ def parse():
     ap.add_argument("--pool", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--b1-steps", type=int, default=500)
-    ap.add_argument("--workload", choices=["c2", "c4"], default="c2",
-                    help="c2: the headline row-sharded batch; c4: vocab-sharded B=512 x V=65536 "
+    ap.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2",
+                    help="c2: the headline row-sharded batch; c3: LM head (LayerNorm + tcgen05 GEMM) + "
+                         "sampling, B=256 x d=1280 x V=8194; c4: vocab-sharded B=512 x V=65536 "
                          "(8 shards on one GPU, or one shard per rank with an NCCL all-gather)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -577,12 +578,173 @@ def run_vocab_sharded(args):
         dist.destroy_process_group()
 
 
+def tensor_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback"
+
+
+def run_head(args):
+    """Config 3: per step LayerNorm + the 1280 x 8194 head GEMM on tcgen05 +
+    the sampling step, B=256 rows (c4s_head_sample). Weights and hidden states
+    rotate through a pool larger than L2 (a decode step reads the head weights
+    from HBM once)."""
+    import torch
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    c4s = load_pkg()
+    wl = c4s.workloads
+    ctx = c4s.SamplingContext(max_vocab=wl.SEMANTIC_VOCAB, device=local)
+    stream = torch.cuda.current_stream(dev)
+    hb = wl.config3()
+    B, d, N = hb.B, hb.hidden.shape[1], hb.N
+    wbytes = N * d * 2
+    npool = max(3, -(-300_000_000 // wbytes))        # > 2x the 126 MB L2
+    g = np.random.default_rng(77)
+    pool = []
+    for k in range(npool):
+        Wk = hb.weight if k == 0 else wl.bf16_bits(g.normal(0, 0.02, size=(N, d)).astype(np.float32))
+        hk = hb.hidden if k == 0 else wl.bf16_bits(g.normal(0, 1, size=(B, d)).astype(np.float32))
+        pool.append(dict(W=torch.from_numpy(Wk.view(np.int16)).to(dev), h=torch.from_numpy(hk.view(np.int16)).to(dev)))
+    gamma, beta, bias = (torch.from_numpy(x).to(dev) for x in (hb.gamma, hb.beta, hb.bias))
+    hist, off = torch.from_numpy(hb.hist).to(dev), torch.from_numpy(hb.hist_off).to(dev)
+    params = c4s.params_tensor(hb.params, dev)
+    rng = torch.from_numpy(hb.rng.view(np.int64).copy()).to(dev)
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+    logits = torch.empty((B, N), dtype=torch.float32, device=dev)
+    norm = torch.empty((B, d), dtype=torch.int16, device=dev)
+
+    def step(s):
+        p = pool[s % npool]
+        ctx.head_sample(p["h"], p["W"], bias, gamma, beta, hist, off, params, rng, out_ids=ids,
+                        norm_out=norm, logits_out=logits)
+
+    def gemm(s):
+        p = pool[s % npool]
+        ctx.head_logits(norm, p["W"], bias, layer_norm=False, logits_out=logits)
+
+    if args.profile_steps:
+        for s in range(args.profile_steps):
+            step(s)
+        torch.cuda.synchronize()
+        return
+    for s in range(max(3, args.warmup)):
+        step(s)
+    torch.cuda.synchronize()
+    clk = ClockSampler(phys_index(local))
+    t_end = time.time() + 2.0
+    s = 0
+    while time.time() < t_end:
+        for _ in range(50):
+            step(s)
+            s += 1
+        torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for s in range(args.steps):
+        step(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    err, _ = ctx.status(reset=True)
+    # the GEMM alone (the tensor-core kernel), events around each launch
+    gt = []
+    for s in range(args.steps):
+        e0.record(stream)
+        gemm(s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        gt.append(e0.elapsed_time(e1))
+    gemm_ms = statistics.median(gt)
+    flops = wl.head_flops(B, d, N)
+    tf_peak, tf_kind = tensor_peaks()
+    hbm_peak, hbm_kind = peaks()
+    achieved = flops / (gemm_ms / 1e3) / 1e12
+    gemm_bytes = wbytes + B * d * 2 + B * N * 4 + N * 4
+    # e2e: hidden states from pinned host memory, ids back, through the public call
+    hh = [torch.from_numpy(np.ascontiguousarray(pool[0]["h"].cpu().numpy())).pin_memory()]
+    ids_h = torch.empty(B, dtype=torch.int32).pin_memory()
+    hdev = torch.empty((B, d), dtype=torch.int16, device=dev)
+
+    def hstep(s):
+        hdev.copy_(hh[0], non_blocking=True)
+        p = pool[s % npool]
+        ctx.head_sample(hdev, p["W"], bias, gamma, beta, hist, off, params, rng, out_ids=ids, norm_out=norm,
+                        logits_out=logits)
+        ids_h.copy_(ids, non_blocking=True)
+
+    for s in range(3):
+        hstep(s)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for s in range(args.steps):
+        hstep(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    # CPU stand-in: float32 GEMM on the host (numpy BLAS, all threads) + the
+    # C oracle's sampling on those logits, one step of the same batch
+    cpu = None
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as orc
+        o = orc.Oracle()
+        x = wl.bf16_float(hb.hidden)
+        xm = x - x.mean(axis=1, keepdims=True)
+        y = xm / np.sqrt((xm * xm).mean(axis=1, keepdims=True) + 1e-5) * hb.gamma + hb.beta
+        Wf = wl.bf16_float(hb.weight)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            lg = y.astype(np.float32) @ Wf.T + hb.bias
+            o.sample_batch(np.ascontiguousarray(lg, np.float32), N, hb.hist, hb.hist_off, hb.params, hb.rng.copy(),
+                           nthreads=os.cpu_count() or 1)
+            n += 1
+            if time.perf_counter() - t0 > min(args.cpu_seconds, 5.0):
+                break
+        el = time.perf_counter() - t0
+        cpu = {"value": B * n / el, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{n} steps of the config-3 batch: numpy float32 GEMM (multithreaded BLAS) + the C "
+                         f"oracle's sampling on {os.cpu_count()} threads (the reference's head runs in MLX, "
+                         "which is not installed)"}
+    line = {
+        "metric": "sampled tokens/s (LM head + sampling, B=256, d=1280, V=8194, config 3)",
+        "value": B / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 GEMM (fp32 accumulate) + f32/f64 sampling", "data": "synthetic",
+        "config": {"workload": "config3: hidden bf16 N(0,1) [256,1280], head bf16 N(0,0.02^2) [8194,1280], "
+                               "LayerNorm + bias, config-0 sampling, history 512",
+                   "l2": f"pool of {npool} weight matrices rotated (> 2x L2)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tf_peak, "traffic": None, "kernel": "head_gemm_kernel",
+                     "peak_kind": tf_kind, "flops_per_launch": flops, "gemm_ms": gemm_ms,
+                     "hbm_achieved_gbs": gemm_bytes / (gemm_ms / 1e3) / 1e9, "hbm_peak": hbm_peak,
+                     "hbm_frac": gemm_bytes / (gemm_ms / 1e3) / 1e9 / hbm_peak},
+        "cpu_baseline": cpu,
+        "e2e": {"value": B / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": B * d * 2,
+                "d2h_bytes_per_step": B * 4, "ms_per_step": ms_e2e},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks, "device_errors": err,
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "c4":
         run_vocab_sharded(args)
+    elif args.workload == "c3":
+        run_head(args)
     else:
         run_ours(args)
 

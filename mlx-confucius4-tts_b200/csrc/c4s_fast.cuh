@@ -1239,10 +1239,12 @@ __device__ __forceinline__ int ubin(unsigned d) {
 }
 template <int NTH, typename Sync>
 __device__ __forceinline__ float u_threshold(float tm, float t2, bool two, float m_x, int k, unsigned* bins,
-                                             unsigned* res, Sync sync) {
+                                             unsigned* res, Sync sync, bool zeroed = false) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < 256; i += NTH) bins[i] = 0u;
-  sync();
+  if (!zeroed) {                                   // else the caller cleared them behind an earlier barrier
+    for (int i = tid; i < 256; i += NTH) bins[i] = 0u;
+    sync();
+  }
   const unsigned km = fkey(m_x);
   if (tm > -INFINITY) atomicAdd(&bins[ubin(km - fkey(tm))], 1u);
   if (two && t2 > -INFINITY) atomicAdd(&bins[ubin(km - fkey(t2))], 1u);

@@ -280,7 +280,7 @@ __device__ __noinline__ int f_topk_list(const RowCtx rc, const float* rb, const 
   // `two`) is finite has >= kw elements >= it, so >= k elements are >= tau,
   // the smallest over the warps (-inf: not enough elements; general path)
   if (k > NT * (two ? 2 : 1)) return -1;
-  const float tau = u_threshold<NT>(tm, t2, two, rc.m_x, k, L.bins, &S.redu[0], [] { csync(); });
+  const float tau = u_threshold<NT>(tm, t2, two, rc.m_x, k, L.bins, &S.redu[0], [] { csync(); }, true);
   // fl(x/T) merges x only with values at most |x| 2^-23 below it: lowering tau
   // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
   const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;
@@ -436,7 +436,7 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
 // rounding band (or the debug flags force the slow paths) it returns false
 // without writing anything, and the caller runs list_job instead.
 __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, const float* srow,
-                                         const unsigned short* li) {
+                                         const unsigned short* li, double* pvs) {
   const int lane = threadIdx.x & 31;
   const int n = J.n, k = J.k;
   const bool k0 = J.kind == JOB_K0;
@@ -472,14 +472,17 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
   };
   unsigned tk = vmin;
   if (k > 0 && k < n && vmin != vmax) tk = (unsigned)(at(64 - k) >> 32);
-  // exact probabilities of the survivors, in sorted order
+  // probabilities of the survivors, in sorted order (Tang's exp_tail, within
+  // 2^-51 of the reference's exp: every decision below is checked against a
+  // band that covers it), also stored by list position for the draw
   double pr[2];
   int nl = 0;
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const unsigned v = (unsigned)(sk[j] >> 32);
     const bool sv = sk[j] != 0ull && v >= tk;
-    pr[j] = sv ? exp((double)__fsub_rn(fkey_inv(v), m_y)) : 0.0;
+    pr[j] = sv ? exp_tail(__fsub_rn(fkey_inv(v), m_y), EXP2_J64) : 0.0;
+    if (sk[j] != 0ull) pvs[(int)(sk[j] & 0xffffffffull)] = pr[j];
     nl += sv ? 1 : 0;
   }
   const double ps = warp_sum_d(pr[0] + pr[1]);
@@ -491,14 +494,9 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
   if (thr < 0.0) {
     kst = 0ull;                                     // p > 1: nothing removed
   } else if (thr == 0.0) {
-    unsigned long long mk0 = KEY_MAX;               // p == 1: only zero probabilities go
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-      if (pr[j] > 0.0) {
-        const unsigned long long y = (sk[j] & 0xffffffff00000000ull) | li[(int)(sk[j] & 0xffffffffull)];
-        mk0 = y < mk0 ? y : mk0;
-      }
-    kst = warp_min_u64(mk0);
+    // p == 1: only zero probabilities go, which exp_tail (0 below -700) does
+    // not tell apart from the reference's smallest ones: list_job decides
+    return false;
   } else {
     // the first sorted position whose running mass from the tail exceeds Th
     const double Th = thr * St;
@@ -531,13 +529,14 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
   // the draw, in index order (list positions)
   int tok = 0;
   if (J.u53 != 0ull) {
+    __syncwarp();                                   // pvs written in sorted order, read by position
     double q[2];
     int kl = 0;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const unsigned long long yk = ((unsigned long long)vkey[j] << 32) | idx[j];
       const bool kept = 2 * lane + j < n && vkey[j] >= tk && yk >= kst;
-      q[j] = kept ? exp((double)__fsub_rn(fkey_inv(vkey[j]), m_y)) : 0.0;
+      q[j] = kept ? pvs[2 * lane + j] : 0.0;
       kl += kept ? 1 : 0;
     }
     const double ls = q[0] + q[1];
@@ -582,7 +581,7 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
 __device__ __noinline__ void f_list_warp(const Args& a, int row, const float* srow, FShared& S, FList L,
                                          unsigned long long* sb, bool refine) {
   if ((threadIdx.x >> 5) == 0) {
-    bool ok = !refine && f_short_job(a, row, S.J, srow, L.li);
+    bool ok = !refine && f_short_job(a, row, S.J, srow, L.li, L.pv);
     if (!ok)
       ok = list_job<false, true, RowKeys>(a, row, S.J, RowKeys{srow, L.li}, sb, L.vk, L.pv, L.hist, refine, S.R,
                                           nullptr);
@@ -649,6 +648,10 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
   const bool two = !P.greedy && do_k && k > NWARP * 32 / 2;   // the two largest per lane seed the list
 
   // ---- row max, per-lane maxima (and second maxima) ----
+  // (top-k rows: the threshold histogram's bins are cleared here, ordered
+  // before their use by the barrier of the max reduction)
+  if (!P.greedy && do_k) L.bins[tid] = 0u;
+  static_assert(NT == 256, "one bin per thread");
   float tm = -INFINITY, t2 = -INFINITY;
 #pragma unroll 3
   for (int q = 0; q < g.nq; ++q) {

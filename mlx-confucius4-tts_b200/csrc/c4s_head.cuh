@@ -13,7 +13,7 @@
 //   one CTA per 128 x 128 tile of the [B, N] output, 6 warps --
 //     warp 0 (one lane)  TMA producer: 128 x 64 bf16 tiles of y and W per
 //                        k-block by cp.async.bulk.tensor (128-byte swizzle)
-//                        into a 4-stage shared-memory ring (full/empty
+//                        into a 6-stage shared-memory ring (full/empty
 //                        mbarriers);
 //     warp 1             allocates 128 TMEM columns; one lane issues
 //                        tcgen05.mma kind::f16 (M 128, N 128, K 16; bf16 in,
@@ -35,7 +35,7 @@
 
 namespace c4s {
 
-constexpr int HG_BM = 128, HG_BN = 128, HG_BK = 64, HG_ST = 4;
+constexpr int HG_BM = 128, HG_BN = 128, HG_BK = 64, HG_ST = 6;
 constexpr int HG_THREADS = 192;
 constexpr unsigned HG_TILE_BYTES = (unsigned)HG_BM * HG_BK * 2;          // one 128 x 64 bf16 tile: 16 KB
 constexpr unsigned HG_STAGE_BYTES = 2 * HG_TILE_BYTES;                    // y tile + W tile
@@ -189,6 +189,13 @@ __global__ void __launch_bounds__(32 * HN_WARPS) ln_kernel(const unsigned short*
   }
 }
 
+#ifdef C4S_TRACE
+__device__ long long g_htrace[1024 * 8];
+#define C4S_HTR(ph) (g_htrace[((blockIdx.y * gridDim.x + blockIdx.x) & 1023) * 8 + (ph)] = clock64())
+#else
+#define C4S_HTR(ph)
+#endif
+
 // ---- logits = y W^T + b on tcgen05 ------------------------------------------
 __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                   const __grid_constant__ CUtensorMap tmB,
@@ -202,6 +209,8 @@ __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * HG_BN, m0 = blockIdx.y * HG_BM;
   const int KB = g.K / HG_BK;
+  const int kstart = KB > 0 ? (int)(blockIdx.x % (unsigned)KB) : 0;
+  if (threadIdx.x == 0) C4S_HTR(0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < HG_ST; ++s) {
       mbar_init(&full[s], 1);
@@ -220,16 +229,22 @@ __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_c
   const unsigned tmem = tmem_base;
   grid_dep_wait();                                 // y is written by the LayerNorm kernel
   grid_dep_launch();
+  if (threadIdx.x == 0) C4S_HTR(1);
   auto give_up = [&]() {
     atomicOr(g.errflags, C4S_DEVERR_TIMEOUT);
     abort_flag = 1;
   };
   if (warp == 0) {
     if (lane == 0) {
-      // TMA producer
-      for (int kb = 0; kb < KB && !abort_flag; ++kb) {
-        const int s = kb % HG_ST;
-        const unsigned ph = (unsigned)(kb / HG_ST) & 1u;
+      // TMA producer. Every CTA of a row block reads the same activations:
+      // each starts at its own k-block (and wraps around), so that the CTAs
+      // running at once read different parts of them instead of queueing on
+      // the same L2 lines; the CTAs of one weight tile start together, and
+      // the second of them finds the tile in L2.
+      for (int it = 0; it < KB && !abort_flag; ++it) {
+        const int s = it % HG_ST;
+        const unsigned ph = (unsigned)(it / HG_ST) & 1u;
+        const int kb = (it + kstart) % KB;
         if (!mbar_wait_1s(&empty[s], ph ^ 1u)) { give_up(); break; }
         unsigned char* sa = hsm + (size_t)s * HG_STAGE_BYTES;
         mbar_arrive_expect_tx(&full[s], HG_STAGE_BYTES);
@@ -240,47 +255,59 @@ __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_c
   } else if (warp == 1) {
     if (lane == 0) {
       // MMA issuer: 4 MMAs of K = 16 per 64-wide k-block
-      int kb = 0;
-      for (; kb < KB && !abort_flag; ++kb) {
-        const int s = kb % HG_ST;
-        const unsigned ph = (unsigned)(kb / HG_ST) & 1u;
+      for (int it = 0; it < KB && !abort_flag; ++it) {
+        const int s = it % HG_ST;
+        const unsigned ph = (unsigned)(it / HG_ST) & 1u;
         if (!mbar_wait_1s(&full[s], ph)) { give_up(); break; }
+        if (it == 0) C4S_HTR(2);
+        if (it == KB / 2) C4S_HTR(3);
         tc_fence_after();
         const unsigned char* sa = hsm + (size_t)s * HG_STAGE_BYTES;
         const unsigned long long ad = sw128_desc(sa), bd = sw128_desc(sa + HG_TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HG_BK / 16; ++kk)
-          umma_bf16(tmem, ad + 2ull * kk, bd + 2ull * kk, (kb | kk) != 0 ? 1u : 0u);
+          umma_bf16(tmem, ad + 2ull * kk, bd + 2ull * kk, (it | kk) != 0 ? 1u : 0u);
         umma_commit(&empty[s]);                     // the stage is free once these MMAs have read it
       }
+      C4S_HTR(4);
       umma_commit(&accum);                          // every MMA issued so far has completed
     }
   } else {
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = rows of the tile
     const bool ok = mbar_wait_1s(&accum, 0u);
     if (!ok) give_up();
+    if (threadIdx.x == 64) C4S_HTR(5);
     tc_fence_after();
     if (ok && !abort_flag && KB > 0) {
+      // each 32 x 32 chunk (lane = row) goes through shared memory (the idle
+      // pipeline buffers: every MMA, hence every load, has completed)
+      // transposed, so that each store writes 32 consecutive logits of one row
       const int q = warp & 3;
-      const int m = m0 + 32 * q + lane;
-      float* orow = g.logits + (long long)m * g.ldl;
+      float* T = reinterpret_cast<float*>(hsm) + (warp - 2) * (32 * 33);
+      const int rows = min(32, g.M - (m0 + 32 * q));   // rows of this warp's quarter inside the output
+      float* obase = g.logits + (long long)(m0 + 32 * q) * g.ldl + n0 + lane;
 #pragma unroll 1
       for (int c = 0; c < HG_BN / 32; ++c) {
+        const int n = n0 + 32 * c + lane;
+        const float bn = (g.bias && n < g.N) ? __ldg(g.bias + n) : 0.0f;
         unsigned r[32];
         tmem_ld32(tmem + ((unsigned)(32 * q) << 16) + (unsigned)(32 * c), r);
         tmem_ld_wait();
-        if (m < g.M) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + 32 * c + j;
-            if (n < g.N) orow[n] = __uint_as_float(r[j]) + (g.bias ? __ldg(g.bias + n) : 0.0f);
-          }
+        for (int j = 0; j < 32; ++j) T[lane * 33 + j] = __uint_as_float(r[j]);   // conflict-free: bank (lane + j)
+        __syncwarp();
+        if (n < g.N) {
+          float* o = obase + 32 * c;
+#pragma unroll 8
+          for (int rr = 0; rr < rows; ++rr) o[(long long)rr * g.ldl] = T[rr * 33 + lane] + bn;
         }
+        __syncwarp();
       }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) C4S_HTR(6);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, HG_TMEM_COLS);

@@ -486,40 +486,47 @@ __device__ __forceinline__ int row_body(const Args& a, const Args& ao, int row, 
 // Rows by cost class for the row kernel, dearest first, so that its last
 // wave holds cheap rows and its CTAs finish together: sampled rows without
 // top-k (octave histogram), top-k above 64 (two maxima per lane), other top-k,
-// then greedy and inactive rows. One CTA of ORDER_NT threads for a chunk of
-// up to K_CHUNK rows: class slots from shared-memory counters (one atomic per
-// class and warp), the class sizes stored to defer_cnt[ORD_CNT + c].
-constexpr int ORDER_NT = 1024;
+// then greedy and inactive rows. One thread per row, ORDER_NT rows per CTA:
+// class slots from shared-memory counters (one atomic per class and warp),
+// then one global atomic per class and CTA reserves the CTA's range of the
+// class; the class sizes accumulate in defer_cnt[ORD_CNT + c] (zero at the
+// start: cleared by the general kernel of the previous launch sequence).
+constexpr int ORDER_NT = 512;
 __global__ void __launch_bounds__(ORDER_NT) order_kernel(Args a) {
-  __shared__ unsigned cnt[ROW_CLASSES];
+  __shared__ unsigned cnt[ROW_CLASSES], gbase[ROW_CLASSES];
   const int lane = threadIdx.x & 31;
-  grid_dep_launch();
-  grid_dep_wait();                                 // the previous call resets the class counters
   if (threadIdx.x < ROW_CLASSES) cnt[threadIdx.x] = 0u;
   __syncthreads();
-  for (int r0 = 0; r0 < a.B; r0 += ORDER_NT) {
-    const int r = r0 + (int)threadIdx.x;
-    int c = -1;
-    if (r < a.B) {
-      const c4s_row_params P = a.params[(long long)r * a.params_stride];
-      const bool act = a.active == nullptr || a.active[r] != 0;
-      const int k = P.top_k;
-      c = (!act || P.greedy) ? 3 : (k <= 0 || k >= a.V) ? 0 : k > RWARP * 32 / 2 ? 1 : 2;
-    }
+  const int r = blockIdx.x * ORDER_NT + (int)threadIdx.x;
+  int c = -1;
+  grid_dep_launch();
+  grid_dep_wait();                                 // the previous sequence clears the class counters (and an
+                                                   // earlier kernel of the stream may write params or active flags)
+  if (r < a.B) {
+    const c4s_row_params P = a.params[(long long)r * a.params_stride];
+    const bool act = a.active == nullptr || a.active[r] != 0;
+    const int k = P.top_k;
+    c = (!act || P.greedy) ? 3 : (k <= 0 || k >= a.V) ? 0 : k > RWARP * 32 / 2 ? 1 : 2;
+  }
+  unsigned slot = 0u;
 #pragma unroll
-    for (int cc = 0; cc < ROW_CLASSES; ++cc) {
-      const unsigned m = __ballot_sync(FULL, c == cc);
-      if (m == 0u) continue;
-      const int leader = __ffs(m) - 1;
-      unsigned base = 0u;
-      if (lane == leader) base = atomicAdd(&cnt[cc], (unsigned)__popc(m));
-      base = __shfl_sync(FULL, base, leader);
-      const unsigned slot = base + (unsigned)__popc(m & ((1u << lane) - 1u));
-      if (c == cc && slot < (unsigned)K_CHUNK) a.order[(size_t)cc * K_CHUNK + slot] = r;
-    }
+  for (int cc = 0; cc < ROW_CLASSES; ++cc) {
+    const unsigned m = __ballot_sync(FULL, c == cc);
+    if (m == 0u) continue;
+    const int leader = __ffs(m) - 1;
+    unsigned base = 0u;
+    if (lane == leader) base = atomicAdd(&cnt[cc], (unsigned)__popc(m));
+    base = __shfl_sync(FULL, base, leader);
+    if (c == cc) slot = base + (unsigned)__popc(m & ((1u << lane) - 1u));
   }
   __syncthreads();
-  if (threadIdx.x < ROW_CLASSES) a.defer_cnt[ORD_CNT + threadIdx.x] = cnt[threadIdx.x];
+  if (threadIdx.x < ROW_CLASSES)
+    gbase[threadIdx.x] = cnt[threadIdx.x] ? atomicAdd(&a.defer_cnt[ORD_CNT + threadIdx.x], cnt[threadIdx.x]) : 0u;
+  __syncthreads();
+  if (c >= 0) {
+    const unsigned s = gbase[c] + slot;
+    if (s < (unsigned)K_CHUNK) a.order[(size_t)c * K_CHUNK + s] = r;
+  }
 }
 
 // The row of the row kernel's t-th ticket (B: none left).

@@ -303,7 +303,7 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       ac.order = nullptr;
       if (ac.B > g1 && ac.params_stride != 0) {
         ac.order = ctx->d_order;
-        e = launch_pdl(order_kernel, 1, ORDER_NT, 0, st, ac);
+        e = launch_pdl(order_kernel, (ac.B + ORDER_NT - 1) / ORDER_NT, ORDER_NT, 0, st, ac);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "order kernel launch");
         if (ev) ctx->tev_mask.back() |= 1u;
       }
@@ -756,6 +756,7 @@ int c4s_trace_read(long long* out, int* info) {
   if (cudaMemcpyFromSymbol(info, c4s::g_trace_info, ni * sizeof(int)) != cudaSuccess) return C4S_ERR_CUDA;
   static long long zl[nt];
   static int zi[ni];
+  if (cudaMemcpyFromSymbol(out + nt, c4s::g_htrace, 1024 * 8 * sizeof(long long)) != cudaSuccess) return C4S_ERR_CUDA;
   if (cudaMemcpyToSymbol(c4s::g_trace, zl, sizeof(zl)) != cudaSuccess) return C4S_ERR_CUDA;
   if (cudaMemcpyToSymbol(c4s::g_trace_info, zi, sizeof(zi)) != cudaSuccess) return C4S_ERR_CUDA;
   return C4S_OK;
