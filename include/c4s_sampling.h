@@ -87,6 +87,8 @@ typedef struct c4s_row_params {
 /* Device-side error bits reported by c4s_get_status().                     */
 #define C4S_DEVERR_HIST_RANGE 1u /* a row's history offsets were out of range */
 #define C4S_DEVERR_TIMEOUT 2u    /* a bounded wait on a bulk copy gave up      */
+#define C4S_DEVERR_HIST_FULL 8u  /* c4s_decode_step: a row's history window was full
+                                    (or its id outside the embedding); the row stopped */
 #define C4S_DEVERR_SHARD 4u      /* vocab-sharded merge: a row it cannot decide
                                     exactly (top_k outside [1, 64], or more than
                                     64 of a shard's values tied at the top_k
@@ -154,6 +156,36 @@ int c4s_sample(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V,
                int32_t params_stride, uint64_t* d_rng, const uint8_t* d_active,
                int32_t* d_out_ids, float* d_out_logits, int64_t out_ld,
                void* stream);
+
+/* c4s_sample with each row's history given as a window of d_hist:
+ * [d_hist_start[b], d_hist_start[b] + d_hist_len[b]) (int64 starts, int32
+ * lengths, both [B]; both NULL: no history). Histories that grow in place on
+ * the device (c4s_decode_step) are read this way without repacking a CSR
+ * array. Same semantics and replacement as c4s_sample.                     */
+int c4s_sample_windows(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V, int64_t ld,
+                       const int32_t* d_hist, const int64_t* d_hist_start, const int32_t* d_hist_len,
+                       int64_t hist_total, const c4s_row_params* d_params, int32_t params_stride,
+                       uint64_t* d_rng, const uint8_t* d_active, int32_t* d_out_ids, float* d_out_logits,
+                       int64_t out_ld, void* stream);
+
+/* The bookkeeping of one decode step after sampling, on the device
+ * (text2semantic.cpp:167-178 single stream, :333-351 batched), for B rows:
+ *   an active row (d_active NULL: every row) whose id is stop_token becomes
+ *   inactive and counts in *d_done_count; any other active row appends its id
+ *   to its history window (d_hist at d_hist_start[b], length d_hist_len[b] <
+ *   hist_cap, advanced) and, with d_latents, the hidden state d_cur[b] that
+ *   predicted it to latents [B][hist_cap][D]; a full window stops the row
+ *   (C4S_DEVERR_HIST_FULL). Then every row's next input embedding:
+ *   d_next_emb[b] = d_emb[tok] + d_pos_emb (bf16 adds rounded to nearest
+ *   even; d_pos_emb is the position row for this step), tok = the appended
+ *   id, 0 for rows that did not append (as the reference embeds them).
+ * bf16 tensors are uint16_t bit patterns, rows of D contiguous elements;
+ * d_cur may be the d_next_emb buffer itself.                               */
+int c4s_decode_step(c4s_ctx* ctx, const int32_t* d_ids, int32_t B, uint8_t* d_active, int32_t stop_token,
+                    int32_t* d_hist, const int64_t* d_hist_start, int32_t* d_hist_len, int32_t hist_cap,
+                    const uint16_t* d_emb, int32_t n_emb, const uint16_t* d_pos_emb, int32_t D,
+                    uint16_t* d_next_emb, const uint16_t* d_cur, uint16_t* d_latents,
+                    uint32_t* d_done_count, void* stream);
 
 /* Apply the processors selected by `stages` (C4S_STAGE_* bits) in place to B
  * rows of d_logits, in the reference order, ignoring params.greedy.

@@ -5,7 +5,7 @@ name `c4s`. CUDA kernels and the C ABI live in csrc/ (built into
 lib/libc4s.so); this module is the Python mirror of the reference's
 c4::t2s::sampling interface on top of that ABI.
 """
-from . import sharding, vocab_shard, workloads  # noqa: F401
+from . import decode, sharding, vocab_shard, workloads  # noqa: F401
 from .sampling import (  # noqa: F401
     C4SError, SamplingContext, argmax, default_context, library, params_tensor,
     repetition_penalty, temperature, top_k, top_p, STAGE_ALL, STAGE_PENALTY,

@@ -68,7 +68,7 @@ struct __align__(16) MetaSlot {
   long long off0, off1;      // history window [off0, off1)
   unsigned long long rng;    // xorshift64 state before this step
   int active;
-  int pad;
+  int hlen;                  // history window length (windowed histories; off1 unused)
 };
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -1027,7 +1027,7 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
   long long h0 = 0, h1 = 0;
   if (pen) {
     h0 = a.hist_off[row];
-    h1 = a.hist_off[row + 1];
+    h1 = a.hist_len ? h0 + a.hist_len[row] : a.hist_off[row + 1];
     if (h0 < 0 || h1 < h0 || h1 > a.hist_total) pen = false;   // the row kernel flagged it
   }
   // history ids eight per thread at a time, the first batch in flight while the bitmap clears

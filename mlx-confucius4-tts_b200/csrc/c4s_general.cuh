@@ -22,7 +22,8 @@ struct Args {
   int B, V;
   long long ld;
   const int* hist;
-  const long long* hist_off;
+  const long long* hist_off;   // CSR [B+1], or with hist_len the window starts [B]
+  const int* hist_len;          // null (CSR), or per-row window lengths [B]
   long long hist_total;
   const c4s_row_params* params;
   int params_stride;
@@ -639,7 +640,7 @@ __device__ __forceinline__ void hist_window(const Args& a, int row, bool do_pen,
   h0 = h1 = 0;
   if (!do_pen) return;
   h0 = a.hist_off[row];
-  h1 = a.hist_off[row + 1];
+  h1 = a.hist_len ? h0 + a.hist_len[row] : a.hist_off[row + 1];
   if (h0 < 0 || h1 < h0 || h1 > a.hist_total) {
     if (threadIdx.x == 0) atomicOr(a.errflags, C4S_DEVERR_HIST_RANGE);
     h0 = h1 = 0;

@@ -565,7 +565,11 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
     const char* prm = reinterpret_cast<const char*>(a.params + (long long)r * a.params_stride);
     if (tid < 3) cp_async8(reinterpret_cast<char*>(&ms.P) + 8 * tid, prm + 8 * tid);
     else if (tid == 3) { if (a.hist_off) cp_async8(&ms.off0, a.hist_off + r); else ms.off0 = 0; }
-    else if (tid == 4) { if (a.hist_off) cp_async8(&ms.off1, a.hist_off + r + 1); else ms.off1 = 0; }
+    else if (tid == 4) {
+      if (a.hist_len) cp_async4(&ms.hlen, a.hist_len + r);
+      else if (a.hist_off) cp_async8(&ms.off1, a.hist_off + r + 1);
+      else ms.off1 = 0;
+    }
     else if (tid == 5) cp_async8(&ms.rng, a.rng + r);
     else if (tid == 6) act_pend = a.active ? (int)a.active[r] : 1;
   };
@@ -602,7 +606,7 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
       long long h0 = 0, h1 = 0;
       if (pen) {
         h0 = cur.off0;
-        h1 = cur.off1;
+        h1 = a.hist_len ? h0 + cur.hlen : cur.off1;
         if (h0 < 0 || h1 < h0 || h1 > a.hist_total) {
           if (tid == 0) atomicOr(a.errflags, C4S_DEVERR_HIST_RANGE);
           h0 = h1 = 0;

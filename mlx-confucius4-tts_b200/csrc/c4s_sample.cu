@@ -45,6 +45,7 @@
 #include "c4s_shard.cuh"
 #include "c4s_fused.cuh"
 #include "c4s_head.cuh"
+#include "c4s_decode.cuh"
 
 namespace c4s {
 
@@ -296,6 +297,7 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       ac.out_ids = a.out_ids + c0;
       if (a.out_logits) ac.out_logits = a.out_logits + (long long)c0 * a.out_ld;
       if (a.hist_off) ac.hist_off = a.hist_off + c0;
+      if (a.hist_len) ac.hist_len = a.hist_len + c0;
       const int g1 = (int)std::min<long long>(ac.B, (long long)ctx->row_occ * ctx->num_sms);
       cudaEvent_t* ev = ctx->timing ? timing_slot(ctx) : nullptr;
       if (ev) cudaEventRecord(ev[0], st);
@@ -649,6 +651,67 @@ int c4s_sample(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V, int64_
   return launch_rows(ctx, a, stream);
 }
 
+int c4s_sample_windows(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V, int64_t ld, const int32_t* d_hist,
+                       const int64_t* d_hist_start, const int32_t* d_hist_len, int64_t hist_total,
+                       const c4s_row_params* d_params, int32_t params_stride, uint64_t* d_rng,
+                       const uint8_t* d_active, int32_t* d_out_ids, float* d_out_logits, int64_t out_ld,
+                       void* stream) {
+  int rc = check_common(ctx, B, V, ld);
+  if (rc) return rc;
+  if (B == 0) return C4S_OK;
+  if (!d_logits || !d_params || !d_rng || !d_out_ids) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if (params_stride != 0 && params_stride != 1) return fail(ctx, C4S_ERR_INVALID, "params_stride not 0/1");
+  if ((d_hist_start == nullptr) != (d_hist_len == nullptr))
+    return fail(ctx, C4S_ERR_INVALID, "history windows need both starts and lengths");
+  if (d_hist_start && (!d_hist && hist_total > 0)) return fail(ctx, C4S_ERR_INVALID, "history ids missing");
+  if (hist_total < 0) return fail(ctx, C4S_ERR_INVALID, "hist_total < 0");
+  if (d_out_logits && out_ld < V) return fail(ctx, C4S_ERR_INVALID, "out_ld < V");
+  if (((uintptr_t)d_logits & 3) || (d_out_logits && ((uintptr_t)d_out_logits & 3)) || ((uintptr_t)d_hist_len & 3))
+    return fail(ctx, C4S_ERR_INVALID, "misaligned pointer");
+  c4s::Args a{};
+  a.logits = d_logits;
+  a.B = B; a.V = V; a.ld = ld;
+  a.hist = d_hist; a.hist_off = reinterpret_cast<const long long*>(d_hist_start); a.hist_len = d_hist_len;
+  a.hist_total = hist_total;
+  a.params = d_params; a.params_stride = params_stride;
+  a.rng = reinterpret_cast<unsigned long long*>(d_rng);
+  a.active = d_active;
+  a.out_ids = d_out_ids;
+  a.out_logits = d_out_logits; a.out_ld = out_ld;
+  a.mode = c4s::MODE_SAMPLE;
+  return launch_rows(ctx, a, stream);
+}
+
+int c4s_decode_step(c4s_ctx* ctx, const int32_t* d_ids, int32_t B, uint8_t* d_active, int32_t stop_token,
+                    int32_t* d_hist, const int64_t* d_hist_start, int32_t* d_hist_len, int32_t hist_cap,
+                    const uint16_t* d_emb, int32_t n_emb, const uint16_t* d_pos_emb, int32_t D,
+                    uint16_t* d_next_emb, const uint16_t* d_cur, uint16_t* d_latents, uint32_t* d_done_count,
+                    void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (B < 0 || D < 1 || hist_cap < 0 || n_emb < 1) return fail(ctx, C4S_ERR_INVALID, "bad size");
+  if (B == 0) return C4S_OK;
+  if (!d_ids || !d_hist || !d_hist_start || !d_hist_len || !d_emb || !d_pos_emb || !d_next_emb || !d_done_count)
+    return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if ((d_latents != nullptr) != (d_cur != nullptr)) return fail(ctx, C4S_ERR_INVALID, "latents need the hidden states");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  c4s::DecodeArgs g{d_ids, B, d_active, stop_token, d_hist, reinterpret_cast<const long long*>(d_hist_start),
+                    d_hist_len, hist_cap, d_emb, n_emb, d_pos_emb, D, d_next_emb, d_cur, d_latents, d_done_count,
+                    ctx->d_err};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)B);
+  cfg.blockDim = dim3(c4s::DEC_NT);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, c4s::decode_step_kernel, g);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "decode step launch");
+  return C4S_OK;
+}
+
 int c4s_process(c4s_ctx* ctx, float* d_logits, int32_t B, int32_t V, int64_t ld, const int32_t* d_hist,
                 const int64_t* d_hist_off, int64_t hist_total, const c4s_row_params* d_params,
                 int32_t params_stride, int32_t stages, void* stream) {
@@ -909,6 +972,8 @@ int c4s_get_status(c4s_ctx* ctx, uint32_t* dev_errors, uint64_t* counters, int32
   }
   if (err & C4S_DEVERR_TIMEOUT) return fail(ctx, C4S_ERR_TIMEOUT, "a bulk-copy wait timed out");
   if (err & C4S_DEVERR_HIST_RANGE) return fail(ctx, C4S_ERR_DEVICE, "history offsets out of range");
+  if (err & C4S_DEVERR_HIST_FULL)
+    return fail(ctx, C4S_ERR_DEVICE, "a decode step found a full history window (the row stopped)");
   if (err & C4S_DEVERR_SHARD)
     return fail(ctx, C4S_ERR_DEVICE, "vocab-sharded merge refused rows it cannot decide exactly (id -1)");
   if (err) return fail(ctx, C4S_ERR_DEVICE, "unknown device error flag");

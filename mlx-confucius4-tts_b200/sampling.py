@@ -93,6 +93,10 @@ def library() -> C.CDLL:
                                                 i64, vp], C.c_int),
                 "c4s_merge_candidates": ([vp, vp, i32, i64, i32, i32, vp, i32, vp, vp, vp, vp], C.c_int),
                 "c4s_test_div_rn": ([vp, C.c_float, vp, i64, vp], C.c_int),
+                "c4s_sample_windows": ([vp, vp, i32, i32, i64, vp, vp, vp, i64, vp, i32, vp, vp, vp, vp, i64, vp],
+                                       C.c_int),
+                "c4s_decode_step": ([vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, vp, vp],
+                                    C.c_int),
                 "c4s_head_logits": ([vp, vp, i32, i32, i64, vp, vp, C.c_float, vp, i32, i64, vp, vp, vp, i64, vp],
                                     C.c_int),
                 "c4s_head_sample": ([vp, vp, i32, i32, i64, vp, vp, C.c_float, vp, i32, i64, vp, vp, vp, i64,
@@ -216,6 +220,35 @@ class SamplingContext:
             _dptr(out_logits), 0 if out_logits is None else out_logits.stride(0), self._stream(stream))
         self._check(rc, "c4s_sample")
         return out_ids
+
+    def sample_windows(self, logits, hist, hist_start, hist_len, params, rng, active=None, out_ids=None,
+                       out_logits=None, V: int | None = None, params_stride: int = 1, stream=None):
+        """c4s_sample with per-row history windows: hist int32, hist_start int64
+        [B], hist_len int32 [B] (row b's ids are hist[start[b]:start[b]+len[b]])."""
+        torch = _torch()
+        B, ld = logits.shape
+        V = ld if V is None else V
+        if out_ids is None:
+            out_ids = torch.empty(B, dtype=torch.int32, device=logits.device)
+        total = 0 if hist is None else hist.numel()
+        rc = self.lib.c4s_sample_windows(
+            self._h, _dptr(logits), B, V, logits.stride(0), _dptr(hist), _dptr(hist_start), _dptr(hist_len), total,
+            _dptr(params), params_stride, _dptr(rng), _dptr(active), _dptr(out_ids), _dptr(out_logits),
+            0 if out_logits is None else out_logits.stride(0), self._stream(stream))
+        self._check(rc, "c4s_sample_windows")
+        return out_ids
+
+    def decode_step(self, ids, active, stop_token: int, hist, hist_start, hist_len, hist_cap: int, emb, pos_row,
+                    next_emb, done_count, cur=None, latents=None, stream=None):
+        """c4s_decode_step: append ids to the history windows, stop rows on
+        stop_token, write next_emb = emb[tok] + pos_row (bf16 bits)."""
+        B = ids.shape[0]
+        D = emb.shape[1]
+        rc = self.lib.c4s_decode_step(
+            self._h, _dptr(ids), B, _dptr(active), stop_token, _dptr(hist), _dptr(hist_start), _dptr(hist_len),
+            hist_cap, _dptr(emb), emb.shape[0], _dptr(pos_row), D, _dptr(next_emb), _dptr(cur), _dptr(latents),
+            _dptr(done_count), self._stream(stream))
+        self._check(rc, "c4s_decode_step")
 
     def head_logits(self, hidden, weight, bias=None, gamma=None, beta=None, eps: float = 1e-5,
                     layer_norm: bool = True, norm_out=None, logits_out=None, stream=None):
