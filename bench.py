@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--pool", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--b1-steps", type=int, default=500)
-    ap.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "qgemv"], default="c2",
                     help="c2: the headline row-sharded batch; c3: LM head (LayerNorm + tcgen05 GEMM) + "
                          "sampling, B=256 x d=1280 x V=8194; c4: vocab-sharded B=512 x V=65536 "
                          "(8 shards on one GPU, or one shard per rank with an NCCL all-gather)")
@@ -144,6 +144,43 @@ def phys_index(local):
 
 
 # ---------------------------------------------------------------------------
+WORKLOAD_C2 = ("config2: B=4096 V=8194 fp32 logits ~N(0,9), ragged history U[0,2048], per-row T U[0.5,1.2], "
+               "top_k {0,20,50,200}, top_p U[0.6,1.0], penalty U[1,10]")
+
+
+def c2_config(rows, world):
+    """The workload dict both arms print (identical for the same launch)."""
+    return {"workload": WORKLOAD_C2, "global_batch": rows * world, "rows_per_gpu": rows, "V": 8194,
+            "l2": "inputs > L2 (a pool of 3 batches rotated on the GPU)"}
+
+
+def cpu_serial_rows_per_s(c4s, batch, rows=192):
+    """The reference's CPU path on ONE thread, rows processed one after the
+    other as generate_batch loops them (text2semantic.cpp:303), on the first
+    `rows` rows of the batch (a bounded sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    impl, kind = (orc.RefOracle(), "reference") if orc.RefOracle.available() else (orc.Oracle(), "port")
+    n = min(rows, batch.B)
+    sub = c4s.workloads.Batch(np.ascontiguousarray(batch.logits[:n]), batch.V, batch.hist, batch.hist_off[:n + 1],
+                              batch.params[:n], batch.rng[:n].copy())
+    t0 = time.perf_counter()
+    impl.sample_batch(sub.logits, sub.V, sub.hist, sub.hist_off, sub.params, sub.rng, nthreads=1)
+    el = time.perf_counter() - t0
+    return n / el, kind, n
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_reference_rows_per_s(c4s, seconds, rows_cap=4096, batch=None):
     """Time the reference CPU path (compiled reference, else the C port) on
     config-2 rows with all host threads; returns (rows/s, kind, threads, rows)."""
@@ -191,16 +228,22 @@ def run_reference(args):
         step()
     el = time.perf_counter() - t0
     v = args.rows * args.steps / el
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    sv, _, sn = cpu_serial_rows_per_s(c4s, b)
     line = {
         "impl": "reference", "metric": "sampled tokens/s (B=4096, V=8194, config 2)", "value": v,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32+f64", "data": "synthetic",
-        "config": {"workload": "config2: B=4096 V=8194 ragged history, per-row T/top_k/top_p/penalty",
-                   "global_batch": args.rows, "rows_per_gpu": args.rows, "parallelism": "cpu"},
+        "config": c2_config(args.rows, world),
+        "execution": f"host CPU, OpenMP over rows, {threads} threads, rank 0 only",
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
                          "sample": f"full {args.rows}-row config-2 batch per step, OpenMP over rows "
-                                   f"with {threads} threads"},
+                                   f"with {threads} threads",
+                         "serial_1core": {"value": sv, "unit": "tokens/s",
+                                          "sample": f"first {sn} rows of the batch, one thread, rows one after "
+                                                    "the other (text2semantic.cpp:303)"},
+                         "cpu_model": cpu_model()},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -228,6 +271,14 @@ def run_ours(args):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def gather_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if world == 1:
+            return [x]
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
 
     c4s = load_pkg()
     wl = c4s.workloads
@@ -289,11 +340,51 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     clocks = clk.stop()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    my_ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(my_ms)
+    per_rank_ms = gather_ranks(my_ms)
     ms_per_step = ms / args.steps
     rows_total = B * world * args.steps
     value = rows_total / (ms / 1e3)
     err, counters = ctx.status(reset=True)
+
+    # ---- strong scaling (N > 1): the one 4096-row config-2 batch split into
+    # contiguous blocks of 4096/N rows, one per rank ----
+    strong = None
+    if world > 1 and B % world == 0:
+        Bs = B // world
+        sp = []
+        for k in range(args.pool):
+            bs = wl.config2(seed=2 + k, B=B)              # the same global batch on every rank
+            r0 = rank * Bs
+            sub = wl.Batch(np.ascontiguousarray(bs.logits[r0:r0 + Bs]), bs.V, bs.hist,
+                           bs.hist_off[r0:r0 + Bs + 1], bs.params[r0:r0 + Bs], bs.rng[r0:r0 + Bs].copy())
+            sp.append(dict(logits=torch.from_numpy(sub.logits).to(dev), hist=torch.from_numpy(sub.hist).to(dev),
+                           hist_off=torch.from_numpy(sub.hist_off).to(dev),
+                           params=c4s.params_tensor(sub.params, dev),
+                           rng=torch.from_numpy(sub.rng.view(np.int64).copy()).to(dev)))
+        ids_s = torch.empty(Bs, dtype=torch.int32, device=dev)
+
+        def sstep(s):
+            p = sp[s % len(sp)]
+            ctx.sample(p["logits"], p["hist"], p["hist_off"], p["params"], p["rng"], out_ids=ids_s)
+
+        for s in range(max(3, args.warmup)):
+            sstep(s)
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for s in range(args.steps):
+            sstep(s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        my_sms = e0.elapsed_time(e1)
+        sms = max_over_ranks(my_sms)
+        strong = {"global_batch": B, "rows_per_gpu": Bs, "value": B * args.steps / (sms / 1e3),
+                  "unit": "tokens/s", "ms_per_step": sms / args.steps,
+                  "per_rank_ms_per_step": [t / args.steps for t in gather_ranks(my_sms)],
+                  "scaling": "strong"}
 
     # ---- per-kernel device time: the same K steps again with CUDA events between
     # the launches (order pre-pass -> row kernel -> list kernel -> general path,
@@ -407,13 +498,33 @@ def run_ours(args):
                       "eager: event-to-event time around one host launch (host launch overhead included)"}
         del g, g64
 
+    # ---- config 1 (B=64 streams): GPU time per step in a captured 64-step loop ----
+    c1 = None
+    if rank == 0:
+        bc1 = wl.config1()
+        dc1 = dict(logits=torch.from_numpy(bc1.logits).to(dev), hist=torch.from_numpy(bc1.hist).to(dev),
+                   hist_off=torch.from_numpy(bc1.hist_off).to(dev), params=c4s.params_tensor(bc1.params, dev),
+                   rng=torch.from_numpy(bc1.rng.view(np.int64).copy()).to(dev))
+        idc1 = torch.empty(bc1.B, dtype=torch.int32, device=dev)
+
+        def s64(s):
+            ctx.sample(dc1["logits"], dc1["hist"], dc1["hist_off"], dc1["params"], dc1["rng"], out_ids=idc1)
+
+        c1 = {"us_per_step": graph_ms_per_step(torch, s64, 64, 5, stream) * 1e3, "rows": bc1.B,
+              "timing": "CUDA-graph replay of 64 dependent steps"}
+
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, kind, threads, nrows = cpu_reference_rows_per_s(c4s, args.cpu_seconds, batch=host[0])
+        sv, _, sn = cpu_serial_rows_per_s(c4s, host[0])
         cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
                "sample": f"{nrows} rows of the config-2 batch (first {min(B, nrows)} rows, wrapping), "
-                         f"OpenMP over rows, {threads} host threads, ~{args.cpu_seconds:.0f} s"}
+                         f"OpenMP over rows, {threads} host threads, ~{args.cpu_seconds:.0f} s",
+               "serial_1core": {"value": sv, "unit": "tokens/s",
+                                "sample": f"first {sn} rows of the batch, one thread, rows one after the other "
+                                          "(text2semantic.cpp:303)"},
+               "cpu_model": cpu_model()}
 
     if rank == 0:
         line = {
@@ -421,12 +532,11 @@ def run_ours(args):
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32+f64", "data": "synthetic",
-            "config": {"workload": "config2: B=4096 V=8194 fp32 logits ~N(0,9), ragged history "
-                                   "U[0,2048], per-row T U[0.5,1.2], top_k {0,20,50,200}, top_p U[0.6,1.0], "
-                                   "penalty U[1,10]",
-                       "global_batch": B * world, "rows_per_gpu": B, "V": wl.SEMANTIC_VOCAB,
-                       "parallelism": f"rows x{world} (no collective)",
-                       "l2": f"pool of {args.pool} batches rotated (inputs > L2)"},
+            "config": c2_config(B, world),
+            "execution": f"rows x{world} (no collective), pool of {args.pool} batches rotated",
+            "per_rank_ms_per_step": [t / args.steps for t in per_rank_ms],
+            "strong": strong,
+            "c1": c1,
             "b1_p50_us": None if b1 is None else b1["graph_step_p50_us"],
             "b1": b1,
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
@@ -578,6 +688,35 @@ def run_vocab_sharded(args):
         dist.destroy_process_group()
 
 
+def graph_ms_per_step(torch, step, nsteps, reps, stream):
+    """GPU time per step of `step(s)` for s in range(nsteps), captured once in
+    a CUDA graph and replayed `reps` times between CUDA events: small steps
+    are timed without the host's per-launch overhead."""
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for s in range(nsteps):
+            step(s)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for s in range(nsteps):
+            step(s)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * nsteps)
+    del g
+    return ms
+
+
 def tensor_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -646,23 +785,19 @@ def run_head(args):
         torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    e0.record(stream)
+    # steps replayed from a CUDA graph of one pass over the pool (the three
+    # launches of a step take less GPU time than Python takes to issue them)
+    reps = max(1, args.steps // npool)
+    ms = graph_ms_per_step(torch, step, npool, reps, stream)
+    clocks = clk.stop()
+    err, _ = ctx.status(reset=True)
+    # the GEMM alone (the tensor-core kernel), the same way
+    gemm_ms = graph_ms_per_step(torch, gemm, npool, reps, stream)
+    eager_t0 = time.perf_counter()
     for s in range(args.steps):
         step(s)
-    e1.record(stream)
     torch.cuda.synchronize()
-    clocks = clk.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    err, _ = ctx.status(reset=True)
-    # the GEMM alone (the tensor-core kernel), events around each launch
-    gt = []
-    for s in range(args.steps):
-        e0.record(stream)
-        gemm(s)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        gt.append(e0.elapsed_time(e1))
-    gemm_ms = statistics.median(gt)
+    eager_ms = (time.perf_counter() - eager_t0) * 1e3 / args.steps
     flops = wl.head_flops(B, d, N)
     tf_peak, tf_kind = tensor_peaks()
     hbm_peak, hbm_kind = peaks()
@@ -716,8 +851,11 @@ def run_head(args):
                          "which is not installed)"}
     line = {
         "metric": "sampled tokens/s (LM head + sampling, B=256, d=1280, V=8194, config 3)",
-        "value": B / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "value": B / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": reps * npool, "warmup": args.warmup,
+        "ms_per_step": ms, "eager_ms_per_step": eager_ms,
+        "timing": "CUDA-graph replay of one pass over the weight pool; eager_ms_per_step: the same step "
+                  "issued from Python each time (host-bound)",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 GEMM (fp32 accumulate) + f32/f64 sampling", "data": "synthetic",
         "config": {"workload": "config3: hidden bf16 N(0,1) [256,1280], head bf16 N(0,0.02^2) [8194,1280], "
                                "LayerNorm + bias, config-0 sampling, history 512",
@@ -737,6 +875,70 @@ def run_head(args):
     ctx.close()
 
 
+def run_qgemv(args):
+    """Quantized decode projections (gpt2.cpp:52-73, int8 group 64: the
+    reference's product default): per step the four projections of one GPT-2
+    layer (c_attn 1280->3840, attn c_proj 1280->1280, mlp c_fc 1280->5120, mlp
+    c_proj 5120->1280) at B=1, the weights of 12 layers rotating (> 2x L2)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    c4s = load_pkg()
+    ctx = c4s.SamplingContext(max_vocab=64, device=0)
+    stream = torch.cuda.current_stream(dev)
+    D, bits, group, B = 1280, 8, 64, 1
+    shapes = [(3 * D, D), (D, D), (4 * D, D), (D, 4 * D)]
+    g = torch.Generator(device=dev).manual_seed(0)
+    layers = []
+    for _ in range(12):
+        lay = []
+        for N, K in shapes:
+            w = torch.randn((N, K), device=dev, generator=g) * 0.02
+            lay.append((*ctx.quantize_affine(w, group, bits), torch.zeros(N, device=dev), N, K))
+            del w
+        layers.append(lay)
+    x = {K: torch.randn((B, K), device=dev, generator=g) for K in (D, 4 * D)}
+    y = {N: torch.empty((B, N), device=dev) for N, _ in shapes}
+
+    def step(s):
+        for q, sc, bi, bo, N, K in layers[s % len(layers)]:
+            ctx.qgemv(x[K], q, sc, bi, group, bits, bias_out=bo, out=y[N])
+
+    for s in range(max(3, args.warmup)):
+        step(s)
+    torch.cuda.synchronize()
+    clk = ClockSampler(phys_index(0))
+    t_end = time.time() + 2.0
+    s = 0
+    while time.time() < t_end:
+        for _ in range(20):
+            step(s)
+            s += 1
+        torch.cuda.synchronize()
+    ms = graph_ms_per_step(torch, step, len(layers), max(1, args.steps // len(layers)), stream)
+    clocks = clk.stop()
+    wbytes = sum(N * K * (bits / 8 + 8 / group) for N, K in shapes)
+    io_bytes = sum(4 * B * (N + K) + 4 * N for N, K in shapes)
+    hbm_peak, kind = peaks()
+    gbs = (wbytes + io_bytes) / (ms / 1e3) / 1e9
+    line = {
+        "metric": "quantized decode projections per GPT-2 layer (int8 group 64, B=1)", "value": ms * 1e3,
+        "unit": "us per layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "timing": "CUDA-graph replay of the 12 layers' projections (4 launches per layer)",
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 math",
+        "data": "synthetic",
+        "config": {"workload": "GPT-2 d=1280 layer: 1280x3840, 1280x1280, 1280x5120, 5120x1280, B=1",
+                   "l2": "12 layers of weights rotated (266 MB > 2x L2)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "kernel": "qgemv_kernel", "peak_kind": kind,
+                     "alg_bytes_per_step": wbytes + io_bytes},
+        "gpu_launches": 4 * args.steps, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -745,6 +947,8 @@ def main():
         run_vocab_sharded(args)
     elif args.workload == "c3":
         run_head(args)
+    elif args.workload == "qgemv":
+        run_qgemv(args)
     else:
         run_ours(args)
 

@@ -187,6 +187,27 @@ int c4s_decode_step(c4s_ctx* ctx, const int32_t* d_ids, int32_t B, uint8_t* d_ac
                     uint16_t* d_next_emb, const uint16_t* d_cur, uint16_t* d_latents,
                     uint32_t* d_done_count, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Quantized decode GEMVs of the T2S GPT-2. The reference's default build
+ * (apps/c4tts_cli.cpp:300-306, C4TTS_QUANT=8) quantizes each projection weight
+ * once (gpt2.cpp:52-60: the (out, in) weight, mx::quantize, group 64) and runs
+ * the decode projections as quantized_matmul(x, w_q, scales, biases,
+ * transpose=true) + bias (gpt2.cpp:61-63). Affine scheme, per group of
+ * `group` consecutive weights of a row: scale = (max - min) / (2^bits - 1),
+ * bias = min, q = round((w - bias) / scale) (half to even); w ~= scale q + bias;
+ * codes packed little-end-first in 32-bit words.
+ *   c4s_quantize_affine: w fp32 [N, K] -> d_q uint32 [N, K * bits / 32],
+ *                        scales / biases fp32 [N, K / group];
+ *   c4s_qgemv:           y fp32 [B, N] = x fp32 [B, K] dequant(q)^T + bias_out
+ *                        (bias_out fp32 [N] or NULL), fp32 accumulation; built
+ *                        for decode batches (weight-bandwidth bound).
+ * bits 4 or 8; group 32, 64 or 128 dividing K; K <= 8192 for the GEMV.     */
+int c4s_quantize_affine(c4s_ctx* ctx, const float* d_w, int32_t N, int32_t K, int32_t group, int32_t bits,
+                        uint32_t* d_q, float* d_scales, float* d_biases, void* stream);
+int c4s_qgemv(c4s_ctx* ctx, const float* d_x, int32_t B, int32_t K, const uint32_t* d_q, const float* d_scales,
+              const float* d_biases, int32_t N, int32_t group, int32_t bits, const float* d_bias_out, float* d_y,
+              void* stream);
+
 /* Apply the processors selected by `stages` (C4S_STAGE_* bits) in place to B
  * rows of d_logits, in the reference order, ignoring params.greedy.
  * Replaces the in-place processors of sampling.cpp:14-71 / t2s.h:83-88:

@@ -46,6 +46,7 @@
 #include "c4s_fused.cuh"
 #include "c4s_head.cuh"
 #include "c4s_decode.cuh"
+#include "c4s_qgemv.cuh"
 
 namespace c4s {
 
@@ -139,6 +140,7 @@ struct c4s_ctx {
   size_t tev_used = 0;
   int cached_V = -1;
   int cached_occ = 0;
+  size_t qg_smem_set = 0;                      // dynamic shared memory allowed for the quantized GEMV
   std::string last_error;
 };
 
@@ -709,6 +711,59 @@ int c4s_decode_step(c4s_ctx* ctx, const int32_t* d_ids, int32_t B, uint8_t* d_ac
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, c4s::decode_step_kernel, g);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "decode step launch");
+  return C4S_OK;
+}
+
+int c4s_quantize_affine(c4s_ctx* ctx, const float* d_w, int32_t N, int32_t K, int32_t group, int32_t bits,
+                        uint32_t* d_q, float* d_scales, float* d_biases, void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (N < 1 || K < 1 || (bits != 4 && bits != 8) || (group != 32 && group != 64 && group != 128) || K % group)
+    return fail(ctx, C4S_ERR_INVALID, "need bits 4 or 8, group 32/64/128 dividing K");
+  if (!d_w || !d_q || !d_scales || !d_biases) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  const long long groups = (long long)N * (K / group);
+  c4s::quantize_kernel<<<(unsigned)((groups + 7) / 8), 256, 0, (cudaStream_t)stream>>>(d_w, N, K, group, bits, d_q,
+                                                                                      d_scales, d_biases);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? C4S_OK : cuda_fail(ctx, e, "quantize launch");
+}
+
+int c4s_qgemv(c4s_ctx* ctx, const float* d_x, int32_t B, int32_t K, const uint32_t* d_q, const float* d_scales,
+              const float* d_biases, int32_t N, int32_t group, int32_t bits, const float* d_bias_out, float* d_y,
+              void* stream) {
+  if (!ctx) return C4S_ERR_INVALID;
+  if (B < 0 || N < 1 || K < 1 || K > c4s::QG_MAXK || (bits != 4 && bits != 8) ||
+      (group != 32 && group != 64 && group != 128) || K % group || K % (128 / bits))
+    return fail(ctx, C4S_ERR_INVALID, "need bits 4 or 8, group 32/64/128 dividing K, K <= 8192");
+  if (B == 0) return C4S_OK;
+  if (!d_x || !d_q || !d_scales || !d_biases || !d_y) return fail(ctx, C4S_ERR_INVALID, "null pointer");
+  if ((uintptr_t)d_q & 15) return fail(ctx, C4S_ERR_INVALID, "packed weights must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
+  c4s::QGemvArgs g{d_x, B, K, N, group, bits, group == 32 ? 5 : group == 64 ? 6 : 7, d_q, d_scales, d_biases,
+                   d_bias_out, d_y};
+  const size_t smem = (size_t)std::min(B, c4s::QG_MAXB) * K * sizeof(float);
+  if (ctx->qg_smem_set < smem) {
+    const cudaError_t ea = cudaFuncSetAttribute(c4s::qgemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)(c4s::QG_MAXB * c4s::QG_MAXK * sizeof(float)));
+    if (ea != cudaSuccess) return cuda_fail(ctx, ea, "qgemv attribute");
+    ctx->qg_smem_set = c4s::QG_MAXB * c4s::QG_MAXK * sizeof(float);
+  }
+  const int rows_per_cta = c4s::QG_WARPS;
+  const int grid = (int)std::min<long long>((N + rows_per_cta - 1) / rows_per_cta, 8LL * ctx->num_sms);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(c4s::QG_NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, c4s::qgemv_kernel, g);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "qgemv launch");
   return C4S_OK;
 }
 

@@ -97,6 +97,8 @@ def library() -> C.CDLL:
                                        C.c_int),
                 "c4s_decode_step": ([vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, vp, vp],
                                     C.c_int),
+                "c4s_quantize_affine": ([vp, vp, i32, i32, i32, i32, vp, vp, vp, vp], C.c_int),
+                "c4s_qgemv": ([vp, vp, i32, i32, vp, vp, vp, i32, i32, i32, vp, vp, vp], C.c_int),
                 "c4s_head_logits": ([vp, vp, i32, i32, i64, vp, vp, C.c_float, vp, i32, i64, vp, vp, vp, i64, vp],
                                     C.c_int),
                 "c4s_head_sample": ([vp, vp, i32, i32, i64, vp, vp, C.c_float, vp, i32, i64, vp, vp, vp, i64,
@@ -249,6 +251,33 @@ class SamplingContext:
             hist_cap, _dptr(emb), emb.shape[0], _dptr(pos_row), D, _dptr(next_emb), _dptr(cur), _dptr(latents),
             _dptr(done_count), self._stream(stream))
         self._check(rc, "c4s_decode_step")
+
+    def quantize_affine(self, w, group: int = 64, bits: int = 8, stream=None):
+        """Affine group quantization (MLX's scheme, gpt2.cpp:52-60) of an fp32
+        CUDA tensor w [N, K] (out x in): returns (q uint32 as int32 [N, K*bits/32],
+        scales fp32 [N, K/group], biases fp32 [N, K/group])."""
+        torch = _torch()
+        N, K = w.shape
+        q = torch.empty((N, K * bits // 32), dtype=torch.int32, device=w.device)
+        sc = torch.empty((N, K // group), dtype=torch.float32, device=w.device)
+        bi = torch.empty((N, K // group), dtype=torch.float32, device=w.device)
+        rc = self.lib.c4s_quantize_affine(self._h, _dptr(w), N, K, group, bits, _dptr(q), _dptr(sc), _dptr(bi),
+                                          self._stream(stream))
+        self._check(rc, "c4s_quantize_affine")
+        return q, sc, bi
+
+    def qgemv(self, x, q, scales, biases, group: int = 64, bits: int = 8, bias_out=None, out=None, stream=None):
+        """y = x dequant(q)^T + bias_out (quantized_matmul(transpose=true) + bias,
+        gpt2.cpp:61-63); x fp32 [B, K]."""
+        torch = _torch()
+        B, K = x.shape
+        N = q.shape[0]
+        if out is None:
+            out = torch.empty((B, N), dtype=torch.float32, device=x.device)
+        rc = self.lib.c4s_qgemv(self._h, _dptr(x), B, K, _dptr(q), _dptr(scales), _dptr(biases), N, group, bits,
+                                _dptr(bias_out), _dptr(out), self._stream(stream))
+        self._check(rc, "c4s_qgemv")
+        return out
 
     def head_logits(self, hidden, weight, bias=None, gamma=None, beta=None, eps: float = 1e-5,
                     layer_norm: bool = True, norm_out=None, logits_out=None, stream=None):

@@ -26,11 +26,12 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 
 
-def build(ref: bool = False) -> None:
-    """Build the C oracle (and, with ref=True, the reference checker)."""
+def build(ref_tree: str | None = None) -> None:
+    """Build the C oracle (and, given the reference source tree, the
+    reference checker)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref:
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    if ref_tree:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_tree}"], check=True)
 
 
 def _ptr(a):

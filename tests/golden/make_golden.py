@@ -142,7 +142,7 @@ def chain_cases():
 
 
 if __name__ == "__main__":
-    orc.build(ref=True)
+    orc.build(ref_tree=REF)
     hf_goldens()
     proc_cases()
     chain_cases()
