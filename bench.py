@@ -905,6 +905,11 @@ def run_qgemv(args):
         for q, sc, bi, bo, N, K in layers[s % len(layers)]:
             ctx.qgemv(x[K], q, sc, bi, group, bits, bias_out=bo, out=y[N])
 
+    if args.profile_steps:
+        for s in range(args.profile_steps):
+            step(s)
+        torch.cuda.synchronize()
+        return
     for s in range(max(3, args.warmup)):
         step(s)
     torch.cuda.synchronize()
