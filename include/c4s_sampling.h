@@ -118,6 +118,16 @@ const char* c4s_status_string(int status);
  * Replaces: nothing in the reference (its processors allocate per call:
  * sampling.cpp:22,33,45,52).                                                */
 int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device);
+
+/* As c4s_create, with the workspace sized for batches of up to `max_rows`
+ * rows per call (c4s_create = max_rows 4096: about 0.76 GB at max_vocab
+ * 8194, most of it candidate lists of 72 KB per row of a 4096-row chunk).
+ * Larger batches still run: the split path takes them in chunks of
+ * max_rows (rounded up to 32, at most 4096) and the fused and general
+ * kernels with at most 2 * max_rows and max_rows CTAs. max_rows 1 (one
+ * row per call, as the reference's processors take) needs about 5 MB.
+ * Replaces: nothing in the reference.                                      */
+int c4s_create_sized(c4s_ctx** out, int32_t max_vocab, int32_t max_rows, int32_t device);
 int c4s_destroy(c4s_ctx* ctx);
 
 /* Text of the last error seen by this context ("" if none). */

@@ -32,7 +32,7 @@ namespace c4s {
 constexpr int F_MAXV = 9212;              // widest row the fast path takes
 constexpr int LCAP = 9216;                // candidates per list (>= F_MAXV: a list can hold a whole row)
 constexpr int LIST_DEEP = 1024;           // rows without top-k: lists go deeper only up to this length
-constexpr int K_CHUNK = 4096;             // rows per launch sequence (list storage)
+constexpr int K_CHUNK = 4096;             // largest rows per launch sequence (list storage)
 constexpr int NOCT = 30;                  // octaves of the estimate (<= 31: one warp lane each); bin NOCT = the rest
 constexpr int LIST_WARPS = 8;             // list kernel: rows (warps) per CTA
 constexpr int LW_CAP = 1024;              // list kernel: longest list one warp takes
@@ -1166,7 +1166,7 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
       }
       t = __shfl_sync(FULL, t, 0);
       if (t >= nq) break;
-      const int row = a.big_rows[(size_t)q * K_CHUNK + t];
+      const int row = a.big_rows[(size_t)q * a.chunk + t];
       const size_t o = (size_t)row * LCAP;
       list_job<false>(a, row, a.jobs[row], GlobalKeys{a.lkeys + o}, a.lsb + o, reinterpret_cast<unsigned*>(wa + LW_VK),
                       reinterpret_cast<double*>(wa + LW_PV), reinterpret_cast<unsigned long long*>(wa + LW_HIST),
@@ -1321,7 +1321,7 @@ __device__ __forceinline__ void fill_job(RowJob& J, const RowCtx& rc, int kind, 
 __device__ __forceinline__ void queue_long_list(const Args& a, int row, int n) {
   // classes: > LW_CAP, (512, 1024], (256, 512], (128, 256], (64, 128], <= 64
   const int q = n > LW_CAP ? 0 : n > 512 ? 1 : n > 256 ? 2 : n > 128 ? 3 : n > 64 ? 4 : 5;
-  a.big_rows[(size_t)q * K_CHUNK + atomicAdd(&a.defer_cnt[3 + 2 * q], 1u)] = row;
+  a.big_rows[(size_t)q * a.chunk + atomicAdd(&a.defer_cnt[3 + 2 * q], 1u)] = row;
 }
 
 enum { ROW_DONE = 0, ROW_GENERAL = 1 };

@@ -46,10 +46,11 @@ struct Args {
   int* big_rows;                // rows whose lists the list kernel works with a whole CTA
   unsigned* defer_cnt;          // [0] count, [1] CTAs of the general-path kernel done, [2] row counter,
                                 // list queues: [3 + 2q]/[4 + 2q] rows queued/taken in class q
-                                // (rows in big_rows + q * K_CHUNK; q = 0: long lists),
+                                // (rows in big_rows + q * chunk; q = 0: long lists),
                                 // [ORD_CNT + c]: rows of the row kernel's cost class c
-  int* order;                   // [ROW_CLASSES][K_CHUNK] rows by cost class, dearest class first
+  int* order;                   // [ROW_CLASSES][chunk] rows by cost class, dearest class first
                                 // (null: the row kernel takes rows in index order)
+  int chunk;                    // rows per split-path launch sequence (the stride of the queues above)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

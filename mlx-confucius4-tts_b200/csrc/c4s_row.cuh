@@ -525,7 +525,7 @@ __global__ void __launch_bounds__(ORDER_NT) order_kernel(Args a) {
   __syncthreads();
   if (c >= 0) {
     const unsigned s = gbase[c] + slot;
-    if (s < (unsigned)K_CHUNK) a.order[(size_t)c * K_CHUNK + s] = r;
+    if (s < (unsigned)a.chunk) a.order[(size_t)c * a.chunk + s] = r;
   }
 }
 
@@ -535,7 +535,7 @@ __device__ __forceinline__ int ticket_row(const Args& a, const RShared& S, int t
   if (a.order == nullptr) return t;
 #pragma unroll
   for (int c = 0; c < ROW_CLASSES; ++c) {
-    if (t < S.ocnt[c]) return t < K_CHUNK ? a.order[(size_t)c * K_CHUNK + t] : a.B;
+    if (t < S.ocnt[c]) return t < a.chunk ? a.order[(size_t)c * a.chunk + t] : a.B;
     t -= S.ocnt[c];
   }
   return a.B;

@@ -117,6 +117,7 @@ struct c4s_ctx {
   int num_sms = 0;
   int scratch_ctas = 0;
   int scratch_stride = 0;
+  int chunk = 0;                               // rows per split-path launch sequence (<= K_CHUNK)
   unsigned long long* d_scratch = nullptr;
   unsigned* d_err = nullptr;
   unsigned long long* d_counters = nullptr;
@@ -127,7 +128,7 @@ struct c4s_ctx {
   bool split_dirty = false;                    // a split-path launch sequence stopped early: its
                                                // queue counters may be stale until cleared
   c4s::RowJob* d_jobs = nullptr;               // fast path: per-row jobs of one chunk
-  unsigned long long* d_lkeys = nullptr;       //   candidate lists [K_CHUNK][LCAP]
+  unsigned long long* d_lkeys = nullptr;       //   candidate lists [chunk][LCAP]
   unsigned long long* d_lsb = nullptr;
   int* d_defer_rows = nullptr;                 //   rows handed to the general path, then long lists
   int* d_order = nullptr;                      //   the row kernel's rows by cost class
@@ -261,15 +262,16 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     return C4S_OK;
   }
   if (a.mode == MODE_SAMPLE && a.V <= F_MAXV) {
-    // split path (large batches, or C4S_DEBUG_SPLIT_PATH), per chunk of K_CHUNK
-    // rows: row kernel -> list kernel -> general path for handed-back rows (->
+    // split path (large batches, or C4S_DEBUG_SPLIT_PATH), per chunk of
+    // ctx->chunk rows: row kernel -> list kernel -> general path for handed-back rows (->
     // masking of processed logits). Many list jobs run concurrently, one per
     // warp, which hides their latency at large batch sizes.
     a.jobs = ctx->d_jobs;
     a.lkeys = ctx->d_lkeys;
     a.lsb = ctx->d_lsb;
     a.defer_rows = ctx->d_defer_rows;
-    a.big_rows = ctx->d_defer_rows + K_CHUNK;        // LIST_CLASSES queues of K_CHUNK rows
+    a.big_rows = ctx->d_defer_rows + ctx->chunk;     // LIST_CLASSES queues of chunk rows
+    a.chunk = ctx->chunk;
     a.defer_cnt = ctx->d_defer_cnt;
     if (ctx->row_occ == 0) {
       int occ = 0;
@@ -289,9 +291,9 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
       if (e != cudaSuccess) return cuda_fail(ctx, e, "clear queue counters");
       ctx->split_dirty = false;
     }
-    for (int c0 = 0; c0 < a.B; c0 += K_CHUNK) {
+    for (int c0 = 0; c0 < a.B; c0 += ctx->chunk) {
       Args ac = a;
-      ac.B = std::min(K_CHUNK, a.B - c0);
+      ac.B = std::min(ctx->chunk, a.B - c0);
       ac.logits = a.logits + (long long)c0 * a.ld;
       ac.params = a.params + (long long)c0 * a.params_stride;
       ac.rng = a.rng + c0;
@@ -341,8 +343,9 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
   }
   const size_t smem = layout_for(a.V).total;
   const int occ = occupancy(ctx, a.V, smem);
-  const int grid = std::min<long long>((long long)a.B, (long long)std::min(occ, 8) * ctx->num_sms);
-  if (grid > ctx->scratch_ctas) return fail(ctx, C4S_ERR_CAPACITY, "grid exceeds scratch slabs");
+  // one scratch slab per CTA: a context sized for few rows runs more rows per CTA
+  const int grid = (int)std::min<long long>(std::min<long long>((long long)a.B, (long long)std::min(occ, 8) * ctx->num_sms),
+                                            (long long)ctx->scratch_ctas);
   rows_kernel<<<grid, NT, smem, (cudaStream_t)stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(ctx, e, "rows_kernel launch");
@@ -495,9 +498,13 @@ const char* c4s_status_string(int s) {
 }
 
 int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
+  return c4s_create_sized(out, max_vocab, c4s::K_CHUNK, device);
+}
+
+int c4s_create_sized(c4s_ctx** out, int32_t max_vocab, int32_t max_rows, int32_t device) {
   if (!out) return C4S_ERR_INVALID;
   *out = nullptr;
-  if (max_vocab < 1 || max_vocab > c4s::MAX_VOCAB || device < 0) return C4S_ERR_INVALID;
+  if (max_vocab < 1 || max_vocab > c4s::MAX_VOCAB || max_rows < 1 || device < 0) return C4S_ERR_INVALID;
   c4s_ctx* ctx = new c4s_ctx();
   ctx->device = device;
   ctx->max_vocab = max_vocab;
@@ -542,16 +549,19 @@ int c4s_create(c4s_ctx** out, int32_t max_vocab, int32_t device) {
   // one slab holds a sort of a whole row (general path, exact fallbacks) or
   // the fused kernel's long candidate list
   ctx->scratch_stride = std::max(p2, c4s::F_MIN_SCRATCH_STRIDE);
-  ctx->scratch_ctas = ctx->num_sms * 8;
+  // sized for max_rows rows per call (larger batches still run, in chunks and
+  // with fewer CTAs): two slabs per fused-kernel CTA, one list per chunk row
+  ctx->scratch_ctas = (int)std::min<long long>((long long)ctx->num_sms * 8, 2LL * max_rows);
+  ctx->chunk = std::min(c4s::K_CHUNK, (max_rows + 31) / 32 * 32);
   e = cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_counters, C4S_NUM_COUNTERS * sizeof(unsigned long long));
-  const size_t nl = (size_t)c4s::K_CHUNK * c4s::LCAP;
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_jobs, (size_t)c4s::K_CHUNK * sizeof(c4s::RowJob));
+  const size_t nl = (size_t)ctx->chunk * c4s::LCAP;
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_jobs, (size_t)ctx->chunk * sizeof(c4s::RowJob));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lkeys, nl * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_lsb, nl * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (1 + c4s::LIST_CLASSES) * (size_t)c4s::K_CHUNK * sizeof(int));
-  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_order, c4s::ROW_CLASSES * (size_t)c4s::K_CHUNK * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_rows, (1 + c4s::LIST_CLASSES) * (size_t)ctx->chunk * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_order, c4s::ROW_CLASSES * (size_t)ctx->chunk * sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_defer_cnt, (c4s::FUSED_CNT + 2) * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(ctx->d_defer_cnt, 0, (c4s::FUSED_CNT + 2) * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->d_default_params, sizeof(c4s_row_params));

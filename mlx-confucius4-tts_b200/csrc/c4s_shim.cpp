@@ -62,7 +62,7 @@ void ensure(int V, size_t H) {
   if (g.ctx && (g.device != dev || g.max_vocab < V)) g.release();
   if (!g.ctx) {
     int mv = V < 8194 ? 8194 : V;
-    rc(c4s_create(&g.ctx, mv, dev), "c4s_create");
+    rc(c4s_create_sized(&g.ctx, mv, 1, dev), "c4s_create_sized");   // one row per call
     g.device = dev;
     g.max_vocab = mv;
     cu(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "cudaStreamCreate");

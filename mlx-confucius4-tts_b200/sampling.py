@@ -76,6 +76,7 @@ def library() -> C.CDLL:
                 "c4s_version": ([], C.c_int),
                 "c4s_status_string": ([C.c_int], C.c_char_p),
                 "c4s_create": ([C.POINTER(vp), i32, i32], C.c_int),
+                "c4s_create_sized": ([C.POINTER(vp), i32, i32, i32], C.c_int),
                 "c4s_destroy": ([vp], C.c_int),
                 "c4s_last_error": ([vp], C.c_char_p),
                 "c4s_set_debug": ([vp, i32], C.c_int),
@@ -130,19 +131,27 @@ def params_tensor(params: np.ndarray, device) -> "torch.Tensor":
 
 
 class SamplingContext:
-    """One c4s context (device workspace) bound to a CUDA device."""
+    """One c4s context (device workspace) bound to a CUDA device.
 
-    def __init__(self, max_vocab: int = workloads.SEMANTIC_VOCAB, device=None):
+    ``max_rows`` sizes the workspace for batches of up to that many rows per
+    call (None: 4096, about 0.76 GB at max_vocab 8194); larger batches still
+    run, in chunks (c4s_create_sized)."""
+
+    def __init__(self, max_vocab: int = workloads.SEMANTIC_VOCAB, device=None, max_rows: int | None = None):
         torch = _torch()
         self.lib = library()
         if device is None:
             device = torch.cuda.current_device()
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         self.max_vocab = max_vocab
+        self.max_rows = max_rows
         h = C.c_void_p()
-        rc = self.lib.c4s_create(C.byref(h), max_vocab, self.device.index or 0)
+        if max_rows is None:
+            rc = self.lib.c4s_create(C.byref(h), max_vocab, self.device.index or 0)
+        else:
+            rc = self.lib.c4s_create_sized(C.byref(h), max_vocab, int(max_rows), self.device.index or 0)
         if rc != 0:
-            raise C4SError(rc, f"c4s_create(max_vocab={max_vocab}, device={self.device})")
+            raise C4SError(rc, f"c4s_create(max_vocab={max_vocab}, max_rows={max_rows}, device={self.device})")
         self._h = h
 
     def close(self):
@@ -438,12 +447,15 @@ _default_ctx: dict = {}
 
 
 def default_context(max_vocab: int = MAX_VOCAB) -> SamplingContext:
+    """The calling thread's context on the current device for the one-row
+    functions below (sized for one row per call: a few MB, not the 0.76 GB
+    of a 4096-row context)."""
     torch = _torch()
     dev = torch.cuda.current_device()
     key = (threading.get_ident(), dev)
     ctx = _default_ctx.get(key)
     if ctx is None:
-        ctx = SamplingContext(max_vocab=max_vocab, device=dev)
+        ctx = SamplingContext(max_vocab=max_vocab, device=dev, max_rows=1)
         _default_ctx[key] = ctx
     return ctx
 

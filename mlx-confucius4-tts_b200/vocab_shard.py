@@ -11,8 +11,38 @@ as -1 with the C4S_DEVERR_SHARD error bit.
 """
 from __future__ import annotations
 
-from .sampling import SHARD_CANDIDATES
+import numpy as np
+
+from . import workloads
+from .sampling import SHARD_CANDIDATES, params_tensor
 from .sharding import shard_rows
+
+
+def check_shardable(params, active=None) -> None:
+    """Raise ValueError if a sampled row's top_k is outside [1, 64]: the merge
+    is exact only there and refuses such rows (id -1, C4S_DEVERR_SHARD).
+    The reference's own T2S entry points default to top_k = 0 (t2s.h:156,169
+    of the reference); sample those rows with SamplingContext.sample on whole
+    rows instead. ``params`` is a host ROW_PARAMS_DTYPE array (one struct or
+    one per row), ``active`` an optional host mask."""
+    p = np.atleast_1d(np.asarray(params, dtype=workloads.ROW_PARAMS_DTYPE))
+    bad = (p["greedy"] == 0) & ((p["top_k"] < 1) | (p["top_k"] > SHARD_CANDIDATES))
+    if active is not None and p.size > 1:
+        bad &= np.asarray(active, dtype=bool).reshape(-1)
+    if bad.any():
+        rows = np.nonzero(bad)[0]
+        raise ValueError(f"vocab-sharded sampling needs 1 <= top_k <= {SHARD_CANDIDATES} on every sampled "
+                         f"row; rows {rows[:8].tolist()}{' ...' if rows.size > 8 else ''} have top_k "
+                         f"{p['top_k'][rows[:8]].tolist()}")
+
+
+def _device_params(params, active, tensor):
+    """Host params are checked (check_shardable) and uploaded to the device of
+    `tensor`; a device tensor is taken as is (refused rows then come back -1)."""
+    if isinstance(params, np.ndarray):
+        check_shardable(params, active if isinstance(active, np.ndarray) else None)
+        return params_tensor(np.atleast_1d(params), tensor.device)
+    return params
 
 
 def shard_vocab(V: int, rank: int, world: int) -> tuple[int, int]:
@@ -28,6 +58,9 @@ def sample_vocab_sharded(ctx, logits_shard, V: int, hist, hist_off, params, rng,
     of each row (rank and world of ``group``, the default process group if
     None). ``hist``/``hist_off`` carry global ids. Returns int32 ids [B],
     identical on every rank; ``rng`` is advanced identically on every rank.
+    ``params`` as a host ROW_PARAMS_DTYPE array is checked first
+    (check_shardable: ValueError for a sampled row with top_k outside
+    [1, 64]); as a device tensor it is used unchecked.
     """
     import torch
     import torch.distributed as dist
@@ -37,6 +70,7 @@ def sample_vocab_sharded(ctx, logits_shard, V: int, hist, hist_off, params, rng,
     voff, width = shard_vocab(V, rank, world)
     B = logits_shard.shape[0]
     dev = logits_shard.device
+    params = _device_params(params, active, logits_shard)
     local = torch.empty((B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
     ctx.shard_candidates(logits_shard, V, voff, hist, hist_off, params, active=active,
                          out=local, V_shard=width, params_stride=params_stride)
@@ -56,9 +90,11 @@ def sample_vocab_split(ctx, logits, num_shards: int, hist, hist_off, params, rng
     rows; shard s is the column block ``shard_vocab(V, s, num_shards)``, and
     one launch writes the candidate blocks straight into the gathered layout
     [G, B, 64]. Also the way to sample rows wider than ``SamplingContext.sample``
-    takes (32768) on one GPU, for 1 <= top_k <= 64."""
+    takes (32768) on one GPU, for 1 <= top_k <= 64 (host ``params`` are
+    checked as in sample_vocab_sharded)."""
     import torch
 
+    params = _device_params(params, active, logits)
     B, ld = logits.shape
     V = ld if V is None else V
     if cand_out is None:

@@ -62,6 +62,8 @@ def test_host_validation_without_device():
     assert lib.c4s_create(C.byref(h), 10**6, 0) == -1      # above the shared-memory limit
     assert lib.c4s_create(C.byref(h), 0, 0) == -1
     assert lib.c4s_create(None, 8194, 0) == -1
+    assert lib.c4s_create_sized(C.byref(h), 8194, 0, 0) == -1   # max_rows < 1
+    assert lib.c4s_create_sized(C.byref(h), 0, 16, 0) == -1
 
 
 def test_no_device_fails_loudly():

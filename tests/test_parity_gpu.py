@@ -207,6 +207,30 @@ def test_batch_of_three_chunks(c4s, oracle, wl, fused):
     assert np.array_equal(bits(lg), bits(lo))
 
 
+@pytest.mark.parametrize("max_rows,B,split", [(96, 1000, False), (96, 200, False), (96, 200, True), (1, 37, False)])
+def test_sized_context(c4s, oracle, wl, max_rows, B, split):
+    """A context sized for max_rows rows per call (c4s_create_sized) samples
+    larger batches in chunks of max_rows (split path) or with fewer CTAs
+    (fused kernel): ids, states and processed logits bit-exact."""
+    free0 = torch.cuda.mem_get_info(0)[0]
+    ctx = c4s.SamplingContext(max_vocab=8194, device=0, max_rows=max_rows)
+    used = free0 - torch.cuda.mem_get_info(0)[0]
+    # per row: two 72 KB candidate lists and two 128 KB scratch slabs; allocation granularity on top
+    assert used <= (32 << 20) + max_rows * (420 << 10), used
+    if split:
+        ctx.set_debug(c4s.sampling.DEBUG_SPLIT_PATH)
+    b = wl.config2(seed=37 + max_rows, B=B)
+    ig, rg, lg = gpu_sample(ctx, b, torch, want_logits=True)
+    io, ro, lo = oracle_sample(oracle, b, want_logits=True)
+    assert np.array_equal(ig, io), np.nonzero(ig != io)[0][:10]
+    assert np.array_equal(rg, ro)
+    assert np.array_equal(bits(lg), bits(lo))
+    # argmax on the general kernel, with fewer CTAs than rows
+    x = torch.from_numpy(b.logits).cuda()
+    assert np.array_equal(ctx.argmax(x).cpu().numpy(), np.argmax(b.logits, axis=1))
+    ctx.close()
+
+
 def test_split_path_recovers_after_failed_launch(c4s, oracle, wl):
     """A split-path call whose list-kernel launch fails on the host (no kernel
     faults: the launch is refused before it is made) returns an error; its

@@ -326,6 +326,28 @@ def test_ties_fallback_and_refusals(sctx, oracle):
     assert np.array_equal(ids[3:], oid[3:])
 
 
+def test_host_params_checked_before_launch():
+    """Host params with a sampled row outside 1 <= top_k <= 64 (the reference's
+    T2S default top_k 0 among them) are refused on the host, before any
+    device call; greedy and inactive rows are exempt."""
+    c4s = load_c4s()
+    vs = c4s.vocab_shard
+    P = c4s.workloads.make_params(4, top_k=30)
+    vs.check_shardable(P)
+    P["top_k"][1] = 0
+    with pytest.raises(ValueError, match=r"rows \[1\]"):
+        vs.check_shardable(P)
+    with pytest.raises(ValueError):
+        vs.sample_vocab_split(None, None, 2, None, None, P, None)    # raises before touching ctx / logits
+    P["greedy"][1] = 1
+    vs.check_shardable(P)
+    P["greedy"][1] = 0
+    P["top_k"][2] = 65
+    vs.check_shardable(P, active=np.array([1, 0, 0, 1], bool))
+    with pytest.raises(ValueError):
+        vs.check_shardable(P[2])                                       # one broadcast struct
+
+
 @pytest.mark.gpu
 def test_invalid_shard_arguments(sctx):
     import torch
