@@ -577,8 +577,10 @@ def run_vocab_sharded(args):
     ctx = c4s.SamplingContext(max_vocab=wl.SEMANTIC_VOCAB, device=local)
     stream = torch.cuda.current_stream(dev)
     B, V = 512, wl.VOCAB_SHARDED_V
-    G = 8 if world == 1 else world
     voff, width = c4s.vocab_shard.shard_vocab(V, rank, world) if world > 1 else (0, V)
+    # candidate blocks: 8 of 8192 columns at every N (N > 1: each rank's shard as sub-shards)
+    nsub = c4s.vocab_shard.sub_shards(c4s.vocab_shard.shard_vocab(V, 0, world)[1], world) if world > 1 else 1
+    G = 8 if world == 1 else world * nsub
     shard_bytes = B * width * 4
     npool = max(3, -(-300_000_000 // shard_bytes))   # > 2x the 126 MB L2 across the pool
     pool = []
@@ -637,15 +639,18 @@ def run_vocab_sharded(args):
     # the shard kernel alone (the only kernel that reads the logits), same inputs
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     shard_ms = 0.0
-    nshard = G if world == 1 else 1      # shards the one shard-kernel launch works
+    nshard = G if world == 1 else nsub   # shards the one shard-kernel launch works
     for s in range(args.steps):
         p = pool[s % npool]
         ev[0].record(stream)
         if world == 1:
             ctx.shard_candidates_split(p["logits"], G, p["hist"], p["hist_off"], p["params"], out=cand, V=V)
-        else:
+        elif nsub == 1:
             ctx.shard_candidates(p["logits"], V, voff, p["hist"], p["hist_off"], p["params"], out=cand[rank],
                                  V_shard=width)
+        else:
+            ctx.shard_candidates(p["logits"], V, voff, p["hist"], p["hist_off"], p["params"],
+                                 out=cand[rank * nsub:(rank + 1) * nsub], V_shard=width, num_sub=nsub)
         ev[1].record(stream)
         torch.cuda.synchronize()
         shard_ms += ev[0].elapsed_time(ev[1])
@@ -672,7 +677,8 @@ def run_vocab_sharded(args):
                                    "T 0.8, penalty 10, global top_k 50 / top_p 0.9",
                        "shards": G, "shard_width": V // G,
                        "parallelism": "8 shards on 1 GPU" if world == 1 else
-                                      f"vocab x{world}, NCCL all-gather of 64 candidates/row/shard",
+                                      f"vocab x{world} ({nsub} sub-shards per rank), NCCL all-gather of 64 "
+                                      f"candidates/row/sub-shard",
                        "l2": f"pool of {npool} batches rotated (inputs > 2x L2)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None, "kernel": "shard_kernel",

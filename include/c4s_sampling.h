@@ -380,6 +380,23 @@ int c4s_shard_candidates_split(c4s_ctx* ctx, const float* d_logits, int32_t B,
                                c4s_candidate* d_cand, int64_t shard_stride,
                                void* stream);
 
+/* The candidates of one GPU's vocabulary shard [vocab_offset, vocab_offset +
+ * V_shard) of [0, V) (arguments as c4s_shard_candidates), computed as
+ * `num_sub` contiguous sub-shards of the shard's columns (split as
+ * c4s_shard_candidates_split splits whole rows; every sub-shard 64..32768
+ * wide): sub-shard s's [B][64] block at d_cand + s * shard_stride. A rank
+ * whose shard is wide (32768 columns of a 65536 vocabulary on two GPUs)
+ * keeps several CTAs per SM this way; the gathered blocks of all ranks,
+ * rank-major, are in vocabulary order for c4s_merge_candidates.
+ * Replaces the same per-row body of text2semantic.cpp:303-331.             */
+int c4s_shard_candidates_sub(c4s_ctx* ctx, const float* d_logits, int32_t B,
+                             int32_t V_shard, int64_t ld, int32_t vocab_offset,
+                             int32_t V, int32_t num_sub, const int32_t* d_hist,
+                             const int64_t* d_hist_off, int64_t hist_total,
+                             const c4s_row_params* d_params, int32_t params_stride,
+                             const uint8_t* d_active, c4s_candidate* d_cand,
+                             int64_t shard_stride, void* stream);
+
 /* Token ids from the candidates of `num_shards` shards (1..C4S_MAX_SHARDS),
  * shard s's block at d_cand + s * shard_stride (shard_stride >= B * 64, in
  * candidates: the layout of an all-gather of the [B][64] blocks, shards in

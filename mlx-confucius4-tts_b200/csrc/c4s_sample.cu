@@ -937,13 +937,24 @@ int c4s_shard_candidates_split(c4s_ctx* ctx, const float* d_logits, int32_t B, i
                                int64_t hist_total, const c4s_row_params* d_params, int32_t params_stride,
                                const uint8_t* d_active, c4s_candidate* d_cand, int64_t shard_stride,
                                void* stream) {
+  return c4s_shard_candidates_sub(ctx, d_logits, B, V, ld, 0, V, num_shards, d_hist, d_hist_off, hist_total,
+                                  d_params, params_stride, d_active, d_cand, shard_stride, stream);
+}
+
+int c4s_shard_candidates_sub(c4s_ctx* ctx, const float* d_logits, int32_t B, int32_t V_shard, int64_t ld,
+                             int32_t vocab_offset, int32_t V, int32_t num_shards, const int32_t* d_hist,
+                             const int64_t* d_hist_off, int64_t hist_total, const c4s_row_params* d_params,
+                             int32_t params_stride, const uint8_t* d_active, c4s_candidate* d_cand,
+                             int64_t shard_stride, void* stream) {
   if (!ctx) return C4S_ERR_INVALID;
   if (B < 0) return fail(ctx, C4S_ERR_INVALID, "B < 0");
   if (num_shards < 1 || num_shards > c4s::MAX_SHARDS) return fail(ctx, C4S_ERR_INVALID, "num_shards outside [1, 16]");
-  if (V < 1 || V / num_shards < c4s::SHARD_CAND) return fail(ctx, C4S_ERR_INVALID, "a shard narrower than 64");
-  const int widest = V / num_shards + (V % num_shards ? 1 : 0);
+  if (V_shard < 1 || V_shard / num_shards < c4s::SHARD_CAND) return fail(ctx, C4S_ERR_INVALID, "a shard narrower than 64");
+  if (vocab_offset < 0 || (int64_t)vocab_offset + V_shard > V)
+    return fail(ctx, C4S_ERR_INVALID, "shard outside [0, V)");
+  const int widest = V_shard / num_shards + (V_shard % num_shards ? 1 : 0);
   if (widest > c4s::MAX_VOCAB) return fail(ctx, C4S_ERR_CAPACITY, "a shard wider than 32768");
-  if (ld < V) return fail(ctx, C4S_ERR_INVALID, "ld < V");
+  if (ld < V_shard) return fail(ctx, C4S_ERR_INVALID, "ld < V_shard");
   if (B == 0) return C4S_OK;
   if (shard_stride < (int64_t)B * c4s::SHARD_CAND) return fail(ctx, C4S_ERR_INVALID, "shard_stride < B * 64");
   if (!d_logits || !d_params || !d_cand) return fail(ctx, C4S_ERR_INVALID, "null pointer");
@@ -953,7 +964,7 @@ int c4s_shard_candidates_split(c4s_ctx* ctx, const float* d_logits, int32_t B, i
   if (((uintptr_t)d_logits & 3) || ((uintptr_t)d_cand & 7)) return fail(ctx, C4S_ERR_INVALID, "misaligned pointer");
   c4s::ShardArgs a{};
   a.logits = d_logits;
-  a.B = B; a.Vs = widest; a.ld = ld; a.voff = 0; a.Vtot = V;
+  a.B = B; a.Vs = widest; a.ld = ld; a.voff = vocab_offset; a.Vtot = V_shard;
   a.hist = d_hist; a.hist_off = reinterpret_cast<const long long*>(d_hist_off); a.hist_total = hist_total;
   a.params = d_params; a.params_stride = params_stride;
   a.active = d_active;

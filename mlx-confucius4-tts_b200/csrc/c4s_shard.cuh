@@ -38,12 +38,12 @@ constexpr unsigned CAND_TIES = C4S_CAND_TIES;
 static_assert(SHARD_CAND * MAX_SHARDS % NT == 0, "merge ranks whole passes of the block");
 
 struct ShardArgs {
-  const float* logits;   // G == 1: this shard's columns, row r at logits + r * ld;
-                         // G > 1: whole rows, shard s at the columns shard_span(s)
+  const float* logits;   // row r at logits + r * ld: G == 1 one shard's columns;
+                         // G > 1 the columns Vtot split into G shards (shard_span(s))
   int B, Vs;             // rows; shard width (G > 1: the widest shard)
   long long ld;
-  int voff, Vtot;        // G == 1: global index of column 0; full vocabulary
-  int G;                 // shards worked by this launch (1, or all of a whole row)
+  int voff, Vtot;        // global index of column 0; G > 1: the width that is split
+  int G;                 // shards worked by this launch (1, or all of the given columns)
   long long cand_stride; // G > 1: candidates between the shards' blocks
   const int* hist;
   const long long* hist_off;
@@ -110,11 +110,14 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
   for (long long item = blockIdx.x; item < items; item += gridDim.x) {
     const int row = (int)(item / a.G), sh = (int)(item % a.G);
     if (a.active && !a.active[row]) continue;
-    int voff = a.voff, Vs = a.Vs;
-    if (a.G > 1) shard_span(a.Vtot, a.G, sh, voff, Vs);
+    int voff = a.voff, Vs = a.Vs, loff = 0;       // loff: the shard's first column in the given ones
+    if (a.G > 1) {
+      shard_span(a.Vtot, a.G, sh, loff, Vs);
+      voff += loff;
+    }
     c4s_candidate* out = a.cand + (long long)sh * a.cand_stride + (long long)row * SHARD_CAND;
     const c4s_row_params P = a.params[(long long)row * a.params_stride];
-    const float* g = a.logits + (long long)row * a.ld + (a.G > 1 ? voff : 0);
+    const float* g = a.logits + (long long)row * a.ld + loff;
     // 1. stage the shard's row (16-byte loads when the row is aligned)
     if ((((uintptr_t)g) & 15) == 0) {
       const float4* g4 = reinterpret_cast<const float4*>(g);

@@ -92,6 +92,8 @@ def library() -> C.CDLL:
                                           vp], C.c_int),
                 "c4s_shard_candidates_split": ([vp, vp, i32, i32, i64, i32, vp, vp, i64, vp, i32, vp, vp,
                                                 i64, vp], C.c_int),
+                "c4s_shard_candidates_sub": ([vp, vp, i32, i32, i64, i32, i32, i32, vp, vp, i64, vp, i32, vp,
+                                              vp, i64, vp], C.c_int),
                 "c4s_merge_candidates": ([vp, vp, i32, i64, i32, i32, vp, i32, vp, vp, vp, vp], C.c_int),
                 "c4s_test_div_rn": ([vp, C.c_float, vp, i64, vp], C.c_int),
                 "c4s_sample_windows": ([vp, vp, i32, i32, i64, vp, vp, vp, i64, vp, i32, vp, vp, vp, vp, i64, vp],
@@ -368,16 +370,27 @@ class SamplingContext:
 
     def shard_candidates(self, logits, V: int, vocab_offset: int, hist, hist_off, params,
                          active=None, out=None, V_shard: int | None = None, params_stride: int = 1,
-                         stream=None):
+                         stream=None, num_sub: int = 1):
         """Candidates of one vocab shard: ``logits`` [B, ld] holds the shard's
         columns [vocab_offset, vocab_offset + V_shard) of rows of width V.
-        Returns int64 [B, 64] raw c4s_candidate records (value, global index)."""
+        Returns int64 [B, 64] raw c4s_candidate records (value, global index);
+        with num_sub > 1, [num_sub, B, 64]: the shard's columns as num_sub
+        contiguous sub-shards (c4s_shard_candidates_sub)."""
         torch = _torch()
         B, ld = logits.shape
         V_shard = ld if V_shard is None else V_shard
+        total = 0 if hist is None else hist.numel()
+        if num_sub > 1:
+            if out is None:
+                out = torch.empty((num_sub, B, SHARD_CANDIDATES), dtype=torch.int64, device=logits.device)
+            rc = self.lib.c4s_shard_candidates_sub(
+                self._h, _dptr(logits), B, V_shard, logits.stride(0), vocab_offset, V, num_sub, _dptr(hist),
+                _dptr(hist_off), total, _dptr(params), params_stride, _dptr(active), _dptr(out),
+                out.stride(0), self._stream(stream))
+            self._check(rc, "c4s_shard_candidates_sub")
+            return out
         if out is None:
             out = torch.empty((B, SHARD_CANDIDATES), dtype=torch.int64, device=logits.device)
-        total = 0 if hist is None else hist.numel()
         rc = self.lib.c4s_shard_candidates(
             self._h, _dptr(logits), B, V_shard, logits.stride(0), vocab_offset, V, _dptr(hist),
             _dptr(hist_off), total, _dptr(params), params_stride, _dptr(active), _dptr(out),

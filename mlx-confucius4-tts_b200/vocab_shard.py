@@ -14,7 +14,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import workloads
-from .sampling import SHARD_CANDIDATES, params_tensor
+from .sampling import MAX_SHARDS, SHARD_CANDIDATES, params_tensor
 from .sharding import shard_rows
 
 
@@ -45,13 +45,26 @@ def _device_params(params, active, tensor):
     return params
 
 
+SUB_WIDTH = 8192              # widest sub-shard a rank's candidate launch works
+
+
 def shard_vocab(V: int, rank: int, world: int) -> tuple[int, int]:
     """(first column, width) of `rank`'s contiguous vocabulary shard."""
     return shard_rows(V, rank, world)
 
 
+def sub_shards(width: int, world: int, sub_width: int = SUB_WIDTH) -> int:
+    """Sub-shards of a rank's `width` columns: blocks of at most `sub_width`
+    (so that a wide shard keeps several CTAs per SM), at most
+    C4S_MAX_SHARDS blocks over all ranks, at least 64 columns each."""
+    n = max(1, -(-width // sub_width))
+    n = min(n, max(1, MAX_SHARDS // world), max(1, width // SHARD_CANDIDATES))
+    return n
+
+
 def sample_vocab_sharded(ctx, logits_shard, V: int, hist, hist_off, params, rng, group=None,
-                         active=None, out_ids=None, params_stride: int = 1, cand_out=None):
+                         active=None, out_ids=None, params_stride: int = 1, cand_out=None,
+                         sub_width: int = SUB_WIDTH):
     """One sampling step on this rank's shard of every row.
 
     ``logits_shard`` [B, ld] holds the columns ``shard_vocab(V, rank, world)``
@@ -60,7 +73,10 @@ def sample_vocab_sharded(ctx, logits_shard, V: int, hist, hist_off, params, rng,
     identical on every rank; ``rng`` is advanced identically on every rank.
     ``params`` as a host ROW_PARAMS_DTYPE array is checked first
     (check_shardable: ValueError for a sampled row with top_k outside
-    [1, 64]); as a device tensor it is used unchecked.
+    [1, 64]); as a device tensor it is used unchecked. Each rank computes
+    its shard as ``sub_shards(width, world)`` sub-shards of at most
+    ``sub_width`` columns; the gathered blocks ([world * sub, B, 64],
+    rank-major) are in vocabulary order.
     """
     import torch
     import torch.distributed as dist
@@ -71,15 +87,22 @@ def sample_vocab_sharded(ctx, logits_shard, V: int, hist, hist_off, params, rng,
     B = logits_shard.shape[0]
     dev = logits_shard.device
     params = _device_params(params, active, logits_shard)
-    local = torch.empty((B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
-    ctx.shard_candidates(logits_shard, V, voff, hist, hist_off, params, active=active,
-                         out=local, V_shard=width, params_stride=params_stride)
+    # every rank's width gives the same sub-shard count (widths differ by at most one)
+    nsub = sub_shards(shard_vocab(V, 0, world)[1], world, sub_width)
+    local = torch.empty((nsub, B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
+    if nsub == 1:
+        ctx.shard_candidates(logits_shard, V, voff, hist, hist_off, params, active=active,
+                             out=local[0], V_shard=width, params_stride=params_stride)
+    else:
+        ctx.shard_candidates(logits_shard, V, voff, hist, hist_off, params, active=active,
+                             out=local, V_shard=width, params_stride=params_stride, num_sub=nsub)
     if world > 1:
         if cand_out is None:
-            cand_out = torch.empty((world, B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
-        dist.all_gather_into_tensor(cand_out.view(world * B, SHARD_CANDIDATES), local, group=group)
+            cand_out = torch.empty((world * nsub, B, SHARD_CANDIDATES), dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(cand_out.view(world * nsub * B, SHARD_CANDIDATES),
+                                    local.view(nsub * B, SHARD_CANDIDATES), group=group)
     else:
-        cand_out = local.unsqueeze(0)
+        cand_out = local
     return ctx.merge_candidates(cand_out, V, params, rng, active=active, out_ids=out_ids,
                                 params_stride=params_stride)
 

@@ -44,7 +44,14 @@ class OracleShardContext:
         self.o = oracle
 
     def shard_candidates(self, logits, V, vocab_offset, hist, hist_off, params, active=None,
-                         out=None, V_shard=None, params_stride=1):
+                         out=None, V_shard=None, params_stride=1, num_sub=1):
+        if num_sub > 1:                             # sub-shard s of the shard's columns into out[s]
+            c4s = load_c4s()
+            for s in range(num_sub):
+                so, sw = c4s.vocab_shard.shard_vocab(V_shard, s, num_sub)
+                self.shard_candidates(logits[:, so:so + sw], V, vocab_offset + so, hist, hist_off, params,
+                                      active, out[s], sw, params_stride)
+            return out
         x_all = logits.numpy()
         P = np.frombuffer(params.numpy().tobytes(), dtype=load_c4s().workloads.ROW_PARAMS_DTYPE)
         h = hist.numpy()
@@ -92,7 +99,7 @@ class OracleShardContext:
         return out
 
 
-def _gloo_rank(rank, world, port, V, B, q):
+def _gloo_rank(rank, world, port, V, B, q, sub_width):
     import torch
     import torch.distributed as dist
     sys_path_setup()
@@ -108,7 +115,7 @@ def _gloo_rank(rank, world, port, V, B, q):
         rng = torch.from_numpy(b.rng.view(np.int64).copy())
         ids = c4s.vocab_shard.sample_vocab_sharded(
             OracleShardContext(orc.Oracle()), logits, V, torch.from_numpy(b.hist),
-            torch.from_numpy(b.hist_off), params, rng)
+            torch.from_numpy(b.hist_off), params, rng, sub_width=sub_width)
         q.put((rank, ids.numpy().copy(), rng.numpy().view(np.uint64).copy()))
     finally:
         dist.destroy_process_group()
@@ -161,16 +168,20 @@ def test_candidate_merge_is_exact_against_whole_rows(c4s, oracle):
     assert np.array_equal(rng.numpy().view(np.uint64), ro)
 
 
-def test_gloo_two_ranks_match_whole_rows(oracle):
+@pytest.mark.parametrize("sub_width", [8192, 700])
+def test_gloo_two_ranks_match_whole_rows(oracle, sub_width):
     """world_size 2 over gloo: sample_vocab_sharded's shard bounds, gather
-    layout and merge give every rank the whole-row ids and states."""
+    layout and merge give every rank the whole-row ids and states, each rank's
+    shard in one block or (sub_width 700) as three sub-shards, six blocks."""
     import torch.multiprocessing as mp
     c4s = load_c4s()
-    V, B, world = 4096, 8, 2
+    V, B, world = 4096 + 3, 8, 2
+    assert c4s.vocab_shard.sub_shards(c4s.vocab_shard.shard_vocab(V, 0, world)[1], world, sub_width) == \
+        (1 if sub_width == 8192 else 3)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, V, B, q)) for r in range(world)]
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, V, B, q, sub_width)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=180) for _ in range(world)]
@@ -446,3 +457,40 @@ def test_split_launch_matches_per_shard_calls(sctx):
                               out=per[s], V_shard=width)
     torch.cuda.synchronize()
     assert torch.equal(split, per)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_sub_shards_of_a_rank_match_whole_rows(sctx, oracle, world):
+    """Config 4 as world ranks would run it, on one GPU: each rank's shard as
+    sub-shards of at most 8192 columns (c4s_shard_candidates_sub), the blocks
+    concatenated rank-major as the all-gather lays them out, then the merge:
+    ids and states equal whole-row sampling; each rank's blocks equal one
+    c4s_shard_candidates call per sub-shard."""
+    import torch
+    c4s = load_c4s()
+    vs = c4s.vocab_shard
+    b = c4s.workloads.config4(seed=40 + world, B=128)
+    d = to_dev(b, torch)
+    nsub = vs.sub_shards(vs.shard_vocab(b.V, 0, world)[1], world)
+    assert world * nsub == 8
+    blocks = []
+    for r in range(world):
+        voff, width = vs.shard_vocab(b.V, r, world)
+        x = d["logits"][:, voff:voff + width]
+        sub = sctx.shard_candidates(x, b.V, voff, d["hist"], d["hist_off"], d["params"], V_shard=width,
+                                    num_sub=nsub)
+        for s in range(nsub):
+            so, sw = vs.shard_vocab(width, s, nsub)
+            one = sctx.shard_candidates(d["logits"][:, voff + so:], b.V, voff + so, d["hist"], d["hist_off"],
+                                        d["params"], V_shard=sw)
+            assert torch.equal(sub[s], one)
+        blocks.append(sub)
+    cand = torch.cat(blocks, 0)
+    ids = sctx.merge_candidates(cand, b.V, d["params"], d["rng"])
+    torch.cuda.synchronize()
+    err, _ = sctx.status(reset=True)
+    oid, ro = _oracle(oracle, b)
+    assert err == 0
+    assert np.array_equal(ids.cpu().numpy(), oid)
+    assert np.array_equal(d["rng"].cpu().numpy().view(np.uint64), ro)
