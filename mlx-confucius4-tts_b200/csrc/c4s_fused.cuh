@@ -128,6 +128,7 @@ struct FShared {
   int tslot;                                       // trace builds: the row's slot
   RowJob J;
   LRed R;
+  double tab[64];                                  // exp_tail's 2^(j/64) table, staged once per launch
 };
 
 struct FList {
@@ -274,8 +275,9 @@ __device__ __forceinline__ float list_threshold_w(const RowCtx& rc, int bl) {
 
 // Top-k row: the list of elements >= the maxima threshold (at least k of
 // them, every one that can survive top-k). Returns its length, or -1.
-__device__ __noinline__ int f_topk_list(const RowCtx rc, const float* rb, const FGeo g, FShared& S, FList L,
-                                        unsigned short* gli, int k, bool two, float tm, float t2) {
+__device__ __forceinline__ int f_topk_list_body(const RowCtx& rc, const float* rb, const FGeo& g, FShared& S,
+                                                const FList& L, unsigned short* gli, int k, bool two, float tm,
+                                                float t2) {
   // a warp whose kw-th largest lane maximum (of the two largest per lane when
   // `two`) is finite has >= kw elements >= it, so >= k elements are >= tau,
   // the smallest over the warps (-inf: not enough elements; general path)
@@ -287,6 +289,10 @@ __device__ __noinline__ int f_topk_list(const RowCtx rc, const float* rb, const 
   if (!(tau_lo > -INFINITY)) return -1;
   float unused;
   return f_gather<false>(rb, g, S, L, gli, [&](float x) { return x >= tau_lo; }, &unused);
+}
+__device__ __noinline__ int f_topk_list(const RowCtx rc, const float* rb, const FGeo g, FShared& S, FList L,
+                                        unsigned short* gli, int k, bool two, float tm, float t2) {
+  return f_topk_list_body(rc, rb, g, S, L, gli, k, two, tm, t2);
 }
 
 // Row without top-k (top-p over the whole row, sampling.cpp:42-71): octave
@@ -412,7 +418,7 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
       const float x = f4c(v, c);
       if (x > -INFINITY) {
         const float y = do_t ? div_rn(x, T, rT) : x;
-        if (fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), EXP2_J64);
+        if (fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), S.tab);
       }
     }
   }
@@ -425,6 +431,28 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
   csync();
 }
 
+// Ascending order of the warp's 64 distinct keys (lane l holds positions 2l
+// and 2l+1): each key's rank is the number of smaller keys, counted over
+// all 64 by shuffles (32 independent steps, no compare-exchange chain), and
+// the keys are scattered to their ranks in `buf` (64 u64 of shared memory)
+// and read back in order. Whole warp calls.
+__device__ __forceinline__ void warp_rank_sort2(unsigned long long (&k)[2], unsigned long long* buf) {
+  const int lane = threadIdx.x & 31;
+  int r0 = 0, r1 = 0;
+#pragma unroll 8
+  for (int s = 0; s < 32; ++s) {
+    const unsigned long long o0 = __shfl_sync(FULL, k[0], s), o1 = __shfl_sync(FULL, k[1], s);
+    r0 += (o0 < k[0] ? 1 : 0) + (o1 < k[0] ? 1 : 0);
+    r1 += (o0 < k[1] ? 1 : 0) + (o1 < k[1] ? 1 : 0);
+  }
+  buf[r0] = k[0];
+  buf[r1] = k[1];
+  __syncwarp();
+  k[0] = buf[2 * lane];
+  k[1] = buf[2 * lane + 1];
+  __syncwarp();
+}
+
 // The list job of a list of at most 64 entries, by one warp with the list in
 // registers (lane l holds list positions 2l and 2l+1; positions are in index
 // order): tempered value keys; one ascending register sort of (value key,
@@ -434,9 +462,11 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
 // draw (text2semantic.cpp:150-165) on a prefix scan in index order. Every
 // decision is the one list_job takes; when one of them falls inside its
 // rounding band (or the debug flags force the slow paths) it returns false
-// without writing anything, and the caller runs list_job instead.
-__device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, const float* srow,
-                                         const unsigned short* li, double* pvs) {
+// without writing anything, and the caller runs list_job instead. `tab` is
+// exp_tail's table in shared memory; pvs holds at least 128 doubles (the
+// sort's scatter buffer follows the 64 probabilities).
+__device__ __forceinline__ bool f_short_job_body(const Args& a, int row, RowJob& J, const float* srow,
+                                                 const unsigned short* li, double* pvs, const double* tab) {
   const int lane = threadIdx.x & 31;
   const int n = J.n, k = J.k;
   const bool k0 = J.kind == JOB_K0;
@@ -462,11 +492,15 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
   }
   const unsigned vmin = __reduce_min_sync(FULL, lmin), vmax = __reduce_max_sync(FULL, lmax);
   if (k0 && J.ykex >= vmin) return false;         // list_job hands such a row to the general path
-  // ascending (value key, position); padding (key 0) sorts first
+  // ascending (value key, position); padding (key = its position, below
+  // every element's key: value keys are >= 1) sorts first
   unsigned long long sk[2];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) sk[j] = 2 * lane + j < n ? ((unsigned long long)vkey[j] << 32) | (unsigned)(2 * lane + j) : 0ull;
-  warp_sort_regs<2>(sk);
+  for (int j = 0; j < 2; ++j) {
+    const unsigned p = 2 * lane + j;
+    sk[j] = (int)p < n ? ((unsigned long long)vkey[j] << 32) | p : (unsigned long long)p;
+  }
+  warp_rank_sort2(sk, reinterpret_cast<unsigned long long*>(pvs + 64));
   auto at = [&](int pos) {                          // sorted key at position pos (uniform)
     return __shfl_sync(FULL, (pos & 1) ? sk[1] : sk[0], pos >> 1);
   };
@@ -480,9 +514,10 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const unsigned v = (unsigned)(sk[j] >> 32);
-    const bool sv = sk[j] != 0ull && v >= tk;
-    pr[j] = sv ? exp_tail(__fsub_rn(fkey_inv(v), m_y), EXP2_J64) : 0.0;
-    if (sk[j] != 0ull) pvs[(int)(sk[j] & 0xffffffffull)] = pr[j];
+    const bool real = v != 0u;                      // not padding
+    const bool sv = real && v >= tk;
+    pr[j] = sv ? exp_tail(__fsub_rn(fkey_inv(v), m_y), tab) : 0.0;
+    if (real) pvs[(int)(sk[j] & 0xffffffffull)] = pr[j];
     nl += sv ? 1 : 0;
   }
   const double ps = warp_sum_d(pr[0] + pr[1]);
@@ -577,17 +612,38 @@ __device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, cons
   return true;
 }
 
-// The list job on a short list, by warp 0 (the other warps wait at the barrier).
-__device__ __noinline__ void f_list_warp(const Args& a, int row, const float* srow, FShared& S, FList L,
-                                         unsigned long long* sb, bool refine) {
+__device__ __noinline__ bool f_short_job(const Args& a, int row, RowJob& J, const float* srow,
+                                         const unsigned short* li, double* pvs, const double* tab) {
+  return f_short_job_body(a, row, J, srow, li, pvs, tab);
+}
+
+// list_job on a list of at most 256 entries, by one warp (out of line).
+__device__ __noinline__ bool f_warp_list_job(const Args& a, int row, const float* srow, FShared& S, FList L,
+                                             unsigned long long* sb, bool refine) {
+  return list_job<false, true, RowKeys>(a, row, S.J, RowKeys{srow, L.li}, sb, L.vk, L.pv, L.hist, refine, S.R,
+                                        nullptr);
+}
+
+// The list job on a short list, by warp 0 (the other warps wait at the
+// barrier). INL: the register-resident short job inlined into the caller
+// (the small-batch kernel, which has the registers for it).
+template <bool INL>
+__device__ __forceinline__ void f_list_warp_body(const Args& a, int row, const float* srow, FShared& S,
+                                                 const FList& L, unsigned long long* sb, bool refine) {
   if ((threadIdx.x >> 5) == 0) {
-    bool ok = !refine && f_short_job(a, row, S.J, srow, L.li, L.pv);
-    if (!ok)
-      ok = list_job<false, true, RowKeys>(a, row, S.J, RowKeys{srow, L.li}, sb, L.vk, L.pv, L.hist, refine, S.R,
-                                          nullptr);
+    bool ok = false;
+    if (!refine) {
+      if constexpr (INL) ok = f_short_job_body(a, row, S.J, srow, L.li, L.pv, S.tab);
+      else ok = f_short_job(a, row, S.J, srow, L.li, L.pv, S.tab);
+    }
+    if (!ok) ok = f_warp_list_job(a, row, srow, S, L, sb, refine);
     if (threadIdx.x == 0) S.lres = ok ? 1 : 0;
   }
   csync();
+}
+__device__ __noinline__ void f_list_warp(const Args& a, int row, const float* srow, FShared& S, FList L,
+                                         unsigned long long* sb, bool refine) {
+  f_list_warp_body<false>(a, row, srow, S, L, sb, refine);
 }
 
 // The list job on a long list, by the whole CTA; li/vk/pv in shared memory
@@ -638,8 +694,9 @@ enum { F_DONE = 0, F_GENERAL = 1 };
 
 // One staged, penalised row on the fast path. Returns F_DONE (id, state and
 // processed logits written) or F_GENERAL.
-__device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, const float* rb, const FGeo g,
-                                  FShared& S, FList L) {
+template <bool INL>
+__device__ __forceinline__ int f_row_body(const Args& a, int row, const MetaSlot& M, const float* rb, const FGeo& g,
+                                          FShared& S, const FList& L) {
   const int V = a.V;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const c4s_row_params P = M.P;
@@ -735,7 +792,9 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
   unsigned short* gli = reinterpret_cast<unsigned short*>(slab);
   unsigned* gvk = reinterpret_cast<unsigned*>(slab + F_GL_VK);
   double* gpv = reinterpret_cast<double*>(slab + F_GL_PV);
-  const int ng = do_k ? f_topk_list(rc, rb, g, S, L, gli, k, two, tm, t2) : f_k0_list(a, rc, rb, g, S, L, gli);
+  int ng;
+  if constexpr (INL) ng = do_k ? f_topk_list_body(rc, rb, g, S, L, gli, k, two, tm, t2) : f_k0_list(a, rc, rb, g, S, L, gli);
+  else ng = do_k ? f_topk_list(rc, rb, g, S, L, gli, k, two, tm, t2) : f_k0_list(a, rc, rb, g, S, L, gli);
   if (ng < 0) return F_GENERAL;
   if (tid == 0) {
     fill_job(S.J, rc, do_k ? JOB_TOPK : JOB_K0, ng, do_k ? k : 0);
@@ -753,7 +812,10 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
   const float* srow = rb + g.shift;
   for (int pass = 0; pass < 2; ++pass) {
     const bool refine = pass == 1;
-    if (ng <= 256) f_list_warp(a, row, srow, S, L, sb, refine);
+    if (ng <= 256) {
+      if constexpr (INL) f_list_warp_body<true>(a, row, srow, S, L, sb, refine);
+      else f_list_warp(a, row, srow, S, L, sb, refine);
+    }
     else if (ng <= FLC) f_list_cta(a, row, srow, S, L.li, L.vk, L.pv, L.hist, sb, refine);
     else f_list_cta(a, row, srow, S, gli, gvk, gpv, L.hist, sb, refine);
     C4S_TR(S.tslot, 5 + pass);
@@ -765,11 +827,19 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
   csync();
   return F_DONE;
 }
+__device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, const float* rb, const FGeo g,
+                                  FShared& S, FList L) {
+  return f_row_body<false>(a, row, M, rb, g, S, L);
+}
 
 // Fused persistent kernel: rows handed out dynamically (the first G
-// statically), each finished in its CTA.
-constexpr int FUSED_MINB = 3;                      // resident CTAs per SM the register budget allows
-__global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
+// statically), each finished in its CTA. Two forms: MINB = 3 resident CTAs
+// per SM with the per-row paths out of line (batches above one row per SM),
+// and MINB = 1, one CTA per SM with every register it needs and the common
+// path (top-k row, short list) inlined: no spills and no call frames on the
+// latency-bound path of small batches (B <= SMs, B = 1 among them).
+template <int MINB, bool INL>
+__global__ void __launch_bounds__(NT, MINB) fused_kernel_t(Args a) {
   extern __shared__ __align__(128) unsigned char fsm[];
   __shared__ FShared S;
   __shared__ Shared GS;                             // general path
@@ -787,6 +857,7 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
   const int G = gridDim.x;
   unsigned* ctr = a.defer_cnt;                     // [0] row tickets, [1] CTAs done
 
+  if (tid < 64) S.tab[tid] = EXP2_J64[tid];
   if (tid == 0) {
     mbar_init(&S.bar, 1);
     mbar_init(&GS.bar, 1);
@@ -941,7 +1012,10 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
       }
       C4S_TR(j, 2);
       const FGeo g = fgeo(V, sg.shift);
-      if (f_row(sa, row, cur, rb, g, S, L) == F_GENERAL) {
+      int fr;
+      if constexpr (INL) fr = f_row_body<true>(sa, row, cur, rb, g, S, L);
+      else fr = f_row(sa, row, cur, rb, g, S, L);
+      if (fr == F_GENERAL) {
         C4S_TR_INFO(j, 3);
         csync();
         if (!general_row(sa, row, reinterpret_cast<float*>(fsm + GL.row), reinterpret_cast<unsigned*>(fsm + GL.bitmap),
@@ -984,5 +1058,10 @@ __global__ void __launch_bounds__(NT, FUSED_MINB) fused_kernel(Args a) {
     }
   }
 }
+
+// the batched form (B > SMs) and the small-batch form
+constexpr int FUSED_MINB = 3;
+inline constexpr auto fused_kernel = fused_kernel_t<FUSED_MINB, false>;
+inline constexpr auto fused_small_kernel = fused_kernel_t<1, true>;
 
 }  // namespace c4s
