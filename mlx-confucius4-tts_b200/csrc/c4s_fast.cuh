@@ -162,8 +162,10 @@ __device__ __forceinline__ void defer_row(const Args& a, int row) {
 // List kernel: one warp per row
 // ===========================================================================
 
-// Reduction scratch of a list job run by a whole CTA.
+// Reduction scratch of a list job run by a whole CTA, and exp_tail's table
+// (staged into shared memory once per launch by every kernel that runs list jobs).
 struct LRed {
+  double tab[64];
   double d[NWARP];
   double d3[NWARP][3];
   unsigned long long q[NWARP];
@@ -511,59 +513,110 @@ __device__ __forceinline__ unsigned radix_kth(const unsigned* __restrict__ vk, i
   return prefix;
 }
 
-// The largest v with base + sum(pv[e] : vk[e] < v) <= Th (v = prefix if
-// none), by bisection over the key bits below b0 under `prefix`; base is the
-// mass below the searched range. One pass over the staged list per bit (no
-// atomics: contended 64-bit shared-memory adds are slow). The search only has
-// to land on the crossing value, which the caller checks with double sums and
-// their error band.
-template <bool CTA>
-__device__ __forceinline__ unsigned bisect_mass(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
-                                                unsigned prefix, int b0, double base, double Th, LRed& R) {
-  using G = LG<CTA>;
+// The same search by a whole CTA (long lists), by bisection two bits a step:
+// three thresholds summed in one pass over the staged list and one pair of
+// barriers per step (no atomics: on thousands of keys contended
+// shared-memory adds cost more than the extra passes).
+__device__ __forceinline__ unsigned bisect_mass_cta(const unsigned* __restrict__ vk, const double* __restrict__ pv,
+                                                    int n, unsigned prefix, int b0, double base, double Th, LRed& R) {
+  using G = LG<true>;
   unsigned v = prefix;
-  if constexpr (CTA) {
-    // two bits per step: three thresholds, one pair of CTA barriers
-    for (int b = b0; b >= 0; b -= 2) {
-      const int lo = b >= 1 ? b - 1 : 0;
-      const unsigned c0 = v | (1u << lo), c1 = v | (2u << lo), c2 = v | (3u << lo);
-      double g0 = 0.0, g1 = 0.0, g2 = 0.0;
-      for (int e = G::rank(); e < n; e += G::N) {
-        const unsigned x = vk[e];
-        const double p = pv[e];
-        g0 += x < c0 ? p : 0.0;
-        g1 += x < c1 ? p : 0.0;
-        g2 += x < c2 ? p : 0.0;
-      }
-      G::sum3(g0, g1, g2, R);
-      if (lo < b && base + g2 <= Th) v = c2;
-      else if (lo < b && base + g1 <= Th) v = c1;
-      else if (base + g0 <= Th) v = c0;
+  for (int b = b0; b >= 0; b -= 2) {
+    const int lo = b >= 1 ? b - 1 : 0;
+    const unsigned c0 = v | (1u << lo), c1 = v | (2u << lo), c2 = v | (3u << lo);
+    double g0 = 0.0, g1 = 0.0, g2 = 0.0;
+    for (int e = G::rank(); e < n; e += G::N) {
+      const unsigned x = vk[e];
+      const double p = pv[e];
+      g0 += x < c0 ? p : 0.0;
+      g1 += x < c1 ? p : 0.0;
+      g2 += x < c2 ? p : 0.0;
     }
-    return v;
-  } else {
-    for (int b = b0; b >= 0; --b) {
-      const unsigned c = v | (1u << b);
-      double g0 = 0.0, g1 = 0.0;
-      int e = G::rank();
-      for (; e + G::N < n; e += 2 * G::N) {
-        g0 += vk[e] < c ? pv[e] : 0.0;
-        g1 += vk[e + G::N] < c ? pv[e + G::N] : 0.0;
-      }
-      if (e < n) g0 += vk[e] < c ? pv[e] : 0.0;
-      if (base + G::sum(g0 + g1, R) <= Th) v = c;
-    }
-    return v;
+    G::sum3(g0, g1, g2, R);
+    if (lo < b && base + g2 <= Th) v = c2;
+    else if (lo < b && base + g1 <= Th) v = c1;
+    else if (base + g0 <= Th) v = c0;
   }
+  return v;
+}
+
+// Top-p search of a list job over the value keys that share `prefix` above
+// bit b0: the largest key c whose mass below, base + G(c) (G(c) = sum of p
+// over keys < c; removed candidates have p = 0), is <= Th -- the value of the
+// crossing element -- found DB bits at a time from b0 down. A pass sums the
+// masses of the keys that share the prefix found so far into 2^DB bins by
+// their next digit (double atomics in shared memory `hist`) and takes the
+// largest digit whose mass below is <= Th. The bins' sums are re-associated;
+// the caller checks the group the search ends on against its own sums and
+// their rounding band, as it checks any search. Whole group calls.
+template <bool CTA, int DB>
+__device__ __forceinline__ unsigned radix_mass(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
+                                               unsigned prefix, int b0, double base, double Th,
+                                               double* __restrict__ hist, LRed& R) {
+  using G = LG<CTA>;
+  constexpr int NB = 1 << DB, PL = NB / 32;
+  const int lane = threadIdx.x & 31;
+  unsigned v = prefix;
+  double below = base;
+  for (int hi = b0; hi >= 0;) {
+    const int w = hi + 1 < DB ? hi + 1 : DB;
+    const int lo = hi - w + 1;
+    const unsigned pmask = hi >= 31 ? 0u : ~((2u << hi) - 1u);
+    const unsigned dmask = (1u << w) - 1u;          // the digit: bits lo..hi
+    for (int i = G::rank(); i < NB; i += G::N) hist[i] = 0.0;
+    G::sync();
+    for (int e = G::rank(); e < n; e += G::N) {
+      const unsigned x = vk[e];
+      const double p = pv[e];
+      if ((x & pmask) == v && p > 0.0) atomicAdd(&hist[(x >> lo) & dmask], p);
+    }
+    G::sync();
+    if (!CTA || threadIdx.x < 32) {
+      double c[PL], sl = 0.0;
+#pragma unroll
+      for (int j = 0; j < PL; ++j) { c[j] = hist[PL * lane + j]; sl += c[j]; }
+      double incl = sl;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += y;
+      }
+      // the bins whose mass below is <= Th are a prefix [0, D] of the digits
+      double run = below + (incl - sl), ex = below;
+      int cnt = 0;
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        if (run <= Th) { ++cnt; ex = run; }
+        run += c[j];
+      }
+      int d = __reduce_add_sync(FULL, cnt) - 1;    // bins above the digit's range are empty
+      d = d < 0 ? 0 : d > (int)dmask ? (int)dmask : d;
+      const double exd = __shfl_sync(FULL, ex, d / PL);
+      if (CTA) {
+        if (threadIdx.x == 0) { R.e = d; R.x = exd; }
+      } else {
+        v |= (unsigned)d << lo;
+        below = exd;
+      }
+    }
+    if (CTA) {
+      csync();
+      v |= (unsigned)R.e << lo;
+      below = R.x;
+      csync();
+    }
+    hi = lo - 1;
+  }
+  return v;
 }
 
 // From a value key c of the list, steps to the neighbouring value group
 // (next survivor key below or above) until it reaches the group whose mass
 // range [base + G(v), base + G(v) + M(v)) holds Th, G(v) being the mass of
-// the survivors below v and M(v) that of the group v: the group bisect_mass
-// ends on. A refinement whose exact tail moved the crossing by little gets
+// the survivors below v and M(v) that of the group v: the group the searches
+// (radix_mass, bisect_mass_cta) end on. A refinement whose exact tail moved the crossing by little gets
 // there in a pass or two; false after 8 steps or past either end of the list
-// (the caller then bisects). Rounding differences against bisect_mass's sums
+// (the caller then searches). Rounding differences against the searches' sums
 // are harmless: the caller's band check accepts only a crossing that every
 // summation order agrees on.
 template <bool CTA>
@@ -702,7 +755,9 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
     const unsigned v = vk[e];
     double p = 0.0;
     if (v >= tk) {
-      p = exp((double)__fsub_rn(fkey_inv(v), m_y));    // prob(): the reference's exp((double)(y - max))
+      // the reference's exp((double)(y - max)) within 2^-51 (Tang's exp_tail);
+      // the bands below cover it, and the exact fallbacks use prob()
+      p = exp_tail(__fsub_rn(fkey_inv(v), m_y), R.tab);
       ++ns;
       smin = v < smin ? v : smin;
     }
@@ -731,17 +786,14 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
     for (int e = r0; e < n; e += GN)
       if (vk[e] >= tk && pv[e] > 0.0) mk0 = ykey(e) < mk0 ? ykey(e) : mk0;
     kst = G::qmin(mk0, R);
-  } else if (!CTA && (ns <= 128 || (ns <= 256 && (INL || n <= LW_CAP / 2)))) {
+  } else if (!CTA && ns <= 128) {
     // few survivors: sort them in registers and find the crossing on a prefix
-    // scan; 256 keys need 2 KB: the fused kernel's histogram area, or the list
-    // kernel's unused upper half of the probability area
+    // scan (the 128 keys' buffer is the 1 KB histogram area)
     const double Th = thr * St;
     int pos = 0;
     double before = 0.0, cur = 0.0;
-    unsigned long long* cbuf = (INL || ns <= 128) ? hist : reinterpret_cast<unsigned long long*>(pv + LW_CAP / 2);
-    const bool hit = ns <= 64    ? warp_sorted_crossing<2>(vk, pv, n, tk, ns, tail, Th, cbuf, &pos, &before, &cur)
-                     : ns <= 128 ? warp_sorted_crossing<4>(vk, pv, n, tk, ns, tail, Th, cbuf, &pos, &before, &cur)
-                                 : warp_sorted_crossing<8>(vk, pv, n, tk, ns, tail, Th, cbuf, &pos, &before, &cur);
+    const bool hit = ns <= 64 ? warp_sorted_crossing<2>(vk, pv, n, tk, ns, tail, Th, hist, &pos, &before, &cur)
+                              : warp_sorted_crossing<4>(vk, pv, n, tk, ns, tail, Th, hist, &pos, &before, &cur);
     if (hit) {
       const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
       kst = ykey(pos);
@@ -760,28 +812,9 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
     unsigned v = b0 < 0 ? smin32 : (b0 >= 31 ? 0u : (vmax32 & ~((2u << b0) - 1u)));
     // a refinement starts from the first pass's crossing and bisects only if that fails
     const bool near = refine && J.vcross != 0u && step_to_crossing<CTA>(vk, pv, n, tk, tail, Th, J.vcross, &v, R);
-    if (near) {
-    } else if (!CTA && ns < n && n <= LW_CAP / 2) {
-      // one warp: bisect over the survivors only, gathered into the unused
-      // upper half of the warp's staging area (top-k zeroes the others' mass)
-      unsigned* cvk = vk + LW_CAP / 2;
-      double* cpv = pv + LW_CAP / 2;
-      int cb = 0;
-      for (int e0 = 0; e0 < n; e0 += 32) {
-        const int e = e0 + r0;
-        const bool sv = e < n && vk[e] >= tk;
-        const unsigned bal = __ballot_sync(FULL, sv);
-        if (sv) {
-          const int o = cb + __popc(bal & ((1u << r0) - 1u));
-          cvk[o] = vk[e];
-          cpv[o] = pv[e];
-        }
-        cb += __popc(bal);
-      }
-      __syncwarp();
-      v = bisect_mass<CTA>(cvk, cpv, ns, v, b0, tail, Th, R);
-    } else {
-      v = bisect_mass<CTA>(vk, pv, n, v, b0, tail, Th, R);
+    if (!near) {
+      if constexpr (CTA) v = bisect_mass_cta(vk, pv, n, v, b0, tail, Th, R);
+      else v = radix_mass<false, 7>(vk, pv, n, v, b0, tail, Th, reinterpret_cast<double*>(hist), R);
     }
     double Gs = 0.0, Mg = 0.0;
     int cg = 0;
@@ -955,6 +988,7 @@ constexpr size_t LW_VK = 0, LW_PV = (size_t)LW_CAP * 4, LW_HIST = LW_PV + (size_
 constexpr size_t LW_BYTES = LW_HIST + 128 * 8;            // per warp
 static_assert(LW_BYTES - LW_HIST >= 256 * sizeof(unsigned), "radix histogram");
 static_assert(LW_BYTES - LW_HIST >= 32 * 4 * sizeof(unsigned long long), "sorted-crossing keys");
+static_assert(LW_BYTES - LW_HIST >= 128 * sizeof(double), "a warp's top-p search bins");
 constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)LCAP * 8;
 constexpr size_t LIST_SMEM_W = (size_t)LIST_WARPS * LW_BYTES, LIST_SMEM_B = LB_HIST + 256 * 8;
 constexpr size_t LIST_SMEM = LIST_SMEM_W > LIST_SMEM_B ? LIST_SMEM_W : LIST_SMEM_B;   // warps' areas / one long list
@@ -1000,7 +1034,8 @@ __device__ __forceinline__ Staged stage_row(const float* g, int V, float* rowbuf
 __device__ const double EXP2_J64[64] = C4S_EXP2_J64_TABLE;   // exp_tail's table
 
 // A row without top-k whose top-p crossing fell inside the band of its
-// estimated tail, in the list kernel (whole CTA): the exact tail mass (sum of
+// estimated tail, or whose list is long (a whole CTA's), in the list kernel
+// (whole CTA): the exact tail mass (sum of
 // exp((double)(y - m_y)) over every element below the list, each penalised
 // and tempered as the reference does, re-associated: its rounding is inside
 // the list's double-sum band; each term by exp_tail, within 2^-51 of the
@@ -1080,7 +1115,7 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
     float x = srow[i];
     if (pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
     const float y = do_t ? div_rn(x, T, rT) : x;
-    if (x > -INFINITY && fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), EXP2_J64);
+    if (x > -INFINITY && fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), R.tab);
   }
   const double tail = LG<true>::sum(t, R);
   if (tid == 0) {
@@ -1111,6 +1146,7 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
   __shared__ Args sa;                               // for refine_in_list (no local copy)
   __shared__ unsigned long long lbar;               // refinements' bulk row copies
   __shared__ unsigned lst[2];                       // its phase; set after a wait gave up
+  if (threadIdx.x < 64) R.tab[threadIdx.x] = EXP2_J64[threadIdx.x];
   if (threadIdx.x == 0) {
     rq[0] = 0;
     sa = a;
@@ -1145,7 +1181,10 @@ __global__ void __launch_bounds__(32 * LIST_WARPS, 2) list_kernel(Args a) {
       if (t >= (int)nbig) return false;
       const int r = a.big_rows[t];
       const size_t o = (size_t)r * LCAP;
-      list_job<true>(a, r, a.jobs[r], GlobalKeys{a.lkeys + o}, a.lsb + o, bvk, bpv, bh, false, R, rq);
+      // a long list of a row without top-k gets its exact tail first: its
+      // one pass is then final (no refinement behind it on the critical path)
+      if (a.jobs[r].kind == JOB_K0) refine_in_list(sa, r, bm, bvk, bpv, bh, R, &lbar, lst);
+      else list_job<true>(a, r, a.jobs[r], GlobalKeys{a.lkeys + o}, a.lsb + o, bvk, bpv, bh, false, R, rq);
     }
   };
   cta_work();

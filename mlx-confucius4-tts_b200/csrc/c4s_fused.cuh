@@ -64,6 +64,7 @@ static_assert(FL_VK % 16 == 0 && FL_PV % 16 == 0 && FL_HIST % 16 == 0, "aligned 
 static_assert((size_t)NWARP * F_WSTRIDE * 4 <= (size_t)FLC * 12, "octave bins fit in the key/probability arrays");
 static_assert(FLC <= LW_CAP && FLC <= LCAP, "a list the warp job takes fits its staging");
 static_assert(((F_MAXV + 31) / 32) * 4 <= 2048, "penalty bitmap fits the histogram area");
+static_assert(128 * sizeof(double) <= 2048, "a warp list job's top-p search bins fit the histogram area");
 // The CTA's list slab in global memory (lists of FLC..LCAP entries): indices,
 // value keys, probabilities; F_SLAB_BYTES must fit one scratch stride.
 constexpr size_t F_GL_VK = (size_t)LCAP * 2;
@@ -128,7 +129,6 @@ struct FShared {
   int tslot;                                       // trace builds: the row's slot
   RowJob J;
   LRed R;
-  double tab[64];                                  // exp_tail's 2^(j/64) table, staged once per launch
 };
 
 struct FList {
@@ -418,7 +418,7 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
       const float x = f4c(v, c);
       if (x > -INFINITY) {
         const float y = do_t ? div_rn(x, T, rT) : x;
-        if (fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), S.tab);
+        if (fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), S.R.tab);
       }
     }
   }
@@ -633,8 +633,8 @@ __device__ __forceinline__ void f_list_warp_body(const Args& a, int row, const f
   if ((threadIdx.x >> 5) == 0) {
     bool ok = false;
     if (!refine) {
-      if constexpr (INL) ok = f_short_job_body(a, row, S.J, srow, L.li, L.pv, S.tab);
-      else ok = f_short_job(a, row, S.J, srow, L.li, L.pv, S.tab);
+      if constexpr (INL) ok = f_short_job_body(a, row, S.J, srow, L.li, L.pv, S.R.tab);
+      else ok = f_short_job(a, row, S.J, srow, L.li, L.pv, S.R.tab);
     }
     if (!ok) ok = f_warp_list_job(a, row, srow, S, L, sb, refine);
     if (threadIdx.x == 0) S.lres = ok ? 1 : 0;
@@ -857,7 +857,7 @@ __global__ void __launch_bounds__(NT, MINB) fused_kernel_t(Args a) {
   const int G = gridDim.x;
   unsigned* ctr = a.defer_cnt;                     // [0] row tickets, [1] CTAs done
 
-  if (tid < 64) S.tab[tid] = EXP2_J64[tid];
+  if (tid < 64) S.R.tab[tid] = EXP2_J64[tid];
   if (tid == 0) {
     mbar_init(&S.bar, 1);
     mbar_init(&GS.bar, 1);
