@@ -168,6 +168,7 @@ struct LRed {
   double tab[64];
   double d[NWARP];
   double d3[NWARP][3];
+  unsigned long long q3[NWARP][3];
   unsigned long long q[NWARP];
   int i[NWARP];
   int e;
@@ -513,29 +514,52 @@ __device__ __forceinline__ unsigned radix_kth(const unsigned* __restrict__ vk, i
   return prefix;
 }
 
+// Fixed-point masses of the searches: p (<= 1) in units of 2^-48, truncated
+// (the sums of up to LCAP of them stay below 2^62). Integer sums have none of
+// the long dependent latency of double adds; the error, below one unit per
+// element, only moves the search, which the caller checks.
+constexpr double MASS_Q = 0x1p48;
+static_assert((double)LCAP * MASS_Q < 0x1p62, "fixed-point masses of a list cannot overflow");
+__device__ __forceinline__ unsigned long long mass_q(double p) { return __double2ull_rz(p * MASS_Q); }
+
 // The same search by a whole CTA (long lists), by bisection two bits a step:
 // three thresholds summed in one pass over the staged list and one pair of
 // barriers per step (no atomics: on thousands of keys contended
 // shared-memory adds cost more than the extra passes).
 __device__ __forceinline__ unsigned bisect_mass_cta(const unsigned* __restrict__ vk, const double* __restrict__ pv,
                                                     int n, unsigned prefix, int b0, double base, double Th, LRed& R) {
-  using G = LG<true>;
   unsigned v = prefix;
+  const double thq = (Th - base) * MASS_Q;          // the mass allowed below the crossing
   for (int b = b0; b >= 0; b -= 2) {
     const int lo = b >= 1 ? b - 1 : 0;
     const unsigned c0 = v | (1u << lo), c1 = v | (2u << lo), c2 = v | (3u << lo);
-    double g0 = 0.0, g1 = 0.0, g2 = 0.0;
-    for (int e = G::rank(); e < n; e += G::N) {
+    unsigned long long g0 = 0ull, g1 = 0ull, g2 = 0ull;
+    for (int e = threadIdx.x; e < n; e += NT) {
       const unsigned x = vk[e];
-      const double p = pv[e];
-      g0 += x < c0 ? p : 0.0;
-      g1 += x < c1 ? p : 0.0;
-      g2 += x < c2 ? p : 0.0;
+      const unsigned long long q = mass_q(pv[e]);
+      g0 += x < c0 ? q : 0ull;
+      g1 += x < c1 ? q : 0ull;
+      g2 += x < c2 ? q : 0ull;
     }
-    G::sum3(g0, g1, g2, R);
-    if (lo < b && base + g2 <= Th) v = c2;
-    else if (lo < b && base + g1 <= Th) v = c1;
-    else if (base + g0 <= Th) v = c0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      g0 += __shfl_xor_sync(FULL, g0, o);
+      g1 += __shfl_xor_sync(FULL, g1, o);
+      g2 += __shfl_xor_sync(FULL, g2, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      R.q3[threadIdx.x >> 5][0] = g0;
+      R.q3[threadIdx.x >> 5][1] = g1;
+      R.q3[threadIdx.x >> 5][2] = g2;
+    }
+    csync();
+    g0 = g1 = g2 = 0ull;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) { g0 += R.q3[w][0]; g1 += R.q3[w][1]; g2 += R.q3[w][2]; }
+    csync();
+    if (lo < b && (double)g2 <= thq) v = c2;
+    else if (lo < b && (double)g1 <= thq) v = c1;
+    else if ((double)g0 <= thq) v = c0;
   }
   return v;
 }
@@ -545,55 +569,57 @@ __device__ __forceinline__ unsigned bisect_mass_cta(const unsigned* __restrict__
 // over keys < c; removed candidates have p = 0), is <= Th -- the value of the
 // crossing element -- found DB bits at a time from b0 down. A pass sums the
 // masses of the keys that share the prefix found so far into 2^DB bins by
-// their next digit (double atomics in shared memory `hist`) and takes the
-// largest digit whose mass below is <= Th. The bins' sums are re-associated;
-// the caller checks the group the search ends on against its own sums and
-// their rounding band, as it checks any search. Whole group calls.
+// their next digit (64-bit integer atomics in shared memory `hist`) and takes the
+// largest digit whose mass below is <= Th. The bins hold fixed-point masses
+// (mass_q); the caller checks the group the search ends on against its own
+// double sums and their rounding band, as it checks any search. Whole group
+// calls.
 template <bool CTA, int DB>
 __device__ __forceinline__ unsigned radix_mass(const unsigned* __restrict__ vk, const double* __restrict__ pv, int n,
                                                unsigned prefix, int b0, double base, double Th,
-                                               double* __restrict__ hist, LRed& R) {
+                                               unsigned long long* __restrict__ hist, LRed& R) {
   using G = LG<CTA>;
   constexpr int NB = 1 << DB, PL = NB / 32;
   const int lane = threadIdx.x & 31;
   unsigned v = prefix;
-  double below = base;
+  const double thq = (Th - base) * MASS_Q;          // the mass allowed below the crossing
+  unsigned long long below = 0ull;                  // fixed-point mass below the prefix's range
   for (int hi = b0; hi >= 0;) {
     const int w = hi + 1 < DB ? hi + 1 : DB;
     const int lo = hi - w + 1;
     const unsigned pmask = hi >= 31 ? 0u : ~((2u << hi) - 1u);
     const unsigned dmask = (1u << w) - 1u;          // the digit: bits lo..hi
-    for (int i = G::rank(); i < NB; i += G::N) hist[i] = 0.0;
+    for (int i = G::rank(); i < NB; i += G::N) hist[i] = 0ull;
     G::sync();
     for (int e = G::rank(); e < n; e += G::N) {
       const unsigned x = vk[e];
-      const double p = pv[e];
-      if ((x & pmask) == v && p > 0.0) atomicAdd(&hist[(x >> lo) & dmask], p);
+      const unsigned long long q = mass_q(pv[e]);
+      if ((x & pmask) == v && q != 0ull) atomicAdd(&hist[(x >> lo) & dmask], q);
     }
     G::sync();
     if (!CTA || threadIdx.x < 32) {
-      double c[PL], sl = 0.0;
+      unsigned long long c[PL], sl = 0ull;
 #pragma unroll
       for (int j = 0; j < PL; ++j) { c[j] = hist[PL * lane + j]; sl += c[j]; }
-      double incl = sl;
+      unsigned long long incl = sl;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const double y = __shfl_up_sync(FULL, incl, o);
+        const unsigned long long y = __shfl_up_sync(FULL, incl, o);
         if (lane >= o) incl += y;
       }
-      // the bins whose mass below is <= Th are a prefix [0, D] of the digits
-      double run = below + (incl - sl), ex = below;
+      // the bins whose mass below is within the budget are a prefix [0, D] of the digits
+      unsigned long long run = below + (incl - sl), ex = below;
       int cnt = 0;
 #pragma unroll
       for (int j = 0; j < PL; ++j) {
-        if (run <= Th) { ++cnt; ex = run; }
+        if ((double)run <= thq) { ++cnt; ex = run; }
         run += c[j];
       }
       int d = __reduce_add_sync(FULL, cnt) - 1;    // bins above the digit's range are empty
       d = d < 0 ? 0 : d > (int)dmask ? (int)dmask : d;
-      const double exd = __shfl_sync(FULL, ex, d / PL);
+      const unsigned long long exd = __shfl_sync(FULL, ex, d / PL);
       if (CTA) {
-        if (threadIdx.x == 0) { R.e = d; R.x = exd; }
+        if (threadIdx.x == 0) { R.e = d; R.q[0] = exd; }
       } else {
         v |= (unsigned)d << lo;
         below = exd;
@@ -602,7 +628,7 @@ __device__ __forceinline__ unsigned radix_mass(const unsigned* __restrict__ vk, 
     if (CTA) {
       csync();
       v |= (unsigned)R.e << lo;
-      below = R.x;
+      below = R.q[0];
       csync();
     }
     hi = lo - 1;
@@ -710,6 +736,8 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
   const bool do_t = T != 1.0f;
   const float rT = do_t ? __frcp_rn(T) : 1.0f;
   unsigned long long vmin = ~0ull, vmax = 0ull;
+  unsigned long long redo = 0ull;
+  static_assert((LCAP + NT - 1) / NT <= 64 && (LW_CAP + 31) / 32 <= 64, "a member's entries fit the redo mask");
   for (int e0 = r0; e0 < n; e0 += 8 * GN) {
     unsigned v[8];
 #pragma unroll
@@ -722,12 +750,25 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
       const int e = e0 + q * GN;
       if (e < n) {
         const float x = fkey_inv(v[q]);
-        const unsigned y = fkey(do_t ? div_rn(x, T, rT) : x);
-        vk[e] = y;
-        vmin = y < vmin ? y : vmin;
-        vmax = y > vmax ? y : vmax;
+        bool ok = true;
+        const unsigned y = fkey(do_t ? div_rn_try(x, T, rT, ok) : x);
+        if (ok) {
+          vk[e] = y;
+          vmin = y < vmin ? y : vmin;
+          vmax = y > vmax ? y : vmax;
+        } else {
+          redo |= 1ull << ((e - r0) / GN);
+        }
       }
     }
+  }
+  // quotients div_rn_try could not prove (bit j: entry r0 + j GN)
+  for (; redo; redo &= redo - 1ull) {
+    const int e = r0 + (__ffsll(redo) - 1) * GN;
+    const unsigned y = fkey(div_call(fkey_inv(keys.val(e)), T));
+    vk[e] = y;
+    vmin = y < vmin ? y : vmin;
+    vmax = y > vmax ? y : vmax;
   }
   vmin = G::qmin(vmin, R);
   vmax = G::qmax(vmax, R);
@@ -814,7 +855,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
     const bool near = refine && J.vcross != 0u && step_to_crossing<CTA>(vk, pv, n, tk, tail, Th, J.vcross, &v, R);
     if (!near) {
       if constexpr (CTA) v = bisect_mass_cta(vk, pv, n, v, b0, tail, Th, R);
-      else v = radix_mass<false, 7>(vk, pv, n, v, b0, tail, Th, reinterpret_cast<double*>(hist), R);
+      else v = radix_mass<false, 7>(vk, pv, n, v, b0, tail, Th, hist, R);
     }
     double Gs = 0.0, Mg = 0.0;
     int cg = 0;
@@ -988,7 +1029,7 @@ constexpr size_t LW_VK = 0, LW_PV = (size_t)LW_CAP * 4, LW_HIST = LW_PV + (size_
 constexpr size_t LW_BYTES = LW_HIST + 128 * 8;            // per warp
 static_assert(LW_BYTES - LW_HIST >= 256 * sizeof(unsigned), "radix histogram");
 static_assert(LW_BYTES - LW_HIST >= 32 * 4 * sizeof(unsigned long long), "sorted-crossing keys");
-static_assert(LW_BYTES - LW_HIST >= 128 * sizeof(double), "a warp's top-p search bins");
+static_assert(LW_BYTES - LW_HIST >= 128 * sizeof(unsigned long long), "a warp's top-p search bins");
 constexpr size_t LB_VK = 0, LB_PV = (size_t)LCAP * 4, LB_HIST = LB_PV + (size_t)LCAP * 8;
 constexpr size_t LIST_SMEM_W = (size_t)LIST_WARPS * LW_BYTES, LIST_SMEM_B = LB_HIST + 256 * 8;
 constexpr size_t LIST_SMEM = LIST_SMEM_W > LIST_SMEM_B ? LIST_SMEM_W : LIST_SMEM_B;   // warps' areas / one long list
@@ -1110,14 +1151,34 @@ __device__ __noinline__ void refine_in_list(const Args& a, int row, unsigned* bm
   const unsigned ykex = J.ykex;
   const float m_y = J.m_y;
   const float* srow = rowbuf + sg.shift;
-  double t = 0.0;
-  for (int i = tid; i < V; i += NT) {
+  // each term: penalised, tempered, its exp if it lies below the list; four
+  // independent sums per thread keep four exp_tail chains in flight
+  // (quotients div_rn_try cannot prove are redone after the loop: bit k of
+  // `redo` = element tid + k NT)
+  unsigned long long redo = 0ull;
+  auto term = [&](int i, bool exact) -> double {
     float x = srow[i];
-    if (pen && ((bm[i >> 5] >> (i & 31)) & 1u)) x = (x < 0.0f) ? __fmul_rn(x, pp) : div_rn(x, pp, rpen);
-    const float y = do_t ? div_rn(x, T, rT) : x;
-    if (x > -INFINITY && fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), R.tab);
+    bool ok = true, ok2 = true;
+    if (pen && ((bm[i >> 5] >> (i & 31)) & 1u))
+      x = (x < 0.0f) ? __fmul_rn(x, pp) : exact ? div_rn(x, pp, rpen) : div_rn_try(x, pp, rpen, ok);
+    const float y = (do_t && x > -INFINITY) ? (exact ? div_rn(x, T, rT) : div_rn_try(x, T, rT, ok2)) : x;
+    if (!(ok && ok2)) {
+      redo |= 1ull << ((i - tid) / NT);
+      return 0.0;
+    }
+    return (x > -INFINITY && fkey(y) <= ykex) ? exp_tail(__fsub_rn(y, m_y), R.tab) : 0.0;
+  };
+  double t0 = 0.0, t1 = 0.0, t2 = 0.0, t3 = 0.0;
+  int i = tid;
+  for (; i + 3 * NT < V; i += 4 * NT) {
+    t0 += term(i, false);
+    t1 += term(i + NT, false);
+    t2 += term(i + 2 * NT, false);
+    t3 += term(i + 3 * NT, false);
   }
-  const double tail = LG<true>::sum(t, R);
+  for (; i < V; i += NT) t0 += term(i, false);
+  for (; redo; redo &= redo - 1ull) t0 += term(tid + (__ffsll(redo) - 1) * NT, true);
+  const double tail = LG<true>::sum((t0 + t1) + (t2 + t3), R);
   if (tid == 0) {
     J.tail = tail;
     J.tail_err = ldexp(tail, -50);

@@ -64,7 +64,7 @@ static_assert(FL_VK % 16 == 0 && FL_PV % 16 == 0 && FL_HIST % 16 == 0, "aligned 
 static_assert((size_t)NWARP * F_WSTRIDE * 4 <= (size_t)FLC * 12, "octave bins fit in the key/probability arrays");
 static_assert(FLC <= LW_CAP && FLC <= LCAP, "a list the warp job takes fits its staging");
 static_assert(((F_MAXV + 31) / 32) * 4 <= 2048, "penalty bitmap fits the histogram area");
-static_assert(128 * sizeof(double) <= 2048, "a warp list job's top-p search bins fit the histogram area");
+static_assert(128 * sizeof(unsigned long long) <= 2048, "a warp list job's top-p search bins fit the histogram area");
 // The CTA's list slab in global memory (lists of FLC..LCAP entries): indices,
 // value keys, probabilities; F_SLAB_BYTES must fit one scratch stride.
 constexpr size_t F_GL_VK = (size_t)LCAP * 2;
@@ -410,19 +410,28 @@ __device__ __noinline__ void f_exact_tail(const Args& a, const float* rb, const 
   const float rT = do_t ? __frcp_rn(T) : 1.0f;
   const unsigned ykex = S.J.ykex;
   const float m_y = S.J.m_y;
-  double t = 0.0;
+  double t[4] = {0.0, 0.0, 0.0, 0.0};               // one sum per float4 lane: four exp_tail chains in flight
+  unsigned long long redo = 0ull;                   // elements whose quotient div_rn_try could not prove
+  auto term = [&](float x, float y) {
+    return (x > -INFINITY && fkey(y) <= ykex) ? exp_tail(__fsub_rn(y, m_y), S.R.tab) : 0.0;
+  };
   for (int q = 0; q < g.nq; ++q) {
     const float4 v = fload(rb, fslot(g, q));
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const float x = f4c(v, c);
-      if (x > -INFINITY) {
-        const float y = do_t ? div_rn(x, T, rT) : x;
-        if (fkey(y) <= ykex) t += exp_tail(__fsub_rn(y, m_y), S.R.tab);
-      }
+      bool ok = true;
+      const float y = (do_t && x > -INFINITY) ? div_rn_try(x, T, rT, ok) : x;
+      if (ok) t[c] += term(x, y);
+      else redo |= 1ull << (4 * q + c);
     }
   }
-  const double tail = LG<true>::sum(t, S.R);
+  for (; redo; redo &= redo - 1ull) {
+    const int b = __ffsll(redo) - 1;
+    const float x = f4c(fload(rb, fslot(g, b >> 2)), b & 3);
+    t[0] += term(x, div_call(x, T));
+  }
+  const double tail = LG<true>::sum((t[0] + t[1]) + (t[2] + t[3]), S.R);
   if (threadIdx.x == 0) {
     S.J.tail = tail;
     S.J.tail_err = ldexp(tail, -50);
@@ -477,15 +486,24 @@ __device__ __forceinline__ bool f_short_job_body(const Args& a, int row, RowJob&
   const float m_y = J.m_y;
   unsigned vkey[2], idx[2];
   unsigned lmin = ~0u, lmax = 0u;
+  float xs[2];
+  bool ok[2] = {true, true};
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int p = 2 * lane + j;
     vkey[j] = 0u;
     idx[j] = 0u;
+    xs[j] = 0.0f;
     if (p < n) {
       idx[j] = li[p];
-      const float x = srow[idx[j]];
-      vkey[j] = fkey(do_t ? div_rn(x, T, rT) : x);
+      xs[j] = srow[idx[j]];
+      vkey[j] = fkey(do_t ? div_rn_try(xs[j], T, rT, ok[j]) : xs[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    if (!ok[j]) vkey[j] = fkey(div_call(xs[j], T));  // rare: the quotient div_rn_try could not prove
+    if (2 * lane + j < n) {
       lmin = min(lmin, vkey[j]);
       lmax = max(lmax, vkey[j]);
     }
@@ -986,12 +1004,20 @@ __global__ void __launch_bounds__(NT, MINB) fused_kernel_t(Args a) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) orig[q] = (unsigned)hid[q] < (unsigned)V ? srow[hid[q]] : 0.0f;
           csync();
+          unsigned redo = 0u;                       // quotients div_rn_try could not prove
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             if ((unsigned)hid[q] < (unsigned)V) {
               const float s = orig[q];
-              srow[hid[q]] = (s < 0.0f) ? __fmul_rn(s, pv) : div_rn(s, pv, rpen);
+              bool ok = true;
+              const float y = (s < 0.0f) ? __fmul_rn(s, pv) : div_rn_try(s, pv, rpen, ok);
+              if (ok) srow[hid[q]] = y;
+              else redo |= 1u << q;
             }
+          }
+          for (; redo; redo &= redo - 1u) {
+            const int q = __ffs(redo) - 1;
+            srow[hid[q]] = div_call(orig[q], pv);
           }
         } else {
           csync();                                 // the bitmap is clear

@@ -116,21 +116,30 @@ __device__ __noinline__ float div_call(float x, float d) { return __fdiv_rn(x, d
 // is the float nearest to x/d. Quotients it cannot prove -- near-ties, powers
 // of two (whose lower neighbour is half an ulp away), |q| outside
 // [2^-100, 2^100], d outside [2^-100, 2^100] -- come from __fdiv_rn.
-__device__ __forceinline__ float div_rn(float x, float d, float rd) {
-  float q = __fmul_rn(x, rd);
-  if (x == 0.0f) return q;                          // signed zero (the corrections would lose -0)
-  float r = __fmaf_rn(-q, d, x);
-  q = __fmaf_rn(r, rd, q);
+//
+// div_rn_try is the same without the fallback: the quotient and whether the
+// proof holds. Its callers compute many quotients with no call in between
+// (a possible call at every quotient keeps the compiler from overlapping
+// them) and send the rare unproven ones to div_call afterwards.
+__device__ __forceinline__ float div_rn_try(float x, float d, float rd, bool& ok) {
+  const float q0 = __fmul_rn(x, rd);
+  float r = __fmaf_rn(-q0, d, x);
+  float q = __fmaf_rn(r, rd, q0);
   r = __fmaf_rn(-q, d, x);
   q = __fmaf_rn(r, rd, q);
   r = __fmaf_rn(-q, d, x);
   const unsigned bq = __float_as_uint(q) & 0x7fffffffu;
   const float hulp = __uint_as_float((bq & 0x7f800000u) - (24u << 23));   // ulp(q) / 2
   const float ad = fabsf(d);
-  const bool ok = bq >= 0x0d800000u && bq <= 0x71800000u && (bq & 0x007fffffu) != 0u && ad >= 7.8886e-31f &&
-                  ad <= 1.2676e30f && fabsf(r) < __fmul_rn(__fmul_rn(hulp, ad), 0.99999905f);
-  if (ok) return q;
-  return div_call(x, d);
+  const bool zero = x == 0.0f;                      // signed zero (the corrections would lose -0)
+  ok = zero || (bq >= 0x0d800000u && bq <= 0x71800000u && (bq & 0x007fffffu) != 0u && ad >= 7.8886e-31f &&
+                ad <= 1.2676e30f && fabsf(r) < __fmul_rn(__fmul_rn(hulp, ad), 0.99999905f));
+  return zero ? q0 : q;
+}
+__device__ __forceinline__ float div_rn(float x, float d, float rd) {
+  bool ok;
+  const float q = div_rn_try(x, d, rd, ok);
+  return ok ? q : div_call(x, d);
 }
 
 // Not inlined: CUDA's exp(double) is large and is called from many sites.

@@ -666,13 +666,21 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
             if (!(atomicOr(&S.bm[t >> 5], bit) & bit)) first |= 1u << q;
           }
         }
+        unsigned redo = 0u;                         // quotients div_rn_try could not prove
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
           if (first & (1u << q)) {
             const int t = hid[q];
             const float sv = srow[t];
-            srow[t] = (sv < 0.0f) ? __fmul_rn(sv, pv) : div_rn(sv, pv, rpen);
+            bool ok = true;
+            const float y = (sv < 0.0f) ? __fmul_rn(sv, pv) : div_rn_try(sv, pv, rpen, ok);
+            if (ok) srow[t] = y;
+            else redo |= 1u << q;
           }
+        }
+        for (; redo; redo &= redo - 1u) {
+          const int t = hid[__ffs(redo) - 1];
+          srow[t] = div_call(srow[t], pv);
         }
         for (long long jj = h0 + tid + 16LL * RT; jj < h1; jj += RT) apply(a.hist[jj]);
         rsync();
