@@ -851,11 +851,12 @@ __device__ __noinline__ int f_row(const Args& a, int row, const MetaSlot& M, con
 }
 
 // Fused persistent kernel: rows handed out dynamically (the first G
-// statically), each finished in its CTA. Two forms: MINB = 3 resident CTAs
-// per SM with the per-row paths out of line (batches above one row per SM),
-// and MINB = 1, one CTA per SM with every register it needs and the common
-// path (top-k row, short list) inlined: no spills and no call frames on the
-// latency-bound path of small batches (B <= SMs, B = 1 among them).
+// statically), each finished in its CTA. Three forms: MINB = 3 resident CTAs
+// per SM with the per-row paths out of line (batches above two rows per SM);
+// MINB = 1, one CTA per SM with every register it needs and the common path
+// (top-k row, short list) inlined: no spills and no call frames on the
+// latency-bound path of small batches (B <= SMs, B = 1 among them); and
+// MINB = 2 with the same inlining for batches of up to two rows per SM.
 template <int MINB, bool INL>
 __global__ void __launch_bounds__(NT, MINB) fused_kernel_t(Args a) {
   extern __shared__ __align__(128) unsigned char fsm[];
@@ -1085,9 +1086,11 @@ __global__ void __launch_bounds__(NT, MINB) fused_kernel_t(Args a) {
   }
 }
 
-// the batched form (B > SMs) and the small-batch form
+// the batched form (B > 2 SMs), the small-batch form (B <= SMs) and between
+// them two CTAs per SM with the common path inlined (128 registers)
 constexpr int FUSED_MINB = 3;
 inline constexpr auto fused_kernel = fused_kernel_t<FUSED_MINB, false>;
 inline constexpr auto fused_small_kernel = fused_kernel_t<1, true>;
+inline constexpr auto fused_mid_kernel = fused_kernel_t<2, true>;
 
 }  // namespace c4s

@@ -126,6 +126,7 @@ struct c4s_ctx {
   int list_occ = 0;                            // resident list-kernel CTAs per SM
   int fused_occ = 0;                           // resident fused-kernel CTAs per SM
   int fused_small_occ = 0;                     //   and of its small-batch form
+  int fused_mid_occ = 0;                       //   and of its two-per-SM form
   bool split_dirty = false;                    // a split-path launch sequence stopped early: its
                                                // queue counters may be stale until cleared
   c4s::RowJob* d_jobs = nullptr;               // fast path: per-row jobs of one chunk
@@ -242,24 +243,31 @@ int launch_rows(c4s_ctx* ctx, c4s::Args& a, void* stream) {
     a.defer_cnt = ctx->d_defer_cnt + FUSED_CNT;
     const size_t smem = fused_smem_bytes(a.V);
     if (ctx->fused_occ == 0) {
-      int occ = 0, occ1 = 0;
+      int occ = 0, occ1 = 0, occ2 = 0;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fused_kernel, NT, fused_smem_bytes(F_MAXV)) !=
               cudaSuccess || occ < 1 ||
           cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, fused_small_kernel, NT, fused_smem_bytes(F_MAXV)) !=
-              cudaSuccess || occ1 < 1)
+              cudaSuccess || occ1 < 1 ||
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ2, fused_mid_kernel, NT, fused_smem_bytes(F_MAXV)) !=
+              cudaSuccess || occ2 < 1)
         return fail(ctx, C4S_ERR_CUDA, "fused kernel occupancy");
       ctx->fused_occ = occ;
       ctx->fused_small_occ = occ1;
+      ctx->fused_mid_occ = occ2;
     }
+    // one row per CTA while the rows fit the small form's (then the mid form's) CTAs
     const bool small = a.B <= (long long)ctx->fused_small_occ * ctx->num_sms;
+    const bool mid = !small && a.B <= (long long)ctx->fused_mid_occ * ctx->num_sms;
     // every CTA uses two scratch slabs (blockIdx.x and grid + blockIdx.x)
-    const int occ = small ? ctx->fused_small_occ : ctx->fused_occ;
+    const int occ = small ? ctx->fused_small_occ : mid ? ctx->fused_mid_occ : ctx->fused_occ;
     const int grid = (int)std::min<long long>(std::min<long long>(a.B, (long long)occ * ctx->num_sms),
                                               (long long)ctx->scratch_ctas / 2);
     cudaEvent_t* ev = ctx->timing ? timing_slot(ctx) : nullptr;
     if (ev)
       for (int k = 0; k < TEV - 1; ++k) cudaEventRecord(ev[k], st0);
-    e = small ? launch_pdl(fused_small_kernel, grid, NT, smem, st0, a) : launch_pdl(fused_kernel, grid, NT, smem, st0, a);
+    e = small ? launch_pdl(fused_small_kernel, grid, NT, smem, st0, a)
+        : mid ? launch_pdl(fused_mid_kernel, grid, NT, smem, st0, a)
+              : launch_pdl(fused_kernel, grid, NT, smem, st0, a);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "fused kernel launch");
     if (ev) {
       cudaEventRecord(ev[TEV - 1], st0);
@@ -544,6 +552,12 @@ int c4s_create_sized(c4s_ctx** out, int32_t max_vocab, int32_t max_rows, int32_t
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(c4s::fused_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c4s::fused_smem_bytes(c4s::F_MAXV));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::fused_mid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)c4s::fused_smem_bytes(c4s::F_MAXV));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(c4s::fused_mid_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
   // the row kernel keeps five rows in flight per SM only with the largest
   // shared-memory carveout
   if (e == cudaSuccess)
