@@ -40,6 +40,8 @@ constexpr int HG_THREADS = 192;
 constexpr unsigned HG_TILE_BYTES = (unsigned)HG_BM * HG_BK * 2;          // one 128 x 64 bf16 tile: 16 KB
 constexpr unsigned HG_STAGE_BYTES = 2 * HG_TILE_BYTES;                    // y tile + W tile
 constexpr size_t HG_SMEM = (size_t)HG_ST * HG_STAGE_BYTES + 1024;        // + alignment slack (1024-byte tiles)
+// the epilogue's transposed chunks (4 warps x 4 chunks x 32 x 33 floats) reuse the pipeline buffers
+static_assert(4 * (HG_BN / 32) * 32 * 33 * 4 <= HG_ST * HG_STAGE_BYTES, "epilogue buffers fit the pipeline's");
 constexpr unsigned HG_TMEM_COLS = 128;                                   // fp32 accumulator, 128 lanes x 128 columns
 // Instruction descriptor of tcgen05.mma kind::f16: D fp32 (bits 4-5 = 1),
 // A and B bf16 (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0),
@@ -281,27 +283,40 @@ __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_c
     if (ok && !abort_flag && KB > 0) {
       // each 32 x 32 chunk (lane = row) goes through shared memory (the idle
       // pipeline buffers: every MMA, hence every load, has completed)
-      // transposed, so that each store writes 32 consecutive logits of one row
+      // transposed, so that each store writes 32 consecutive logits of one
+      // row. All four chunks are read from TMEM at once and transposed into
+      // their own buffers before any store, so the loads' latency and the
+      // stores overlap instead of alternating chunk by chunk.
+      constexpr int NCH = HG_BN / 32;
       const int q = warp & 3;
-      float* T = reinterpret_cast<float*>(hsm) + (warp - 2) * (32 * 33);
+      float* T = reinterpret_cast<float*>(hsm) + (warp - 2) * (NCH * 32 * 33);
       const int rows = min(32, g.M - (m0 + 32 * q));   // rows of this warp's quarter inside the output
       float* obase = g.logits + (long long)(m0 + 32 * q) * g.ldl + n0 + lane;
-#pragma unroll 1
-      for (int c = 0; c < HG_BN / 32; ++c) {
+      float bn[NCH];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
         const int n = n0 + 32 * c + lane;
-        const float bn = (g.bias && n < g.N) ? __ldg(g.bias + n) : 0.0f;
-        unsigned r[32];
-        tmem_ld32(tmem + ((unsigned)(32 * q) << 16) + (unsigned)(32 * c), r);
+        bn[c] = (g.bias && n < g.N) ? __ldg(g.bias + n) : 0.0f;
+      }
+      {
+        unsigned r[NCH][32];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) tmem_ld32(tmem + ((unsigned)(32 * q) << 16) + (unsigned)(32 * c), r[c]);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) T[lane * 33 + j] = __uint_as_float(r[j]);   // conflict-free: bank (lane + j)
-        __syncwarp();
-        if (n < g.N) {
+        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) T[c * 32 * 33 + lane * 33 + j] = __uint_as_float(r[c][j]);   // bank (lane + j)
+      }
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        if (n0 + 32 * c + lane < g.N) {
           float* o = obase + 32 * c;
+          const float* t = T + c * 32 * 33 + lane;
 #pragma unroll 8
-          for (int rr = 0; rr < rows; ++rr) o[(long long)rr * g.ldl] = T[rr * 33 + lane] + bn;
+          for (int rr = 0; rr < rows; ++rr) o[(long long)rr * g.ldl] = t[rr * 33] + bn[c];
         }
-        __syncwarp();
       }
     }
   }
