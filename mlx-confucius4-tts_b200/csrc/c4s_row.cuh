@@ -611,8 +611,11 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
           if (tid == 0) atomicOr(a.errflags, C4S_DEVERR_HIST_RANGE);
           h0 = h1 = 0;
         }
-        for (int w = tid; w < nbm; w += RT) S.bm[w] = 0u;
       }
+      // histories beyond the ids the threads hold in registers de-duplicate through a bitmap
+      const bool longh = h1 - h0 > 16LL * RT;
+      if (longh)
+        for (int w = tid; w < nbm; w += RT) S.bm[w] = 0u;
       // the first 16 ids per thread in flight while the row arrives
       int hid[16];
 #pragma unroll
@@ -655,34 +658,51 @@ __global__ void __launch_bounds__(RT, 5) row_kernel(Args a) {
             }
           }
         };
-        // claim the ids first (independent atomics in flight together), then
-        // penalise the ones this thread claimed first
-        unsigned first = 0u;
+        if (!longh) {
+          // every id reads its logit, a barrier, every id writes the
+          // penalised value: ids that repeat write the same value, so no
+          // de-duplication (bitmap, atomics) is needed
+          float orig[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const int t = hid[q];
-          if ((unsigned)t < (unsigned)V) {
-            const unsigned bit = 1u << (t & 31);
-            if (!(atomicOr(&S.bm[t >> 5], bit) & bit)) first |= 1u << q;
+          for (int q = 0; q < 16; ++q) orig[q] = (unsigned)hid[q] < (unsigned)V ? srow[hid[q]] : 0.0f;
+          rsync();
+          unsigned redo = 0u;                       // quotients div_rn_try could not prove
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if ((unsigned)hid[q] < (unsigned)V) {
+              const float sv = orig[q];
+              bool ok = true;
+              const float y = (sv < 0.0f) ? __fmul_rn(sv, pv) : div_rn_try(sv, pv, rpen, ok);
+              if (ok) srow[hid[q]] = y;
+              else redo |= 1u << q;
+            }
           }
-        }
-        unsigned redo = 0u;                         // quotients div_rn_try could not prove
+          for (; redo; redo &= redo - 1u) {
+            const int q = __ffs(redo) - 1;
+            srow[hid[q]] = div_call(orig[q], pv);
+          }
+        } else {
+          // claim the ids first (independent atomics in flight together),
+          // then penalise the ones this thread claimed first
+          unsigned first = 0u;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if (first & (1u << q)) {
+          for (int q = 0; q < 16; ++q) {
             const int t = hid[q];
-            const float sv = srow[t];
-            bool ok = true;
-            const float y = (sv < 0.0f) ? __fmul_rn(sv, pv) : div_rn_try(sv, pv, rpen, ok);
-            if (ok) srow[t] = y;
-            else redo |= 1u << q;
+            if ((unsigned)t < (unsigned)V) {
+              const unsigned bit = 1u << (t & 31);
+              if (!(atomicOr(&S.bm[t >> 5], bit) & bit)) first |= 1u << q;
+            }
           }
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if (first & (1u << q)) {
+              const int t = hid[q];
+              const float sv = srow[t];
+              srow[t] = (sv < 0.0f) ? __fmul_rn(sv, pv) : div_rn(sv, pv, rpen);
+            }
+          }
+          for (long long jj = h0 + tid + 16LL * RT; jj < h1; jj += RT) apply(a.hist[jj]);
         }
-        for (; redo; redo &= redo - 1u) {
-          const int t = hid[__ffs(redo) - 1];
-          srow[t] = div_call(srow[t], pv);
-        }
-        for (long long jj = h0 + tid + 16LL * RT; jj < h1; jj += RT) apply(a.hist[jj]);
         rsync();
       }
       const RGeo g = rgeo(V, sg.shift);
