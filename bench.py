@@ -58,8 +58,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="only run this many steps of the main loop (for ncu), print nothing")
-    ap.add_argument("--profile-config", choices=["c2", "c0"], default="c2",
-                    help="with --profile-steps: c2 = config-2 rows (--rows), c0 = one config-0 row")
+    ap.add_argument("--profile-config", choices=["c2", "c0", "c2k0", "c2k20"], default="c2",
+                    help="with --profile-steps: c2 = config-2 rows (--rows), c0 = one config-0 row, "
+                         "c2k0 / c2k20 = config-2 rows all without top-k / all with top_k 20")
     return ap.parse_args()
 
 
@@ -295,6 +296,8 @@ def run_ours(args):
             b = wl.config0(seed=k)
         else:
             b = wl.config2(seed=2 + k, B=B, row_offset=rank * B)
+            if args.profile_steps and args.profile_config in ("c2k0", "c2k20"):
+                b.params["top_k"][:] = 0 if args.profile_config == "c2k0" else 20
         pool.append(dict(
             logits=torch.from_numpy(b.logits).to(dev),
             hist=torch.from_numpy(b.hist).to(dev),

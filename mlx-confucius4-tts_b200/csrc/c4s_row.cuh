@@ -182,7 +182,7 @@ __device__ __noinline__ int topk_body(const Args& a, int row, const RowCtx rc, c
   // when `two`) is finite has >= kw elements >= it, so >= k elements are >=
   // tau, the smallest over the warps (-inf: not enough elements; general path)
   if (k > RT * (two ? 2 : 1)) return ROW_GENERAL;
-  const float tau = u_threshold<RT>(tm, t2, two, rc.m_x, k, &S.hw[0][0][0], &S.redu[0], [] { rsync(); });
+  const float tau = u_threshold<RT>(tm, t2, two, rc.m_x, k, &S.hw[0][0][0], &S.redu[0], [] { rsync(); }, true);
   // fl(x/T) merges x only with values at most |x| 2^-23 below it: lowering tau
   // by 2^-18 relative (+ 2^-18 absolute) keeps every x tied with tau after /T
   const float tau_lo = tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f;
@@ -403,6 +403,11 @@ __device__ __forceinline__ int row_body(const Args& a, const Args& ao, int row, 
   const bool two = !P.greedy && do_k && k > RWARP * 32 / 2;   // the two largest per lane seed the list
 
   // ---- row max, per-lane maxima (and second maxima), valid elements per lane ----
+  // (top-k rows: the threshold histogram's bins are cleared here, ordered
+  // before their use by the barrier of the max reduction; the area's last
+  // use, the previous row's staging, ended before the row's barriers)
+  if (!P.greedy && do_k)
+    for (int i = tid; i < 256; i += RT) (&S.hw[0][0][0])[i] = 0u;
   float tm = -INFINITY, t2 = -INFINITY;
 #pragma unroll 4
   for (int q = 0; q < g.nq; ++q) {
@@ -425,7 +430,8 @@ __device__ __forceinline__ int row_body(const Args& a, const Args& ao, int row, 
 #pragma unroll
   for (int w = 1; w < RWARP; ++w) kall = kall > S.redu[w] ? kall : S.redu[w];
   const float m_x = fkey_inv(kall);
-  rsync();
+  // (S.redu is next written behind later barriers: the greedy path's below,
+  // the threshold's result and the no-top-k path's after their own barriers)
 
   RowCtx rc;
   rc.row = row; rc.V = V; rc.i0 = 0;
@@ -434,6 +440,7 @@ __device__ __forceinline__ int row_body(const Args& a, const Args& ao, int row, 
 
   // ---- greedy: first index of the max (sampling.cpp:73-76) ----
   if (P.greedy) {
+    rsync();                                       // every warp has read S.redu
     unsigned cand = 0xffffffffu;
     if (m_x > -INFINITY && tm == m_x) {
       for (int q = 0; q < g.nq; ++q) {
