@@ -36,11 +36,13 @@
 namespace c4s {
 
 constexpr int HG_BM = 128, HG_BN = 128, HG_BK = 64, HG_ST = 6;
-constexpr int HG_THREADS = 192;
+constexpr int HG_EPI_WARPS = 16;                   // four per TMEM lane quarter, each a quarter of the columns
+constexpr int HG_THREADS = 64 + 32 * HG_EPI_WARPS;  // producer warp, MMA warp, epilogue warps
 constexpr unsigned HG_TILE_BYTES = (unsigned)HG_BM * HG_BK * 2;          // one 128 x 64 bf16 tile: 16 KB
 constexpr unsigned HG_STAGE_BYTES = 2 * HG_TILE_BYTES;                    // y tile + W tile
 constexpr size_t HG_SMEM = (size_t)HG_ST * HG_STAGE_BYTES + 1024;        // + alignment slack (1024-byte tiles)
-// the epilogue's transposed chunks (4 warps x 4 chunks x 32 x 33 floats) reuse the pipeline buffers
+// the epilogue's transposed chunks (all warps' 32 x 33-float chunks) reuse the pipeline buffers
+static_assert(HG_EPI_WARPS % 4 == 0 && (HG_BN / 32) % (HG_EPI_WARPS / 4) == 0, "whole chunks per epilogue warp");
 static_assert(4 * (HG_BN / 32) * 32 * 33 * 4 <= HG_ST * HG_STAGE_BYTES, "epilogue buffers fit the pipeline's");
 constexpr unsigned HG_TMEM_COLS = 128;                                   // fp32 accumulator, 128 lanes x 128 columns
 // Instruction descriptor of tcgen05.mma kind::f16: D fp32 (bits 4-5 = 1),
@@ -275,33 +277,36 @@ __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_c
       umma_commit(&accum);                          // every MMA issued so far has completed
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = rows of the tile
+    // epilogue warps: warp w reads TMEM lanes 32 (w % 4) .. + 31 = rows of the tile
     const bool ok = mbar_wait_1s(&accum, 0u);
     if (!ok) give_up();
     if (threadIdx.x == 64) C4S_HTR(5);
     tc_fence_after();
     if (ok && !abort_flag && KB > 0) {
-      // each 32 x 32 chunk (lane = row) goes through shared memory (the idle
+      // warp w reads TMEM lane quarter q = w % 4 (the hardware's rule) and,
+      // with the other warp of its quarter, half of the tile's columns. Each
+      // 32 x 32 chunk (lane = row) goes through shared memory (the idle
       // pipeline buffers: every MMA, hence every load, has completed)
       // transposed, so that each store writes 32 consecutive logits of one
-      // row. All four chunks are read from TMEM at once and transposed into
-      // their own buffers before any store, so the loads' latency and the
-      // stores overlap instead of alternating chunk by chunk.
-      constexpr int NCH = HG_BN / 32;
+      // row; the warp's chunks are read from TMEM at once and transposed
+      // before any store, so the loads' latency and the stores overlap.
+      constexpr int NCH = HG_BN / 32 / (HG_EPI_WARPS / 4);   // chunks per warp
       const int q = warp & 3;
+      const int c0 = ((warp - 2) >> 2) * NCH;                // the warp's first chunk
       float* T = reinterpret_cast<float*>(hsm) + (warp - 2) * (NCH * 32 * 33);
       const int rows = min(32, g.M - (m0 + 32 * q));   // rows of this warp's quarter inside the output
       float* obase = g.logits + (long long)(m0 + 32 * q) * g.ldl + n0 + lane;
       float bn[NCH];
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
-        const int n = n0 + 32 * c + lane;
+        const int n = n0 + 32 * (c0 + c) + lane;
         bn[c] = (g.bias && n < g.N) ? __ldg(g.bias + n) : 0.0f;
       }
       {
         unsigned r[NCH][32];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) tmem_ld32(tmem + ((unsigned)(32 * q) << 16) + (unsigned)(32 * c), r[c]);
+        for (int c = 0; c < NCH; ++c)
+          tmem_ld32(tmem + ((unsigned)(32 * q) << 16) + (unsigned)(32 * (c0 + c)), r[c]);
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < NCH; ++c)
@@ -311,8 +316,8 @@ __global__ void __launch_bounds__(HG_THREADS, 1) head_gemm_kernel(const __grid_c
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
-        if (n0 + 32 * c + lane < g.N) {
-          float* o = obase + 32 * c;
+        if (n0 + 32 * (c0 + c) + lane < g.N) {
+          float* o = obase + 32 * (c0 + c);
           const float* t = T + c * 32 * 33 + lane;
 #pragma unroll 8
           for (int rr = 0; rr < rows; ++rr) o[(long long)rr * g.ldl] = t[rr * 33] + bn[c];
