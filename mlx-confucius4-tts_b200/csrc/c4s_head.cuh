@@ -10,7 +10,7 @@
 // device: ln_kernel writes y in bf16 (the GEMM operand type), and
 // head_gemm_kernel computes logits = y W^T + b with fp32 accumulation:
 //
-//   one CTA per 128 x 128 tile of the [B, N] output, 6 warps --
+//   one CTA per 128 x 128 tile of the [B, N] output, 18 warps --
 //     warp 0 (one lane)  TMA producer: 128 x 64 bf16 tiles of y and W per
 //                        k-block by cp.async.bulk.tensor (128-byte swizzle)
 //                        into a 6-stage shared-memory ring (full/empty
@@ -19,7 +19,8 @@
 //                        tcgen05.mma kind::f16 (M 128, N 128, K 16; bf16 in,
 //                        fp32 accumulator in TMEM), tcgen05.commit frees each
 //                        stage and finally signals the accumulator;
-//     warps 2-5          epilogue: tcgen05.ld of their 32 TMEM lanes (rows),
+//     warps 2-17         epilogue, four per TMEM lane quarter: tcgen05.ld of
+//                        a 32-column chunk of their 32 TMEM lanes (rows),
 //                        + bias, fp32 stores of the logits.
 //   No cluster, no multicast: every TMA load reads this GPU's own memory.
 //   Every mbarrier wait is bounded (about 1 s); a wait that gives up sets
