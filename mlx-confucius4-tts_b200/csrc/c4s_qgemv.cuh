@@ -146,6 +146,63 @@ __global__ void __launch_bounds__(QG_NT) qgemv_kernel(QGemvArgs g) {
   }
 }
 
+// The decode case -- one row of x, 8-bit codes -- without the staging of x:
+// each lane's chunks (16 codes = 16 B) are loaded together with the 16
+// values of x they multiply (four float4 through L1; x is a few KB that every
+// warp reads) and their group's scale and bias, QG_INFLIGHT chunks at a time,
+// so a warp's row costs about one memory round trip instead of the staging
+// pass, a CTA barrier and then the weights. The products are summed in the
+// same order as qgemv_rows (per lane: chunks in order, the 16 weights of a
+// chunk in order; then the warp's shuffle tree). Needs x 16-byte aligned.
+__global__ void __launch_bounds__(QG_NT, 2) qgemv1_kernel(QGemvArgs g) {
+  grid_dep_wait();                                 // x comes from the previous kernel
+  grid_dep_launch();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nchunk = g.K >> 4;                     // 16 codes per chunk
+  const int ng = g.K >> g.glog;
+  const float4* x4 = reinterpret_cast<const float4*>(g.x);
+  for (int n = blockIdx.x * QG_WARPS + warp; n < g.N; n += gridDim.x * QG_WARPS) {
+    const uint4* wr = reinterpret_cast<const uint4*>(g.q + (size_t)n * (g.K / 4));
+    const float* srow = g.scales + (size_t)n * ng;
+    const float* brow = g.biases + (size_t)n * ng;
+    float acc = 0.0f;
+    for (int c0 = lane; c0 < nchunk; c0 += QG_INFLIGHT * 32) {
+      uint4 w[QG_INFLIGHT];
+      float4 xv[QG_INFLIGHT][4];
+      float sc[QG_INFLIGHT], bi[QG_INFLIGHT];
+#pragma unroll
+      for (int u = 0; u < QG_INFLIGHT; ++u) {
+        const int c = c0 + 32 * u;
+        const bool ok = c < nchunk;
+        const int kg = (c * 16) >> g.glog;         // group >= 16: a chunk lies in one group
+        w[u] = ok ? __ldcs(wr + c) : make_uint4(0u, 0u, 0u, 0u);   // streamed once
+        sc[u] = ok ? __ldg(srow + kg) : 0.0f;
+        bi[u] = ok ? __ldg(brow + kg) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[u][j] = ok ? __ldg(x4 + 4 * c + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < QG_INFLIGHT; ++u) {
+        if (c0 + 32 * u >= nchunk) break;
+        const unsigned word[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float xe[4] = {xv[u][j].x, xv[u][j].y, xv[u][j].z, xv[u][j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float wv = fmaf(sc[u], (float)((word[j] >> (8 * e)) & 0xffu), bi[u]);
+            acc = fmaf(xe[e], wv, acc);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+    if (lane == 0) g.y[n] = acc + (g.bias_out ? g.bias_out[n] : 0.0f);
+  }
+}
+
 // Affine quantization of w [N, K] (one warp per group of <= 128 weights,
 // lane l holding elements l, l + 32, ...): min / max by warp reductions,
 // q = round-half-even((w - min) / scale), clamped to [0, 2^bits - 1]; a

@@ -776,6 +776,22 @@ int c4s_qgemv(c4s_ctx* ctx, const float* d_x, int32_t B, int32_t K, const uint32
   if (!dg.ok) return fail(ctx, C4S_ERR_CUDA, "cannot select the context's device");
   c4s::QGemvArgs g{d_x, B, K, N, group, bits, group == 32 ? 5 : group == 64 ? 6 : 7, d_q, d_scales, d_biases,
                    d_bias_out, d_y};
+  if (B == 1 && bits == 8 && ((uintptr_t)d_x & 15) == 0) {
+    // the decode case: no staging of x (qgemv1_kernel)
+    const int grid = (int)std::min<long long>((N + c4s::QG_WARPS - 1) / c4s::QG_WARPS, 8LL * ctx->num_sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(c4s::QG_NT);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, c4s::qgemv1_kernel, g);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "qgemv launch");
+    return C4S_OK;
+  }
   const size_t smem = (size_t)std::min(B, c4s::QG_MAXB) * K * sizeof(float);
   if (ctx->qg_smem_set < smem) {
     const cudaError_t ea = cudaFuncSetAttribute(c4s::qgemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
