@@ -80,20 +80,30 @@ __host__ __device__ inline size_t shard_smem_bytes(int Vs) {
 }
 
 // Writes the row's 64 candidates from an ascending list of keys
-// (~fkey(value) << 32 | local index): largest value first, ties by index.
-// `temper`: srow holds untempered values; the emitted value is RN(x / T).
-__device__ __forceinline__ void shard_emit(c4s_candidate* out, int voff, const float* srow,
-                                           const unsigned long long* list, bool ties, bool temper, float T) {
+// (~fkey(value) << 32 | local index; value already tempered): largest value
+// first, ties by index.
+__device__ __forceinline__ void shard_emit(c4s_candidate* out, int voff, const unsigned long long* list,
+                                           bool ties) {
   const int t = threadIdx.x;
   if (t < SHARD_CAND) {
     const unsigned long long k = list[t];
-    const int li = (int)(unsigned)(k & 0xffffffffull);
-    unsigned gi = (unsigned)(voff + li);
+    unsigned gi = (unsigned)(voff + (int)(unsigned)(k & 0xffffffffull));
     if (t == SHARD_CAND - 1 && ties) gi |= CAND_TIES;
     c4s_candidate c;
-    c.value = temper ? __fdiv_rn(srow[li], T) : srow[li];
+    c.value = fkey_inv(~(unsigned)(k >> 32));
     c.index = (int)gi;
     out[t] = c;
+  }
+}
+
+// Eight 16-byte slots of the staged row per thread: slot (ch * 8 + q) * NT +
+// tid; slots past the row read as -inf.
+constexpr int SHARD_SQ = 8;
+__device__ __forceinline__ void shard_slots(float4 (&v)[SHARD_SQ], const float4* s4, int ch, int nv) {
+#pragma unroll
+  for (int q = 0; q < SHARD_SQ; ++q) {
+    const int f = (ch * SHARD_SQ + q) * NT + (int)threadIdx.x;
+    v[q] = f < nv ? s4[f] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
   }
 }
 
@@ -104,10 +114,23 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
   unsigned* bitmap = reinterpret_cast<unsigned*>(srow + align_up((size_t)a.Vs, 4));  // a.Vs: widest shard
   __shared__ unsigned s_wk[NWARP];
   __shared__ unsigned s_hist[256];
+  __shared__ float s_mx[NWARP];
+  __shared__ int s_scan[NWARP];
+  __shared__ unsigned s_res;
   __shared__ int s_cnt, s_digit, s_want;
+  static_assert(NT == 256, "one histogram bin per thread");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long items = (long long)a.B * a.G;
   for (long long item = blockIdx.x; item < items; item += gridDim.x) {
+    if (tid == 0 && item + gridDim.x < items) {  // the next item's columns into L2 (its aligned interior)
+      const long long nx = item + gridDim.x;
+      const int nrow = (int)(nx / a.G);
+      int nl = 0, nw = a.Vs;
+      if (a.G > 1) shard_span(a.Vtot, a.G, (int)(nx % a.G), nl, nw);
+      const uintptr_t p0 = (uintptr_t)(a.logits + (long long)nrow * a.ld + nl);
+      const uintptr_t b0 = (p0 + 15) & ~(uintptr_t)15, b1 = (p0 + (uintptr_t)nw * 4) & ~(uintptr_t)15;
+      if (b1 > b0) bulk_prefetch_l2((const void*)b0, (unsigned)(b1 - b0));
+    }
     const int row = (int)(item / a.G), sh = (int)(item % a.G);
     if (a.active && !a.active[row]) continue;
     int voff = a.voff, Vs = a.Vs, loff = 0;       // loff: the shard's first column in the given ones
@@ -153,7 +176,7 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
       }
       for (int i = tid; i < (Vs + 31) / 32; i += NT) bitmap[i] = 0u;
     }
-    if (tid == 0) s_cnt = 0;
+    s_hist[tid] = 0u;  // the threshold's bins
     __syncthreads();
     if (pen) {
       const float pv = P.repetition_penalty;
@@ -172,57 +195,69 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
       }
       __syncthreads();
     }
-    // 3. each thread's largest penalised value (16-byte passes over the row;
-    //    the buffer's padding to a multiple of 4 holds -inf)
+    // 3. each thread's two largest penalised values and the row's maximum
+    //    (eight 16-byte slots per thread and pass, held in registers; the
+    //    buffer's padding to a multiple of 4 holds -inf)
     const bool temper = !P.greedy && !(P.temperature == 1.0f || P.temperature <= 0.0f);
     const float T = P.temperature;
     const int nv = (Vs + 3) >> 2;
     const float4* s4 = reinterpret_cast<const float4*>(srow);
-    float tm = -INFINITY;
-    for (int i = tid; i < nv; i += NT) {
-      const float4 v = s4[i];
-      tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-    }
-    const unsigned tmax = fkey(tm);
-    // 4. a lower bound on the 64th largest value: in every warp 8 lanes hold an
-    //    element at least as large as the warp's 8th-largest lane maximum, so
-    //    at least 64 elements are >= the least of the 8 warps' values. Lanes
-    //    without elements hold -inf, which makes the bound -inf (every element).
-    int rank = 0;
-    for (int s = 0; s < 32; ++s) {
-      const unsigned o = __shfl_sync(FULL, tmax, s);
-      rank += (o > tmax) || (o == tmax && s < lane);
-    }
-    const unsigned sel = __ballot_sync(FULL, rank == 7);
-    const unsigned wk = __shfl_sync(FULL, tmax, __ffs(sel) - 1);
-    if (lane == 0) s_wk[warp] = wk;
-    __syncthreads();
-    unsigned tau0 = s_wk[0];
+    const int nch = (nv + SHARD_SQ * NT - 1) / (SHARD_SQ * NT);
+    float4 v[SHARD_SQ];
+    float tm = -INFINITY, t2 = -INFINITY;
+    for (int ch = 0; ch < nch; ++ch) {
+      shard_slots(v, s4, ch, nv);
 #pragma unroll
-    for (int w = 1; w < NWARP; ++w) tau0 = min(tau0, s_wk[w]);
-    const float t0f = fkey_inv(tau0);
-    // 5. every element >= the bound into the list (any order), keyed by its
-    //    tempered value: ~fkey(value) << 32 | local index, ascending = largest
-    //    value first, ties by index. Temperature is monotone, so the list holds
-    //    the 64 largest tempered values unless an element below the bound
-    //    tempers to the list's 64th value (checked below).
-    for (int i = tid; i < nv; i += NT) {
-      const float4 v = s4[i];
-      if (fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)) >= t0f) {
-        const float e[4] = {v.x, v.y, v.z, v.w};
+      for (int q = 0; q < SHARD_SQ; ++q) {
+        const float e[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const int idx = 4 * i + c;
-          if (idx < Vs && e[c] >= t0f) {
-            const float tv = temper ? __fdiv_rn(e[c], T) : e[c];
-            const int pos = atomicAdd(&s_cnt, 1);
-            if (pos < SHARD_LIST) list[pos] = ((unsigned long long)(~fkey(tv)) << 32) | (unsigned)idx;
-          }
+          t2 = fmaxf(t2, fminf(tm, e[c]));
+          tm = fmaxf(tm, e[c]);
+        }
+      }
+    }
+    const float m_x = block_reduce(tm, MaxF{}, s_mx);
+    // 4. a lower bound on the 64th largest value: the 64th largest of the
+    //    threads' two largest values (distinct elements), located in a
+    //    histogram of key distances from the maximum, so at least 64 elements
+    //    are >= tau and few more. Lowered by 2^-18 relative when tempering:
+    //    RN(x / T) merges x only with values at most |x| 2^-23 below it, so the
+    //    list keeps the elements that may temper to a listed value.
+    const float tau = u_threshold<NT>(tm, t2, true, m_x, SHARD_CAND, s_hist, &s_res, [] { csync(); }, true);
+    const float bound = temper ? tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f : tau;
+    // 5. every element >= the bound into the list at its thread's offset (a
+    //    count, a CTA-wide scan, a write), as untempered value bits << 32 |
+    //    local index
+    int cnt = 0;
+#pragma unroll 4
+    for (int f = tid; f < nv; f += NT) {
+      const float4 w = s4[f];
+      const int i0 = 4 * f;
+      cnt += (w.x >= bound) + (i0 + 1 < Vs && w.y >= bound) + (i0 + 2 < Vs && w.z >= bound) +
+             (i0 + 3 < Vs && w.w >= bound);
+    }
+    int n0 = 0;
+    int pos = block_exscan_i32(cnt, s_scan, &n0);
+    if (n0 <= SHARD_LIST && cnt > 0) {
+      for (int f = tid; f < nv; f += NT) {
+        const float4 w = s4[f];
+        if (fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) >= bound) {
+          const float e[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (4 * f + c < Vs && e[c] >= bound)
+              list[pos++] = ((unsigned long long)__float_as_uint(e[c]) << 32) | (unsigned)(4 * f + c);
         }
       }
     }
     __syncthreads();
-    const int n0 = s_cnt;
+    // the key of a list entry: ~fkey(tempered value) << 32 | local index
+    auto tkey = [&](unsigned long long raw) {
+      const float x = __uint_as_float((unsigned)(raw >> 32));
+      const float tv = temper ? __fdiv_rn(x, T) : x;
+      return ((unsigned long long)(~fkey(tv)) << 32) | (raw & 0xffffffffull);
+    };
     bool fast = n0 >= SHARD_CAND && n0 <= SHARD_LIST;
     if (fast) {
       if (n0 <= NT) {
@@ -230,7 +265,11 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         unsigned long long kt = 0ull;
         int r = SHARD_LIST;
         if (tid < n0) {
-          kt = list[tid];
+          kt = tkey(list[tid]);
+          list[tid] = kt;
+        }
+        __syncthreads();
+        if (tid < n0) {
           r = 0;
           const ulonglong2* l2 = reinterpret_cast<const ulonglong2*>(list);  // two keys per load
 #pragma unroll 4
@@ -245,19 +284,19 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         __syncthreads();
       } else {
         const int n2 = next_pow2(n0);
-        for (int i = n0 + tid; i < n2; i += NT) list[i] = KEY_MAX;
+        for (int i = tid; i < n2; i += NT) list[i] = i < n0 ? tkey(list[i]) : KEY_MAX;
         __syncthreads();
         bitonic_sort_u64(list, n2);
       }
       if (temper) {
         // every element below the bound tempers to at most RN(prev(bound) / T)
         const float t64 = fkey_inv(~(unsigned)(list[SHARD_CAND - 1] >> 32));
-        fast = t64 > __fdiv_rn(nextafterf(t0f, -INFINITY), T);
+        fast = t64 > __fdiv_rn(nextafterf(bound, -INFINITY), T);
       }
     }
     if (fast) {
       const bool ties = n0 > SHARD_CAND && (list[SHARD_CAND] >> 32) == (list[SHARD_CAND - 1] >> 32);
-      shard_emit(out, voff, srow, list, ties, temper, T);
+      shard_emit(out, voff, list, ties);
     } else {
       if (temper) {
         for (int i = tid; i < Vs; i += NT) srow[i] = __fdiv_rn(srow[i], T);
@@ -334,7 +373,7 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         __syncthreads();
       }
       bitonic_sort_u64(list, SHARD_CAND);
-      shard_emit(out, voff, srow, list, eq_before > want, false, T);
+      shard_emit(out, voff, list, eq_before > want);
     }
     __syncthreads();
   }
