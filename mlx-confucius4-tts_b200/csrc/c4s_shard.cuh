@@ -107,7 +107,7 @@ __device__ __forceinline__ void shard_slots(float4 (&v)[SHARD_SQ], const float4*
   }
 }
 
-__global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
+__global__ void __launch_bounds__(NT, 3) shard_kernel(ShardArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned long long* list = reinterpret_cast<unsigned long long*>(smem);
   float* srow = reinterpret_cast<float*>(smem + (size_t)SHARD_LIST * 8);
@@ -141,30 +141,22 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
     c4s_candidate* out = a.cand + (long long)sh * a.cand_stride + (long long)row * SHARD_CAND;
     const c4s_row_params P = a.params[(long long)row * a.params_stride];
     const float* g = a.logits + (long long)row * a.ld + loff;
-    // 1. stage the shard's row (16-byte loads when the row is aligned)
-    if ((((uintptr_t)g) & 15) == 0) {
-      const float4* g4 = reinterpret_cast<const float4*>(g);
-      float4* s4 = reinterpret_cast<float4*>(srow);
-      const int n4 = Vs >> 2;
-      for (int i0 = 0; i0 < n4; i0 += 8 * NT) {  // eight 16-byte loads in flight per thread
-        float4 r[8];
+    // 1. stage the shard's row (16-byte loads when the row is aligned), with
+    //    the row's history ids loaded while the first eight slots are in flight
+    const bool al = (((uintptr_t)g) & 15) == 0;
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    float4* s4w = reinterpret_cast<float4*>(srow);
+    const int n4 = al ? Vs >> 2 : 0;
+    float4 r[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int i = i0 + q * NT + tid;
-          if (i < n4) r[q] = __ldg(g4 + i);
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int i = i0 + q * NT + tid;
-          if (i < n4) s4[i] = r[q];
-        }
-      }
-      for (int i = (Vs & ~3) + tid; i < Vs; i += NT) srow[i] = __ldg(g + i);
-    } else {
-      for (int i = tid; i < Vs; i += NT) srow[i] = __ldg(g + i);
+    for (int q = 0; q < 8; ++q) {
+      const int i = q * NT + tid;
+      if (i < n4) r[q] = __ldg(g4 + i);
     }
-    if (tid < ((4 - (Vs & 3)) & 3)) srow[Vs + tid] = -INFINITY;
-    // 2. repetition penalty over the history ids inside this shard
+    // 2. repetition penalty over the history ids inside this shard: up to
+    //    HR ids per thread in registers (read-then-write below), longer
+    //    histories through a de-duplication bitmap
+    constexpr int HR = 4;
     const bool pen = P.repetition_penalty != 1.0f && a.hist_off != nullptr;
     long long h0 = 0, h1 = 0;
     if (pen) {
@@ -174,22 +166,70 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
         if (tid == 0) atomicOr(a.errflags, C4S_DEVERR_HIST_RANGE);
         h0 = h1 = 0;
       }
-      for (int i = tid; i < (Vs + 31) / 32; i += NT) bitmap[i] = 0u;
     }
+    const bool hshort = h1 - h0 <= (long long)HR * NT;
+    int hid[HR];
+#pragma unroll
+    for (int q = 0; q < HR; ++q) {
+      const long long j = h0 + tid + (long long)q * NT;
+      hid[q] = (pen && hshort && j < h1) ? __ldg(a.hist + j) : -1;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = q * NT + tid;
+      if (i < n4) s4w[i] = r[q];
+    }
+    for (int i0 = 8 * NT; i0 < n4; i0 += 8 * NT) {  // wider shards: eight 16-byte loads in flight per thread
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int i = i0 + q * NT + tid;
+        if (i < n4) r[q] = __ldg(g4 + i);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int i = i0 + q * NT + tid;
+        if (i < n4) s4w[i] = r[q];
+      }
+    }
+    for (int i = 4 * n4 + tid; i < Vs; i += NT) srow[i] = __ldg(g + i);
+    if (tid < ((4 - (Vs & 3)) & 3)) srow[Vs + tid] = -INFINITY;
+    if (pen && !hshort)
+      for (int i = tid; i < (Vs + 31) / 32; i += NT) bitmap[i] = 0u;
     s_hist[tid] = 0u;  // the threshold's bins
     __syncthreads();
     if (pen) {
       const float pv = P.repetition_penalty;
       const float rpv = __frcp_rn(pv);
-      for (long long j = h0 + tid; j < h1; j += NT) {
-        const int t = a.hist[j];
-        const unsigned u = (unsigned)t - (unsigned)voff;
-        if (t >= 0 && u < (unsigned)Vs) {
-          const unsigned bit = 1u << (u & 31);
-          const unsigned old = atomicOr(&bitmap[u >> 5], bit);
-          if (!(old & bit)) {
-            const float s = srow[u];
-            srow[u] = (s < 0.0f) ? __fmul_rn(s, pv) : div_rn(s, pv, rpv);
+      if (hshort) {
+        // every id inside the shard reads its value, a barrier, every one
+        // writes the penalised value: repeated ids write the same value
+        float pen_v[HR];
+        unsigned pen_u[HR];
+#pragma unroll
+        for (int q = 0; q < HR; ++q) {
+          pen_u[q] = (unsigned)hid[q] - (unsigned)voff;
+          if (hid[q] >= 0 && pen_u[q] < (unsigned)Vs) {
+            const float s = srow[pen_u[q]];
+            pen_v[q] = (s < 0.0f) ? __fmul_rn(s, pv) : div_rn(s, pv, rpv);
+          } else {
+            pen_u[q] = 0xffffffffu;
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < HR; ++q)
+          if (pen_u[q] != 0xffffffffu) srow[pen_u[q]] = pen_v[q];
+      } else {
+        for (long long j = h0 + tid; j < h1; j += NT) {
+          const int t = a.hist[j];
+          const unsigned u = (unsigned)t - (unsigned)voff;
+          if (t >= 0 && u < (unsigned)Vs) {
+            const unsigned bit = 1u << (u & 31);
+            const unsigned old = atomicOr(&bitmap[u >> 5], bit);
+            if (!(old & bit)) {
+              const float s = srow[u];
+              srow[u] = (s < 0.0f) ? __fmul_rn(s, pv) : div_rn(s, pv, rpv);
+            }
           }
         }
       }
@@ -228,26 +268,50 @@ __global__ void __launch_bounds__(NT) shard_kernel(ShardArgs a) {
     const float bound = temper ? tau - (fabsf(tau) + 1.0f) * 3.814697265625e-06f : tau;
     // 5. every element >= the bound into the list at its thread's offset (a
     //    count, a CTA-wide scan, a write), as untempered value bits << 32 |
-    //    local index
-    int cnt = 0;
-#pragma unroll 4
-    for (int f = tid; f < nv; f += NT) {
-      const float4 w = s4[f];
-      const int i0 = 4 * f;
-      cnt += (w.x >= bound) + (i0 + 1 < Vs && w.y >= bound) + (i0 + 2 < Vs && w.z >= bound) +
-             (i0 + 3 < Vs && w.w >= bound);
-    }
+    //    local index. One pass of slots (Vs <= 8 * 4 * NT) with a finite
+    //    bound: a mask of the thread's elements >= the bound (bit 4q + c:
+    //    element 4 (q NT + tid) + c; the -inf padding never counts), the write
+    //    visits its set bits only.
     int n0 = 0;
-    int pos = block_exscan_i32(cnt, s_scan, &n0);
-    if (n0 <= SHARD_LIST && cnt > 0) {
+    if (nch == 1 && bound > -INFINITY) {
+      shard_slots(v, s4, 0, nv);
+      unsigned m = 0u;
+#pragma unroll
+      for (int q = 0; q < SHARD_SQ; ++q) {
+        m |= (v[q].x >= bound ? 1u : 0u) << (4 * q);
+        m |= (v[q].y >= bound ? 2u : 0u) << (4 * q);
+        m |= (v[q].z >= bound ? 4u : 0u) << (4 * q);
+        m |= (v[q].w >= bound ? 8u : 0u) << (4 * q);
+      }
+      int pos = block_exscan_i32(__popc(m), s_scan, &n0);
+      if (n0 <= SHARD_LIST) {
+        while (m) {
+          const int b = __ffs(m) - 1;
+          m &= m - 1u;
+          const int idx = 4 * ((b >> 2) * NT + tid) + (b & 3);
+          list[pos++] = ((unsigned long long)__float_as_uint(srow[idx]) << 32) | (unsigned)idx;
+        }
+      }
+    } else {
+      int cnt = 0;
+#pragma unroll 4
       for (int f = tid; f < nv; f += NT) {
         const float4 w = s4[f];
-        if (fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) >= bound) {
-          const float e[4] = {w.x, w.y, w.z, w.w};
+        const int i0 = 4 * f;
+        cnt += (w.x >= bound) + (i0 + 1 < Vs && w.y >= bound) + (i0 + 2 < Vs && w.z >= bound) +
+               (i0 + 3 < Vs && w.w >= bound);
+      }
+      int pos = block_exscan_i32(cnt, s_scan, &n0);
+      if (n0 <= SHARD_LIST && cnt > 0) {
+        for (int f = tid; f < nv; f += NT) {
+          const float4 w = s4[f];
+          if (fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) >= bound) {
+            const float e[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            if (4 * f + c < Vs && e[c] >= bound)
-              list[pos++] = ((unsigned long long)__float_as_uint(e[c]) << 32) | (unsigned)(4 * f + c);
+            for (int c = 0; c < 4; ++c)
+              if (4 * f + c < Vs && e[c] >= bound)
+                list[pos++] = ((unsigned long long)__float_as_uint(e[c]) << 32) | (unsigned)(4 * f + c);
+          }
         }
       }
     }

@@ -295,6 +295,42 @@ def test_ragged_shards_strides_and_topk(sctx, oracle, V, G, ld_pad, k):
 
 
 @pytest.mark.gpu
+def test_history_lengths_and_repeats(sctx, oracle):
+    """The shard kernel penalises histories of up to 1024 ids by
+    read-then-write and longer ones through a de-duplication bitmap: rows of
+    0 to 6000 ids, many repeated (ids drawn from a narrow range that falls in
+    one or two shards), out-of-range ids, penalties above and below 1."""
+    import torch
+    c4s = load_c4s()
+    V, G, B = 65536, 8, 48
+    b = c4s.workloads.config4(seed=77, B=B, V=V, top_k=40, top_p=0.85)
+    g = np.random.default_rng(77)
+    lens = np.array([0, 1, 2, 31, 255, 256, 1023, 1024, 1025, 2048, 4000, 6000] * 4)
+    off = np.zeros(B + 1, dtype=np.int64)
+    np.cumsum(lens, out=off[1:])
+    hist = np.empty(int(off[-1]), dtype=np.int32)
+    for r in range(B):
+        n = int(lens[r])
+        if r % 4 == 0:
+            ids = g.integers(0, V, size=n)                 # uniform: few repeats
+        elif r % 4 == 1:
+            ids = g.integers(8000, 8400, size=n)           # narrow: many repeats across a shard edge
+        elif r % 4 == 2:
+            ids = g.integers(-50, V + 50, size=n)          # some out of range (ignored)
+        else:
+            ids = np.argsort(b.logits[r])[-64:][g.integers(0, 64, size=n)]  # the row's largest values
+        hist[off[r]:off[r + 1]] = ids.astype(np.int32)
+    b.hist, b.hist_off = hist, off
+    b.params["repetition_penalty"][::3] = 0.5
+    b.params["temperature"][1::5] = 1.0
+    ids, st, err = _gpu_split(sctx, b, G, torch)
+    oid, ro = _oracle(oracle, b)
+    assert err == 0
+    assert np.array_equal(ids, oid)
+    assert np.array_equal(st, ro)
+
+
+@pytest.mark.gpu
 def test_ties_fallback_and_refusals(sctx, oracle):
     """Rounded logits (ties below the threshold), a shard with more than 1024
     values above the fast path's bound (exact radix fallback), a draw with
