@@ -523,43 +523,149 @@ static_assert((double)LCAP * MASS_Q < 0x1p62, "fixed-point masses of a list cann
 __device__ __forceinline__ unsigned long long mass_q(double p) { return __double2ull_rz(p * MASS_Q); }
 
 // The same search by a whole CTA (long lists), by bisection two bits a step:
-// three thresholds summed in one pass over the staged list and one pair of
-// barriers per step (no atomics: on thousands of keys contended
-// shared-memory adds cost more than the extra passes).
+// three thresholds summed per step and one pair of barriers per step (no
+// atomics: on thousands of keys contended shared-memory adds cost more). Each
+// thread keeps a mask of its entries (entry tid + k NT: bit k) whose keys lie
+// in the interval still searched, [v, v + 2^(b+1)), and the mass of its
+// entries below it: an entry below the interval adds its mass to every later
+// threshold, one above it to none, so only the entries inside are visited
+// (four at a time, their loads in flight together) and the sums are the same
+// integers as over the whole list. Once at most 32 entries are left inside,
+// one warp finishes the search on them (one entry per lane, no CTA barriers).
+// `scratch`: 64 words of shared memory the caller does not need meanwhile.
 __device__ __forceinline__ unsigned bisect_mass_cta(const unsigned* __restrict__ vk, const double* __restrict__ pv,
-                                                    int n, unsigned prefix, int b0, double base, double Th, LRed& R) {
+                                                    int n, unsigned prefix, int b0, double base, double Th, LRed& R,
+                                                    unsigned long long* scratch) {
+  static_assert((LCAP + NT - 1) / NT <= 64, "a thread's entries fit the mask");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   unsigned v = prefix;
   const double thq = (Th - base) * MASS_Q;          // the mass allowed below the crossing
+  const int per = n > tid ? (n - tid + NT - 1) / NT : 0;
+  unsigned long long act = per >= 64 ? ~0ull : ((1ull << per) - 1ull);
+  unsigned long long below = 0ull;                  // this thread's mass of entries below v
+  unsigned long long* h_q = scratch;                // [32] the warp stage's entries: fixed-point masses,
+  unsigned* h_e = reinterpret_cast<unsigned*>(scratch + 32);   // [32] their positions,
+  unsigned* h_n = reinterpret_cast<unsigned*>(scratch + 48);   // [0] their count, [1] the result
+  unsigned long long* h_below = scratch + 49;       // the mass below them
+  if (tid == 0) {
+    h_n[0] = 0u;
+    *h_below = 0ull;
+  }
   for (int b = b0; b >= 0; b -= 2) {
     const int lo = b >= 1 ? b - 1 : 0;
     const unsigned c0 = v | (1u << lo), c1 = v | (2u << lo), c2 = v | (3u << lo);
-    unsigned long long g0 = 0ull, g1 = 0ull, g2 = 0ull;
-    for (int e = threadIdx.x; e < n; e += NT) {
-      const unsigned x = vk[e];
-      const unsigned long long q = mass_q(pv[e]);
-      g0 += x < c0 ? q : 0ull;
-      g1 += x < c1 ? q : 0ull;
-      g2 += x < c2 ? q : 0ull;
+    const unsigned long long end = (unsigned long long)v + (2ull << b);
+    unsigned long long s0 = 0ull, s1 = 0ull, s2 = 0ull, keep = 0ull;
+    for (unsigned long long m = act; m;) {
+      int kk[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        ok[u] = m != 0ull;
+        kk[u] = ok[u] ? __ffsll((long long)m) - 1 : 0;
+        if (ok[u]) m &= m - 1ull;
+      }
+      unsigned x[4];
+      double p[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = tid + kk[u] * NT;
+        x[u] = ok[u] ? vk[e] : 0u;
+        p[u] = ok[u] ? pv[e] : 0.0;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (!ok[u] || (unsigned long long)x[u] >= end) continue;   // above the interval: in no later sum
+        const unsigned long long q = mass_q(p[u]);
+        if (x[u] < v) {                             // below it: in every later sum
+          below += q;
+          continue;
+        }
+        keep |= 1ull << kk[u];
+        s0 += x[u] < c0 ? q : 0ull;
+        s1 += x[u] < c1 ? q : 0ull;
+        s2 += x[u] < c2 ? q : 0ull;
+      }
     }
+    act = keep;
+    unsigned long long g0 = below + s0, g1 = below + s1, g2 = below + s2;
+    int na = __popcll(keep);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       g0 += __shfl_xor_sync(FULL, g0, o);
       g1 += __shfl_xor_sync(FULL, g1, o);
       g2 += __shfl_xor_sync(FULL, g2, o);
     }
-    if ((threadIdx.x & 31) == 0) {
-      R.q3[threadIdx.x >> 5][0] = g0;
-      R.q3[threadIdx.x >> 5][1] = g1;
-      R.q3[threadIdx.x >> 5][2] = g2;
+    na = __reduce_add_sync(FULL, na);
+    if (lane == 0) {
+      R.q3[warp][0] = g0;
+      R.q3[warp][1] = g1;
+      R.q3[warp][2] = g2;
+      R.i[warp] = na;
     }
     csync();
     g0 = g1 = g2 = 0ull;
+    na = 0;
 #pragma unroll
-    for (int w = 0; w < NWARP; ++w) { g0 += R.q3[w][0]; g1 += R.q3[w][1]; g2 += R.q3[w][2]; }
+    for (int w = 0; w < NWARP; ++w) {
+      g0 += R.q3[w][0];
+      g1 += R.q3[w][1];
+      g2 += R.q3[w][2];
+      na += R.i[w];
+    }
     csync();
     if (lo < b && (double)g2 <= thq) v = c2;
     else if (lo < b && (double)g1 <= thq) v = c1;
     else if ((double)g0 <= thq) v = c0;
+    if (b >= 2 && na <= 32) {
+      // the entries inside the old interval (the new one lies in it) to one
+      // warp; the mass below v they do not cover in h_below
+      for (unsigned long long m = keep; m; m &= m - 1ull) {
+        const int e = tid + (__ffsll((long long)m) - 1) * NT;
+        const unsigned slot = atomicAdd(&h_n[0], 1u);
+        h_e[slot] = (unsigned)e;
+        h_q[slot] = mass_q(pv[e]);
+      }
+      unsigned long long wb = below;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wb += __shfl_xor_sync(FULL, wb, o);
+      if (lane == 0 && wb != 0ull) atomicAdd(h_below, wb);
+      csync();
+      if (warp == 0) {
+        const unsigned cnt = h_n[0];
+        unsigned x = 0xffffffffu;
+        unsigned long long q = 0ull;
+        if ((unsigned)lane < cnt) {
+          x = vk[h_e[lane]];
+          q = h_q[lane];
+        }
+        const unsigned long long bw = *h_below;
+        for (int b2 = b - 2; b2 >= 0; b2 -= 2) {
+          // g(c) = mass below the entries + theirs below c: an entry under
+          // v counts in every sum, one at or above the interval's end in none
+          const int lo2 = b2 >= 1 ? b2 - 1 : 0;
+          const unsigned d0 = v | (1u << lo2), d1 = v | (2u << lo2), d2 = v | (3u << lo2);
+          unsigned long long w0 = x < d0 ? q : 0ull, w1 = x < d1 ? q : 0ull, w2 = x < d2 ? q : 0ull;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            w0 += __shfl_xor_sync(FULL, w0, o);
+            w1 += __shfl_xor_sync(FULL, w1, o);
+            w2 += __shfl_xor_sync(FULL, w2, o);
+          }
+          w0 += bw;
+          w1 += bw;
+          w2 += bw;
+          if (lo2 < b2 && (double)w2 <= thq) v = d2;
+          else if (lo2 < b2 && (double)w1 <= thq) v = d1;
+          else if ((double)w0 <= thq) v = d0;
+        }
+        if (lane == 0) h_n[1] = v;
+      }
+      csync();
+      v = h_n[1];
+      csync();                                      // the scratch is free again
+      return v;
+    }
   }
   return v;
 }
@@ -854,7 +960,7 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
     // a refinement starts from the first pass's crossing and bisects only if that fails
     const bool near = refine && J.vcross != 0u && step_to_crossing<CTA>(vk, pv, n, tk, tail, Th, J.vcross, &v, R);
     if (!near) {
-      if constexpr (CTA) v = bisect_mass_cta(vk, pv, n, v, b0, tail, Th, R);
+      if constexpr (CTA) v = bisect_mass_cta(vk, pv, n, v, b0, tail, Th, R, hist);
       else v = radix_mass<false, 7>(vk, pv, n, v, b0, tail, Th, hist, R);
     }
     double Gs = 0.0, Mg = 0.0;
@@ -877,17 +983,24 @@ __device__ __forceinline__ bool list_job(const Args& a, int row, RowJob& J, cons
         t = (int)fmin(fmax(q, 1.0), (double)cg);
       }
       int es = 0, acc = 0;
-      for (int e0 = 0; e0 < n; e0 += GN) {
-        const int e = e0 + r0;
-        const bool m = e < n && vk[e] == v;
-        int tot;
-        const int before = G::exscan_i(m ? 1 : 0, R, &tot);
-        if (t <= acc + tot) {
-          const bool me = m && acc + before + 1 == t;
-          es = (int)G::qmin(me ? (unsigned long long)e : ~0ull, R);
-          break;
+      if (t == 1) {                                 // the group's first member: its least position
+        unsigned long long me = ~0ull;
+        for (int e = r0; e < n; e += GN)
+          if (vk[e] == v) me = (unsigned long long)e < me ? (unsigned long long)e : me;
+        es = (int)G::qmin(me, R);
+      } else {
+        for (int e0 = 0; e0 < n; e0 += GN) {
+          const int e = e0 + r0;
+          const bool m = e < n && vk[e] == v;
+          int tot;
+          const int before = G::exscan_i(m ? 1 : 0, R, &tot);
+          if (t <= acc + tot) {
+            const bool me = m && acc + before + 1 == t;
+            es = (int)G::qmin(me ? (unsigned long long)e : ~0ull, R);
+            break;
+          }
+          acc += tot;
         }
-        acc += tot;
       }
       const double before = Gs + (double)(t - 1) * pg, cur = Gs + (double)t * pg;
       const double bd = 2.0 * ((4.0 * (k0 ? V : ns) + 16.0) * U53 * St) + 2.0 * J.tail_err;
