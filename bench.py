@@ -120,10 +120,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def profiled_traffic(B):
-    """DRAM bytes (read + write) of one row-kernel launch at B rows, from the
-    committed ncu summary of the same workload (scaled by rows if B differs)."""
-    path = os.path.join(ROOT, "profiles", "row_kernel_config2_dram.txt")
+def profiled_traffic(B, profile="row_kernel_config2_dram.txt"):
+    """DRAM bytes (read + write) of one launch of the profiled kernel at B rows,
+    from the committed ncu summary of the same workload (scaled by rows if B
+    differs)."""
+    path = os.path.join(ROOT, "profiles", profile)
     try:
         with open(path) as f:
             for line in f:
@@ -690,7 +691,9 @@ def run_vocab_sharded(args):
                                       f"candidates/row/sub-shard",
                        "l2": f"pool of {npool} batches rotated (inputs > 2x L2)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None, "kernel": "shard_kernel",
+                         "frac": achieved / hbm_peak,
+                         "traffic": profiled_traffic(B, "vocab_sharded_config4.txt") if world == 1 else None,
+                         "kernel": "shard_kernel",
                          "peak_kind": peak_kind, "alg_bytes_per_launch": alg},
             "shard_kernel_ms_per_step": shard_ms,
             "cpu_baseline": cpu,
